@@ -1,0 +1,367 @@
+// K1/K2/K4 + flash-layout ops: paged KV cache <-> LMCache chunk objects.
+//
+// Semantics follow the reference launchers (csrc/mem_kernels.cpp:75-111
+// `multi_layer_kv_transfer`, :113-213 `fused_multi_layer_kv_transfer`,
+// :265-334 `single_layer_kv_transfer`, :1036-1307 dense multi-chunk direct
+// transfer, :1341-1440 `load_and_reshape_flash`):
+//   for every layer l, plane p and token t with slot = slot_mapping[t] >= 0
+//     chunk[p, l, t, :]  <->  paged[l][p][slot, :]
+// The implementation is new: every format is described by PagedDesc/ChunkView
+// (layout.h, kv_copy.cuh) and moved by one of two engines, TMA bulk copies
+// through a shared-memory ring (device<->device) or 16-byte SIMT vectors
+// (host-mapped pinned memory, unaligned rows).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
+#include <cstring>
+#include <algorithm>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kv_copy.cuh"
+#include "mem_kernels.h"
+
+namespace lmc {
+
+// ---------------------------------------------------------------------------
+// TMA engine: one warp per CTA, ring of `stages` shared-memory buffers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned warp_sum(unsigned v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(32)
+    tma_rows_kernel(CopyJob j, int stage_bytes, int stages,
+                    unsigned long long budget_ns) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+  unsigned char *ring = smem + 128;
+  const int lane = threadIdx.x;
+
+  j.num_tokens = effective_tokens(j);
+  const UnitMap m = make_unit_map(j, stage_bytes);
+  const int total_units = m.units_per_layer * j.num_layers;
+  if (static_cast<int>(blockIdx.x) >= total_units) return;
+  const int n_iter =
+      (total_units - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
+
+  if (lane == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  auto issue_loads = [&](int k) {
+    const Unit u = decode_unit(j, m, blockIdx.x + k * gridDim.x);
+    const int s = k % stages;
+    const LaneRuns r = plan_runs(j, u, lane, j.num_tokens);
+    const unsigned rb = j.paged.plane[u.plane].row_bytes;
+    const unsigned total = warp_sum((r.len[0] + r.len[1]) * rb);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
+    __syncwarp();
+    unsigned char *buf = ring + static_cast<size_t>(s) * stage_bytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (r.len[h])
+        bulk_g2s(buf + (h * 32 + lane) * rb, r.src[h], r.len[h] * rb, &bars[s]);
+  };
+
+  auto issue_stores = [&](int k) {
+    const Unit u = decode_unit(j, m, blockIdx.x + k * gridDim.x);
+    const int s = k % stages;
+    const LaneRuns r = plan_runs(j, u, lane, j.num_tokens);
+    const unsigned rb = j.paged.plane[u.plane].row_bytes;
+    unsigned char *buf = ring + static_cast<size_t>(s) * stage_bytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (r.len[h]) bulk_s2g(r.dst[h], buf + (h * 32 + lane) * rb, r.len[h] * rb);
+    bulk_commit();
+  };
+
+  const int prologue = n_iter < stages - 1 ? n_iter : stages - 1;
+  for (int k = 0; k < prologue; ++k) issue_loads(k);
+  for (int k = 0; k < n_iter; ++k) {
+    const int s = k % stages;
+    const unsigned parity = (k / stages) & 1;
+    if (!mbar_wait_bounded(&bars[s], parity, budget_ns)) {
+      if (lane == 0)
+        report_status(j.status, kStatusMbarTimeout, blockIdx.x, k, n_iter);
+      break;
+    }
+    issue_stores(k);
+    const int kn = k + stages - 1;
+    if (kn < n_iter) {
+      bulk_wait_read<1>();
+      __syncwarp();
+      issue_loads(kn);
+    }
+  }
+  bulk_wait_all();
+}
+
+// ---------------------------------------------------------------------------
+// SIMT engine: warp per (layer, plane, token) row, 16 B vectors when aligned.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void warp_copy_row(char *dst, const char *src,
+                                              int rb, int lane) {
+  const bool v16 = ((reinterpret_cast<uintptr_t>(dst) |
+                     reinterpret_cast<uintptr_t>(src) | rb) & 15) == 0;
+  if (v16) {
+    // up to 4 independent 16 B loads in flight per lane before the stores
+    int off = lane * 16;
+    for (; off + 3 * 512 < rb; off += 4 * 512) {
+      int4 a = ld_v4(src + off), b = ld_v4(src + off + 512),
+           c = ld_v4(src + off + 1024), d = ld_v4(src + off + 1536);
+      st_v4(dst + off, a);
+      st_v4(dst + off + 512, b);
+      st_v4(dst + off + 1024, c);
+      st_v4(dst + off + 1536, d);
+    }
+    for (; off < rb; off += 512) st_v4(dst + off, ld_v4(src + off));
+    return;
+  }
+  const bool v4 = ((reinterpret_cast<uintptr_t>(dst) |
+                    reinterpret_cast<uintptr_t>(src) | rb) & 3) == 0;
+  if (v4) {
+    for (int off = lane * 4; off < rb; off += 128)
+      *reinterpret_cast<int *>(dst + off) =
+          *reinterpret_cast<const volatile int *>(src + off);
+    return;
+  }
+  for (int off = lane; off < rb; off += 32) dst[off] = src[off];
+}
+
+__global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
+  j.num_tokens = effective_tokens(j);
+  if (j.num_tokens == 0) return;
+  const int lane = threadIdx.x & 31;
+  const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x +
+                          threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const long long rows = static_cast<long long>(j.num_layers) *
+                         j.paged.num_planes * j.num_tokens;
+  for (long long r = warp; r < rows; r += nwarps) {
+    const int t = static_cast<int>(r % j.num_tokens);
+    const long long lp = r / j.num_tokens;
+    const int p = static_cast<int>(lp % j.paged.num_planes);
+    const int l = static_cast<int>(lp / j.paged.num_planes);
+    const int64_t slot = load_slot(j, t);
+    if (slot < 0) continue;
+    if (slot >= j.paged.num_slots) {
+      if (lane == 0)
+        report_status(j.status, kStatusBadSlot, t, slot, j.paged.num_slots);
+      continue;
+    }
+    const int64_t ct = load_idx(j, t);
+    if (ct < 0 || (j.chunk_idx != nullptr && ct >= j.chunk_idx_limit)) {
+      if (lane == 0)
+        report_status(j.status, kStatusBadIndex, t, ct, j.chunk_idx_limit);
+      continue;
+    }
+    char *pa = paged_addr(j.paged, j.layer_begin + l, p, slot);
+    char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + l, p, ct, j.num_tokens);
+    const int rb = j.paged.plane[p].row_bytes;
+    if (j.to_chunk)
+      warp_copy_row(ca, pa, rb, lane);
+    else
+      warp_copy_row(pa, ca, rb, lane);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+int num_sms(int device) {
+  static int cached[64] = {0};
+  if (device < 0 || device >= 64) device = 0;
+  if (cached[device] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+    cached[device] = v > 0 ? v : 148;
+  }
+  return cached[device];
+}
+
+static int env_int(const char *name, int dflt) {
+  const char *v = std::getenv(name);
+  return v ? std::atoi(v) : dflt;
+}
+
+PagedLayout::PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
+                         std::vector<int64_t> slot_stride,
+                         std::vector<int64_t> row_bytes, int64_t block_size,
+                         int64_t num_slots)
+    : ptrs_(ptrs) {
+  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.is_contiguous(),
+              "PagedLayout: ptrs must be a contiguous int64 tensor");
+  const int np = static_cast<int>(row_bytes.size());
+  TORCH_CHECK(np >= 1 && np <= kMaxPlanes, "PagedLayout: 1..3 planes");
+  TORCH_CHECK(block_stride.size() == row_bytes.size() &&
+                  slot_stride.size() == row_bytes.size(),
+              "PagedLayout: stride lists must match row_bytes");
+  TORCH_CHECK(ptrs.numel() % np == 0, "PagedLayout: ptrs not [L * planes]");
+  std::memset(&desc_, 0, sizeof(desc_));
+  desc_.ptrs = ptrs.data_ptr<int64_t>();
+  desc_.num_planes = np;
+  desc_.num_layers = static_cast<int32_t>(ptrs.numel() / np);
+  desc_.block_size = static_cast<int32_t>(block_size);
+  desc_.num_slots = num_slots;
+  aligned16_ = true;
+  for (int p = 0; p < np; ++p) {
+    desc_.plane[p].block_stride = block_stride[p];
+    desc_.plane[p].slot_stride = slot_stride[p];
+    desc_.plane[p].row_bytes = static_cast<int32_t>(row_bytes[p]);
+    TORCH_CHECK(row_bytes[p] > 0, "PagedLayout: row_bytes must be > 0");
+    if ((block_stride[p] | slot_stride[p] | row_bytes[p]) & 15) aligned16_ = false;
+  }
+  TORCH_CHECK(ptrs.is_cuda(), "PagedLayout: ptrs table must live on the device");
+  // Alignment of the plane base pointers is checked by the Python layer,
+  // which knows them, and recorded with set_bases_aligned().
+}
+
+ChunkLayout::ChunkLayout(std::vector<int64_t> plane_stride_t,
+                         int64_t layer_stride_t, std::vector<int64_t> token_stride,
+                         std::vector<int64_t> col_off) {
+  std::memset(&view_, 0, sizeof(view_));
+  TORCH_CHECK(plane_stride_t.size() <= kMaxPlanes && col_off.size() <= kMaxPlanes,
+              "ChunkLayout: at most 3 planes");
+  for (size_t p = 0; p < plane_stride_t.size(); ++p)
+    view_.plane_stride_t[p] = plane_stride_t[p];
+  for (size_t p = 0; p < col_off.size(); ++p) view_.col_off[p] = col_off[p];
+  view_.layer_stride_t = layer_stride_t;
+  TORCH_CHECK(token_stride.size() >= 1 && token_stride.size() <= kMaxPlanes,
+              "ChunkLayout: 1..3 token strides");
+  for (int p = 0; p < kMaxPlanes; ++p)
+    view_.token_stride[p] =
+        token_stride[std::min<size_t>(p, token_stride.size() - 1)];
+}
+
+static DeviceStatus *status_ptr(const c10::optional<at::Tensor> &status) {
+  if (!status.has_value()) return nullptr;
+  TORCH_CHECK(status->is_cuda() && status->nbytes() >= sizeof(DeviceStatus),
+              "status must be a device tensor of >= 24 bytes");
+  return reinterpret_cast<DeviceStatus *>(status->data_ptr());
+}
+
+void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
+                 int64_t mode, cudaStream_t stream, int device) {
+  if (j.num_tokens <= 0 || j.num_layers <= 0) return;
+  bool use_tma = (mode == 1) || (mode == 0 && chunk_on_device && aligned);
+  if (mode == 1) TORCH_CHECK(aligned, "TMA mode needs 16-byte aligned rows");
+  if (use_tma) {
+    const int stage_bytes = env_int("LMC_TMA_STAGE_BYTES", 16384);
+    const int stages = env_int("LMC_TMA_STAGES", 6);
+    int max_rb = 0;
+    for (int p = 0; p < j.paged.num_planes; ++p)
+      max_rb = std::max(max_rb, static_cast<int>(j.paged.plane[p].row_bytes));
+    const int sb = std::max(stage_bytes, max_rb);
+    const size_t smem = 128 + static_cast<size_t>(sb) * stages;
+    TORCH_CHECK(smem <= 227 * 1024, "TMA ring too large: ", smem);
+    static bool attr_set[64] = {false};
+    if (!attr_set[device & 63]) {
+      cudaFuncSetAttribute(tma_rows_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           227 * 1024);
+      attr_set[device & 63] = true;
+    }
+    // units: recompute on host to size the grid
+    long long units = 0;
+    for (int p = 0; p < j.paged.num_planes; ++p) {
+      int tt = sb / j.paged.plane[p].row_bytes;
+      tt = std::min(64, std::max(1, tt));
+      units += (j.num_tokens + tt - 1) / tt;
+    }
+    units *= j.num_layers;
+    const int per_sm = std::max(1, static_cast<int>((228 * 1024) / (smem + 1024)));
+    const int grid_cap = env_int("LMC_TMA_GRID", num_sms(device) * per_sm);
+    const int grid = static_cast<int>(std::min<long long>(units, grid_cap));
+    const unsigned long long budget_ns = 2000000000ull;  // 2 s
+    tma_rows_kernel<<<grid, 32, smem, stream>>>(j, sb, stages, budget_ns);
+  } else {
+    const long long rows = static_cast<long long>(j.num_layers) *
+                           j.paged.num_planes * j.num_tokens;
+    const long long warps_needed = rows;
+    const int threads = 256;
+    long long blocks = (warps_needed * 32 + threads - 1) / threads;
+    const long long cap = static_cast<long long>(num_sms(device)) *
+                          env_int("LMC_SIMT_BLOCKS_PER_SM", 8);
+    blocks = std::max(1LL, std::min(blocks, cap));
+    simt_rows_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(j);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void kv_transfer(const PagedLayout &paged, const c10::optional<at::Tensor> &chunk,
+                 const c10::optional<at::Tensor> &chunk_ptrs,
+                 const ChunkLayout &layout, int64_t chunk_ntok,
+                 int64_t chunk_tok_off, int64_t chunk_tokens,
+                 bool chunk_on_device, const at::Tensor &slots,
+                 int64_t layer_begin, int64_t chunk_layer_begin,
+                 int64_t num_layers, bool to_chunk, int64_t mode,
+                 const c10::optional<at::Tensor> &status,
+                 const c10::optional<at::Tensor> &chunk_idx,
+                 int64_t chunk_idx_limit,
+                 const c10::optional<at::Tensor> &num_tokens_dev) {
+  TORCH_CHECK(slots.is_cuda(), "slot_mapping must be on the device");
+  TORCH_CHECK(slots.scalar_type() == at::kLong || slots.scalar_type() == at::kInt,
+              "slot_mapping must be int32 or int64");
+  TORCH_CHECK(slots.is_contiguous(), "slot_mapping must be contiguous");
+  TORCH_CHECK(layer_begin >= 0 && num_layers >= 0 &&
+                  layer_begin + num_layers <= paged.desc().num_layers,
+              "layer range out of the paged cache");
+  const c10::cuda::CUDAGuard guard(slots.device());
+  CopyJob j;
+  std::memset(&j, 0, sizeof(j));
+  j.paged = paged.desc();
+  j.chunk = layout.view();
+  bool aligned = paged.aligned();
+  if (chunk_ptrs.has_value()) {
+    TORCH_CHECK(chunk_ptrs->is_cuda() && chunk_ptrs->scalar_type() == at::kLong,
+                "chunk_ptrs must be a device int64 tensor");
+    TORCH_CHECK(chunk_tokens > 0, "chunk_tokens must be > 0");
+    j.chunk.chunk_ptrs = chunk_ptrs->data_ptr<int64_t>();
+    j.chunk.chunk_tokens = static_cast<int32_t>(chunk_tokens);
+  } else {
+    TORCH_CHECK(chunk.has_value(), "either chunk or chunk_ptrs is required");
+    j.chunk.base = static_cast<char *>(chunk->data_ptr());
+    j.chunk.ntok = static_cast<int32_t>(chunk_ntok);
+    j.chunk.tok_off = static_cast<int32_t>(chunk_tok_off);
+    if (!chunk_idx.has_value())
+      TORCH_CHECK(chunk_tok_off + slots.numel() <= chunk_ntok,
+                  "token range exceeds the chunk");
+    chunk_on_device = chunk->is_cuda();
+    if (reinterpret_cast<uintptr_t>(j.chunk.base) & 15) aligned = false;
+  }
+  for (int p = 0; p < j.paged.num_planes; ++p)
+    if ((j.chunk.plane_stride_t[p] | j.chunk.col_off[p] | j.chunk.token_stride[p]) & 15)
+      aligned = false;
+  if (j.chunk.layer_stride_t & 15) aligned = false;
+  j.slots = slots.data_ptr();
+  j.slot_is_i64 = slots.scalar_type() == at::kLong;
+  j.num_tokens = static_cast<int32_t>(slots.numel());
+  j.layer_begin = static_cast<int32_t>(layer_begin);
+  j.chunk_layer_begin = static_cast<int32_t>(chunk_layer_begin);
+  j.num_layers = static_cast<int32_t>(num_layers);
+  j.to_chunk = to_chunk ? 1 : 0;
+  j.status = status_ptr(status);
+  if (chunk_idx.has_value()) {
+    TORCH_CHECK(chunk_idx->is_cuda() && chunk_idx->is_contiguous() &&
+                    chunk_idx->scalar_type() == slots.scalar_type() &&
+                    chunk_idx->numel() == slots.numel(),
+                "chunk_idx: device tensor with the slot mapping's dtype/length");
+    j.chunk_idx = chunk_idx->data_ptr();
+    j.chunk_idx_limit = chunk_idx_limit;
+  }
+  if (num_tokens_dev.has_value()) {
+    TORCH_CHECK(num_tokens_dev->is_cuda() &&
+                    num_tokens_dev->scalar_type() == at::kInt,
+                "num_tokens_dev: device int32 tensor");
+    j.num_tokens_dev = num_tokens_dev->data_ptr<int32_t>();
+  }
+  launch_copy(j, chunk_on_device, aligned, mode,
+              at::cuda::getCurrentCUDAStream(slots.device().index()).stream(),
+              slots.device().index());
+}
+
+}  // namespace lmc

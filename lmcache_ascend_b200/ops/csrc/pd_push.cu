@@ -1,0 +1,252 @@
+// K9: fused disaggregated-prefill KV push over NVLink peer memory.
+//
+// The reference moves prefill KV to the decoder in two steps: a connector
+// gather into registered chunk buffers, then one RDMA write per chunk page
+// (`HcclAgent::WriteBatch`, reference csrc/hccl/hccl_agent.cpp:297-326, driven
+// by lmcache_ascend/v1/storage_backend/pd/sender_mixin.py:339-423).  On B200
+// every GPU of the box reaches every other GPU's HBM through NVSwitch, so the
+// push is one kernel: it reads the prefiller's paged rows (its own HBM) and
+// stores them straight into the decoder's paged blocks through peer-mapped
+// addresses, with no staging buffer, no NCCL call and no TMA multicast.
+//
+// Completion protocol (per layer, so the decoder can start layer l while the
+// prefiller still pushes l+1):
+//   * each CTA finishing a unit (layer, plane, token tile) runs
+//     __syncthreads(); fence.acq_rel.sys; red.release.sys.add(flag[l], 1)
+//     on the decoder's flag word for layer l (the flag lives in decoder HBM);
+//   * the decoder waits with `pd_wait_flags`, a bounded acquire spin that
+//     reports kStatusFlagTimeout instead of hanging.
+// Flags are cumulative counters: the receiver knows how many units each push
+// adds (`push_units_per_layer`) and waits for base + units.
+//
+// Fan-out: one launch may store the same rows to up to kMaxReplicas decoder
+// caches (TP-replicated MLA latent cache); loads happen once.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+#include "kv_copy.cuh"
+#include "mem_kernels.h"
+
+namespace lmc {
+
+constexpr int kMaxReplicas = 4;
+constexpr int kPushWarps = 8;
+
+struct PushJob {
+  PagedDesc src;
+  PagedDesc dst;  // dst.ptrs: [replicas][num_layers * num_planes] peer VAs
+  const void *src_slots;
+  const void *dst_slots;
+  int32_t slot_is_i64;
+  int32_t num_tokens;
+  int32_t layer_begin;
+  int32_t num_layers;
+  int32_t tile_tokens;
+  int32_t replicas;
+  unsigned *flags[kMaxReplicas];  // per replica: flag array [num_layers_total]
+  DeviceStatus *status;
+};
+
+__device__ __forceinline__ int64_t push_slot(const void *p, int is64, int t) {
+  return is64 ? static_cast<const int64_t *>(p)[t]
+              : static_cast<int64_t>(static_cast<const int32_t *>(p)[t]);
+}
+
+__device__ __forceinline__ char *dst_addr(const PagedDesc &pd, int rep,
+                                          int layer, int p, int64_t slot) {
+  const int64_t blk = slot / pd.block_size;
+  const int64_t off = slot - blk * pd.block_size;
+  char *base = reinterpret_cast<char *>(
+      pd.ptrs[(static_cast<int64_t>(rep) * pd.num_layers + layer) * pd.num_planes + p]);
+  return base + blk * pd.plane[p].block_stride + off * pd.plane[p].slot_stride;
+}
+
+// One CTA (8 warps) per unit = (layer, plane, tile).  Each warp moves tokens
+// t0 + w, t0 + w + 8, ...; four tokens are in flight per warp when the row is
+// 512 B (Qwen3-32B TP4 shard: 2 heads x 128 x bf16).
+__global__ void __launch_bounds__(kPushWarps * 32)
+    pd_push_kernel(PushJob j) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int np = j.src.num_planes;
+  const int tiles = (j.num_tokens + j.tile_tokens - 1) / j.tile_tokens;
+  const int units_per_layer = np * tiles;
+  const int total = units_per_layer * j.num_layers;
+  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    const int li = u / units_per_layer;
+    const int rem = u - li * units_per_layer;
+    const int p = rem / tiles;
+    const int tile = rem - p * tiles;
+    const int layer = j.layer_begin + li;
+    const int rb = j.src.plane[p].row_bytes;
+    const int t0 = tile * j.tile_tokens;
+    const int t1 = min(j.num_tokens, t0 + j.tile_tokens);
+    const bool v16 = (rb & 15) == 0;
+    for (int tb = t0 + warp * 4; tb < t1; tb += kPushWarps * 4) {
+      // gather addresses for up to 4 tokens
+      const char *s[4];
+      int64_t ds[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = tb + q;
+        s[q] = nullptr;
+        ds[q] = -1;
+        if (t < t1) {
+          const int64_t ss = push_slot(j.src_slots, j.slot_is_i64, t);
+          const int64_t dd = push_slot(j.dst_slots, j.slot_is_i64, t);
+          if (ss >= 0 && dd >= 0) {
+            if (ss >= j.src.num_slots || dd >= j.dst.num_slots) {
+              if (lane == 0)
+                report_status(j.status, kStatusBadSlot, t, ss, dd);
+            } else {
+              s[q] = paged_addr(j.src, layer, p, ss);
+              ds[q] = dd;
+            }
+          }
+        }
+      }
+      if (v16) {
+        for (int off = lane * 16; off < rb; off += 512) {
+          int4 v[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (s[q]) v[q] = ld_nc_v4(s[q] + off);
+          for (int r = 0; r < j.replicas; ++r) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (s[q]) st_cs_v4(dst_addr(j.dst, r, layer, p, ds[q]) + off, v[q]);
+          }
+        }
+      } else {
+        for (int q = 0; q < 4; ++q) {
+          if (!s[q]) continue;
+          for (int r = 0; r < j.replicas; ++r) {
+            char *d = dst_addr(j.dst, r, layer, p, ds[q]);
+            for (int off = lane; off < rb; off += 32) d[off] = s[q][off];
+          }
+        }
+      }
+    }
+    // publish this unit: all warps' stores are ordered before the release
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      fence_acq_rel_sys();
+      for (int r = 0; r < j.replicas; ++r)
+        if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
+    }
+  }
+}
+
+// Decoder side: one thread per layer waits (bounded) until
+// flags[layer] - targets[i] >= 0.  Writes kStatusFlagTimeout on expiry.
+__global__ void pd_wait_flags_kernel(const unsigned *flags,
+                                     const unsigned *targets, int layer_begin,
+                                     int num_layers,
+                                     unsigned long long budget_ns,
+                                     DeviceStatus *status) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= num_layers) return;
+  unsigned seen = 0;
+  if (!wait_flag_geq(flags + layer_begin + i, targets[i], budget_ns, &seen))
+    report_status(status, kStatusFlagTimeout, layer_begin + i, seen, targets[i]);
+}
+
+static int env_int2(const char *name, int dflt) {
+  const char *v = std::getenv(name);
+  return v ? std::atoi(v) : dflt;
+}
+
+int64_t push_units_per_layer(int64_t num_tokens, int64_t num_planes,
+                             int64_t tile_tokens) {
+  return num_planes * ((num_tokens + tile_tokens - 1) / tile_tokens);
+}
+
+void pd_push(const PagedLayout &src, const PagedLayout &dst,
+             const at::Tensor &src_slots, const at::Tensor &dst_slots,
+             int64_t layer_begin, int64_t num_layers, int64_t replicas,
+             const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
+             int64_t grid, const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(src_slots.is_cuda() && dst_slots.is_cuda(),
+              "slot mappings must live on the device");
+  TORCH_CHECK(src_slots.scalar_type() == dst_slots.scalar_type(),
+              "src/dst slot mappings must share a dtype");
+  TORCH_CHECK(src_slots.numel() == dst_slots.numel(),
+              "src/dst slot mappings must have the same length");
+  TORCH_CHECK(src_slots.is_contiguous() && dst_slots.is_contiguous(),
+              "slot mappings must be contiguous");
+  TORCH_CHECK(replicas >= 1 && replicas <= kMaxReplicas, "1..4 replicas");
+  TORCH_CHECK(src.desc().num_planes == dst.desc().num_planes,
+              "src/dst plane count mismatch");
+  TORCH_CHECK(dst.desc().num_layers % replicas == 0,
+              "dst table must hold replicas * layers entries");
+  const int dst_layers = dst.desc().num_layers / static_cast<int>(replicas);
+  TORCH_CHECK(layer_begin >= 0 && layer_begin + num_layers <= src.desc().num_layers &&
+                  layer_begin + num_layers <= dst_layers,
+              "layer range out of the caches");
+  for (int p = 0; p < src.desc().num_planes; ++p)
+    TORCH_CHECK(src.desc().plane[p].row_bytes == dst.desc().plane[p].row_bytes,
+                "src/dst row size mismatch on plane ", p);
+  TORCH_CHECK(flag_ptrs.empty() || static_cast<int64_t>(flag_ptrs.size()) == replicas,
+              "flag_ptrs: one per replica (or none)");
+  if (src_slots.numel() == 0 || num_layers == 0) return;
+  const c10::cuda::CUDAGuard guard(src_slots.device());
+  PushJob j;
+  std::memset(&j, 0, sizeof(j));
+  j.src = src.desc();
+  j.dst = dst.desc();
+  j.dst.num_layers = dst_layers;
+  j.src_slots = src_slots.data_ptr();
+  j.dst_slots = dst_slots.data_ptr();
+  j.slot_is_i64 = src_slots.scalar_type() == at::kLong;
+  j.num_tokens = static_cast<int32_t>(src_slots.numel());
+  j.layer_begin = static_cast<int32_t>(layer_begin);
+  j.num_layers = static_cast<int32_t>(num_layers);
+  j.tile_tokens = static_cast<int32_t>(tile_tokens > 0 ? tile_tokens : 128);
+  j.replicas = static_cast<int32_t>(replicas);
+  for (size_t r = 0; r < flag_ptrs.size(); ++r)
+    j.flags[r] = reinterpret_cast<unsigned *>(flag_ptrs[r]);
+  if (status.has_value()) {
+    TORCH_CHECK(status->is_cuda() && status->nbytes() >= sizeof(DeviceStatus),
+                "status must be a device tensor of >= 24 bytes");
+    j.status = reinterpret_cast<DeviceStatus *>(status->data_ptr());
+  }
+  const int dev = src_slots.device().index();
+  const long long units =
+      push_units_per_layer(j.num_tokens, j.src.num_planes, j.tile_tokens) *
+      static_cast<long long>(num_layers);
+  int g = grid > 0 ? static_cast<int>(grid)
+                   : env_int2("LMC_PUSH_GRID", num_sms(dev) * 2);
+  g = static_cast<int>(std::max(1LL, std::min<long long>(units, g)));
+  pd_push_kernel<<<g, kPushWarps * 32, 0,
+                   at::cuda::getCurrentCUDAStream(dev).stream()>>>(j);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets,
+                   int64_t layer_begin, double timeout_s,
+                   const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(targets.is_cuda() && targets.scalar_type() == at::kInt,
+              "targets must be a device int32 tensor");
+  const c10::cuda::CUDAGuard guard(targets.device());
+  const int n = static_cast<int>(targets.numel());
+  if (n == 0) return;
+  DeviceStatus *st = nullptr;
+  if (status.has_value())
+    st = reinterpret_cast<DeviceStatus *>(status->data_ptr());
+  const unsigned long long budget =
+      static_cast<unsigned long long>(std::max(0.0, timeout_s) * 1e9);
+  pd_wait_flags_kernel<<<(n + 127) / 128, 128, 0,
+                         at::cuda::getCurrentCUDAStream(targets.device().index())
+                             .stream()>>>(
+      reinterpret_cast<const unsigned *>(flags_ptr),
+      reinterpret_cast<const unsigned *>(targets.data_ptr()),
+      static_cast<int>(layer_begin), n, budget, st);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace lmc

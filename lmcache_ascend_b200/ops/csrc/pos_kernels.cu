@@ -1,0 +1,144 @@
+// K8: fused RoPE re-rotation of cached keys (CacheBlend re-positioning).
+//
+// Semantics of the reference op `rotary_embedding_k_fused(old_positions,
+// new_positions, key, head_size, cos_sin_cache, is_neox)`
+// (csrc/pos_kernels.cpp:164-196, Python wrapper
+// lmcache_ascend/v1/blend/positional_encoding.py:95-118): K was rotated for
+// positions `old`; rewrite it in place as if it had been rotated for `new`.
+//
+// Instead of undoing and redoing the rotation (two roundings), the kernel
+// rotates once by the angle difference, using the angle-difference identities
+//   cos(a - b) = cos a cos b + sin a sin b,  sin(a - b) = sin a cos b - cos a sin b
+// on the cached cos/sin values in fp32, and rounds once to the key dtype.
+// cos_sin_cache is vLLM's layout: [max_position, rot_dim], first half cos,
+// second half sin.  neox pairs (i, i + rot/2); GPT-J pairs (2i, 2i + 1).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace lmc {
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v) { return static_cast<float>(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v) { return static_cast<T>(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+// grid.x = tokens (grid-stride), block threads cover heads * rot/2 pairs
+template <typename KT, typename CT, typename PT>
+__global__ void rope_delta_kernel(const PT *__restrict__ old_pos,
+                                  const PT *__restrict__ new_pos, KT *key,
+                                  const CT *__restrict__ cache, int num_tokens,
+                                  int num_heads, int head_size, int rot_dim,
+                                  int64_t key_stride, bool neox) {
+  const int half = rot_dim / 2;
+  const int pairs = num_heads * half;
+  for (int t = blockIdx.x; t < num_tokens; t += gridDim.x) {
+    const int64_t po = static_cast<int64_t>(old_pos[t]);
+    const int64_t pn = static_cast<int64_t>(new_pos[t]);
+    const CT *co = cache + po * rot_dim;
+    const CT *cn = cache + pn * rot_dim;
+    KT *kt = key + static_cast<int64_t>(t) * key_stride;
+    for (int q = threadIdx.x; q < pairs; q += blockDim.x) {
+      const int h = q / half;
+      const int i = q - h * half;
+      const float ca = to_f(cn[i]), sa = to_f(cn[half + i]);
+      const float cb = to_f(co[i]), sb = to_f(co[half + i]);
+      const float cd = ca * cb + sa * sb;   // cos(new - old)
+      const float sd = sa * cb - ca * sb;   // sin(new - old)
+      KT *kh = kt + static_cast<int64_t>(h) * head_size;
+      const int i1 = neox ? i : 2 * i;
+      const int i2 = neox ? i + half : 2 * i + 1;
+      const float x1 = to_f(kh[i1]);
+      const float x2 = to_f(kh[i2]);
+      kh[i1] = from_f<KT>(x1 * cd - x2 * sd);
+      kh[i2] = from_f<KT>(x2 * cd + x1 * sd);
+    }
+  }
+}
+
+template <typename KT, typename CT>
+static void launch_rope(const at::Tensor &op, const at::Tensor &np, at::Tensor &key,
+                        const at::Tensor &cache, int T, int H, int D, int rot,
+                        int64_t stride, bool neox, cudaStream_t s) {
+  const int threads = std::min(1024, std::max(32, ((H * rot / 2) + 31) / 32 * 32));
+  const int blocks = std::min(T, 148 * 16);
+  if (op.scalar_type() == at::kLong)
+    rope_delta_kernel<KT, CT, int64_t><<<blocks, threads, 0, s>>>(
+        op.data_ptr<int64_t>(), np.data_ptr<int64_t>(),
+        reinterpret_cast<KT *>(key.data_ptr()),
+        reinterpret_cast<const CT *>(cache.data_ptr()), T, H, D, rot, stride, neox);
+  else
+    rope_delta_kernel<KT, CT, int32_t><<<blocks, threads, 0, s>>>(
+        op.data_ptr<int32_t>(), np.data_ptr<int32_t>(),
+        reinterpret_cast<KT *>(key.data_ptr()),
+        reinterpret_cast<const CT *>(cache.data_ptr()), T, H, D, rot, stride, neox);
+}
+
+void rotary_embedding_k_fused(const at::Tensor &old_positions,
+                              const at::Tensor &new_positions, at::Tensor &key,
+                              int64_t head_size, const at::Tensor &cos_sin_cache,
+                              bool is_neox) {
+  TORCH_CHECK(key.is_cuda() && old_positions.is_cuda() && new_positions.is_cuda() &&
+                  cos_sin_cache.is_cuda(),
+              "rope: all tensors must be on the device");
+  TORCH_CHECK(old_positions.scalar_type() == new_positions.scalar_type() &&
+                  (old_positions.scalar_type() == at::kLong ||
+                   old_positions.scalar_type() == at::kInt),
+              "rope: positions must both be int32 or int64");
+  const int T = static_cast<int>(old_positions.numel());
+  TORCH_CHECK(new_positions.numel() == T, "rope: position length mismatch");
+  TORCH_CHECK(key.dim() >= 2 && key.size(0) == T, "rope: key must be [T, H*D]");
+  TORCH_CHECK(key.stride(-1) == 1, "rope: key rows must be contiguous");
+  const int64_t hidden = key.numel() / T;
+  TORCH_CHECK(hidden % head_size == 0, "rope: hidden not a multiple of head_size");
+  const int H = static_cast<int>(hidden / head_size);
+  const int rot = static_cast<int>(cos_sin_cache.size(1));
+  TORCH_CHECK(rot <= head_size && rot % 2 == 0, "rope: bad rot_dim");
+  TORCH_CHECK(cos_sin_cache.is_contiguous(), "rope: cos_sin_cache must be contiguous");
+  const int64_t stride = key.dim() == 2 ? key.stride(0) : hidden;
+  if (key.dim() != 2) TORCH_CHECK(key.is_contiguous(), "rope: key must be contiguous");
+  if (T == 0) return;
+  const c10::cuda::CUDAGuard guard(key.device());
+  auto op = old_positions.contiguous();
+  auto np = new_positions.contiguous();
+  cudaStream_t s = at::cuda::getCurrentCUDAStream().stream();
+  const auto kt = key.scalar_type();
+  const auto ct = cos_sin_cache.scalar_type();
+  const int D = static_cast<int>(head_size);
+#define LMC_ROPE_CASE(KTYPE, KCT)                                                  \
+  if (ct == at::kFloat)                                                            \
+    launch_rope<KTYPE, float>(op, np, key, cos_sin_cache, T, H, D, rot, stride,    \
+                              is_neox, s);                                         \
+  else if (ct == at::kBFloat16)                                                    \
+    launch_rope<KTYPE, __nv_bfloat16>(op, np, key, cos_sin_cache, T, H, D, rot,    \
+                                      stride, is_neox, s);                         \
+  else if (ct == at::kHalf)                                                        \
+    launch_rope<KTYPE, __half>(op, np, key, cos_sin_cache, T, H, D, rot, stride,   \
+                               is_neox, s);                                        \
+  else                                                                             \
+    TORCH_CHECK(false, "rope: unsupported cos_sin_cache dtype");
+  if (kt == at::kBFloat16) {
+    LMC_ROPE_CASE(__nv_bfloat16, 0)
+  } else if (kt == at::kHalf) {
+    LMC_ROPE_CASE(__half, 0)
+  } else if (kt == at::kFloat) {
+    LMC_ROPE_CASE(float, 0)
+  } else {
+    TORCH_CHECK(false, "rope: unsupported key dtype");
+  }
+#undef LMC_ROPE_CASE
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace lmc

@@ -1,0 +1,463 @@
+"""The LMCache engine: store / retrieve / lookup over token-hash chunks.
+
+Public surface follows the reference's ``AscendLMCacheEngine`` and the
+upstream ``LMCacheEngine`` it extends (reference
+lmcache_ascend/v1/cache_engine.py: ``store`` :8951, ``store_layer`` :6030,
+``lookup`` :3801, ``lookup_unpin`` :3823, ``get_finished_stores`` :3651,
+``wait_for_pending_stores`` :3679, ``get_kv_events`` :3796, ``close`` :10153,
+async store worker :3451-3649, health gate :8979; upstream ``retrieve``,
+``retrieve_layer``, ``prefetch``).
+"""
+
+from __future__ import annotations
+
+import queue
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any, Callable, Dict, Generator, List, Optional, Sequence, Tuple
+
+import torch
+
+from ..config import LMCacheEngineConfig, LMCacheEngineMetadata
+from ..utils.keys import CacheEngineKey
+from ..utils.logging import init_logger
+from ..utils.metrics import get_stats
+from ..utils.nvtx import nvtx_range
+from .gpu_connector import GPUConnectorInterface
+from .memory_management import MemoryFormat, MemoryObj
+from .storage_backend.storage_manager import StorageManager
+from .token_database import ChunkedTokenDatabase, SegmentTokenDatabase, TokenDatabase
+
+logger = init_logger(__name__)
+
+
+@dataclass
+class CacheStoreEvent:
+    """KV cache event (reference cache_engine.py:3588-3616)."""
+
+    block_hashes: List[int]
+    parent_block_hash: Optional[int]
+    token_ids: List[int]
+    block_size: int
+    lora_id: Optional[int] = None
+    medium: str = "cpu"
+
+
+class ThreadSafeEventList:
+    """Append/drain list of KV events (reference cache_engine.py:221-254)."""
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._events: List[CacheStoreEvent] = []
+
+    def append(self, e: CacheStoreEvent) -> None:
+        with self._lock:
+            self._events.append(e)
+
+    def drain(self) -> List[CacheStoreEvent]:
+        with self._lock:
+            out, self._events = self._events, []
+            return out
+
+    def __len__(self) -> int:
+        return len(self._events)
+
+
+@dataclass
+class _StoreRequest:
+    req_id: Any
+    tokens: torch.Tensor
+    mask: Optional[torch.Tensor]
+    kwargs: Dict[str, Any]
+    done: threading.Event = field(default_factory=threading.Event)
+    error: Optional[BaseException] = None
+
+
+class LMCacheEngine:
+    def __init__(self, config: LMCacheEngineConfig, metadata: LMCacheEngineMetadata,
+                 gpu_connector: GPUConnectorInterface,
+                 token_database: Optional[TokenDatabase] = None,
+                 storage_manager: Optional[StorageManager] = None,
+                 broadcast_fn: Optional[Callable] = None,
+                 broadcast_object_fn: Optional[Callable] = None,
+                 collective_all_true_fn: Optional[Callable] = None, **kw):
+        self.config = config
+        self.metadata = metadata
+        self.gpu_connector = gpu_connector
+        if token_database is None:
+            token_database = (SegmentTokenDatabase(config, metadata)
+                              if config.enable_blending else
+                              ChunkedTokenDatabase(config, metadata))
+        self.token_database = token_database
+        self.storage_manager = storage_manager or StorageManager(config, metadata, **kw)
+        self.broadcast_fn = broadcast_fn
+        self.broadcast_object_fn = broadcast_object_fn
+        self.collective_all_true_fn = collective_all_true_fn
+        self.stats = get_stats()
+        self.kv_events = ThreadSafeEventList()
+        self._engine_state_lock = threading.RLock()
+        self._lookup_pins: Dict[Any, List[CacheEngineKey]] = {}
+        self._healthy = True
+        self._closed = False
+        # async store worker (reference cache_engine.py:412-421, 3451)
+        self._store_queue: "queue.Queue[Optional[_StoreRequest]]" = queue.Queue(
+            maxsize=max(1, config.store_async_max_queue_size))
+        self._finished_stores: List[Any] = []
+        self._finished_lock = threading.Lock()
+        self._pending = 0
+        self._pending_cv = threading.Condition()
+        self._worker: Optional[threading.Thread] = None
+        if config.store_async:
+            self._worker = threading.Thread(target=self._store_worker_loop,
+                                            name="lmc-store", daemon=True)
+            self._worker.start()
+
+    # ----------------------------------------------------------- set-up
+    def post_init(self, kvcaches=None, **kw) -> None:
+        if kvcaches is not None and hasattr(self.gpu_connector, "register_kv_caches"):
+            self.gpu_connector.register_kv_caches(kvcaches)
+        for b in self.storage_manager.backends.values():
+            hook = getattr(b, "post_init", None)
+            if hook is not None:
+                hook(gpu_connector=self.gpu_connector, engine=self, **kw)
+
+    def is_healthy(self) -> bool:
+        return self._healthy and not self._closed
+
+    def mark_unhealthy(self, why: str) -> None:
+        logger.error("engine marked unhealthy: %s", why)
+        self._healthy = False
+
+    def _passive(self) -> bool:
+        """MLA latent is replicated across TP ranks: only rank 0 stores."""
+        return self.config.save_only_first_rank and self.metadata.worker_id != 0
+
+    def _key(self, key: CacheEngineKey) -> CacheEngineKey:
+        if self.config.save_only_first_rank and key.worker_id != 0:
+            return key.with_worker(0)
+        return key
+
+    # ------------------------------------------------------------ store
+    def _chunks(self, tokens, mask=None, request_configs=None,
+                hashes=None, offsets=None) -> List[Tuple[int, int, CacheEngineKey]]:
+        return [(s, e, self._key(k)) for s, e, k in self.token_database.process_tokens(
+            tokens=tokens, hashes=hashes, offsets=offsets, mask=mask,
+            request_configs=request_configs)]
+
+    @nvtx_range("lmc.store")
+    def store(self, tokens: Optional[torch.Tensor] = None,
+              mask: Optional[torch.Tensor] = None, **kwargs) -> None:
+        """Store the KV of ``tokens`` (chunks not yet cached) from the paged cache.
+
+        kwargs: ``slot_mapping`` (device tensor, one slot per token),
+        ``kvcaches`` (optional re-registration), ``req_id``,
+        ``request_configs``, ``hashes``/``offsets`` (precomputed chunk hashes).
+        """
+        if not self.is_healthy():
+            logger.warning("store skipped: engine unhealthy")
+            return
+        if self._passive():
+            return
+        if self.config.store_async and self._worker is not None:
+            req = _StoreRequest(kwargs.get("req_id"), tokens, mask, kwargs)
+            with self._pending_cv:
+                self._pending += 1
+            self._store_queue.put(req)
+            return
+        self._run_store(tokens, mask, **kwargs)
+
+    def _run_store(self, tokens, mask=None, **kwargs) -> int:
+        with self.stats.phase("store.process_tokens"):
+            chunks = self._chunks(tokens, mask, kwargs.get("request_configs"),
+                                  kwargs.get("hashes"), kwargs.get("offsets"))
+        todo = [(s, e, k) for s, e, k in chunks
+                if self.storage_manager.contains(k) is None]
+        if not todo:
+            return 0
+        if "kvcaches" in kwargs and kwargs["kvcaches"] is not None and \
+                not getattr(self.gpu_connector, "kvcaches_registered", True):
+            self.gpu_connector.register_kv_caches(kwargs["kvcaches"])
+        objs, starts, ends, keys = [], [], [], []
+        fmt = getattr(self.gpu_connector, "memory_format", MemoryFormat.KV_2LTD)
+        dtype = self.gpu_connector.layout.dtype
+        for s, e, k in todo:
+            obj = self.storage_manager.allocate(self.gpu_connector.get_shape(e - s), dtype, fmt)
+            if obj is None:
+                logger.warning("store: out of CPU cache memory after %d chunks", len(objs))
+                break
+            objs.append(obj)
+            starts.append(s)
+            ends.append(e)
+            keys.append(k)
+        if not objs:
+            return 0
+        with self.stats.phase("store.from_gpu"):
+            self.gpu_connector.batched_from_gpu(objs, starts, ends,
+                                                slot_mapping=kwargs["slot_mapping"])
+        with self.stats.phase("store.put"):
+            self.storage_manager.batched_put(keys, objs,
+                                             transfer_spec=kwargs.get("transfer_spec"))
+        for o in objs:
+            o.ref_count_down()
+        if self.config.enable_kv_events:
+            self._emit_events(tokens, starts, ends, keys)
+        n = sum(e - s for s, e in zip(starts, ends))
+        self.stats.inc("stored_tokens", n)
+        return n
+
+    def _emit_events(self, tokens, starts, ends, keys) -> None:
+        toks = tokens.tolist() if isinstance(tokens, torch.Tensor) else list(tokens)
+        parent = None
+        for s, e, k in zip(starts, ends, keys):
+            self.kv_events.append(CacheStoreEvent([k.chunk_hash], parent, toks[s:e], e - s))
+            parent = k.chunk_hash
+
+    def _store_worker_loop(self) -> None:
+        while True:
+            req = self._store_queue.get()
+            if req is None:
+                return
+            try:
+                self._run_store(req.tokens, req.mask, **req.kwargs)
+            except BaseException as e:  # keep the worker alive
+                req.error = e
+                logger.exception("async store failed")
+            finally:
+                with self._finished_lock:
+                    if req.req_id is not None:
+                        self._finished_stores.append(req.req_id)
+                with self._pending_cv:
+                    self._pending -= 1
+                    self._pending_cv.notify_all()
+                req.done.set()
+
+    def get_finished_stores(self) -> List[Any]:
+        with self._finished_lock:
+            out, self._finished_stores = self._finished_stores, []
+            return out
+
+    def wait_for_pending_stores(self, timeout: Optional[float] = None) -> bool:
+        with self._pending_cv:
+            return self._pending_cv.wait_for(lambda: self._pending == 0, timeout=timeout)
+
+    # --------------------------------------------------------- retrieve
+    @nvtx_range("lmc.retrieve")
+    def retrieve(self, tokens: torch.Tensor, mask: Optional[torch.Tensor] = None,
+                 **kwargs) -> torch.Tensor:
+        """Load the longest cached prefix of ``tokens`` into the paged cache.
+
+        Returns a bool mask over ``tokens``: True where KV was loaded.
+        """
+        n = len(tokens)
+        ret = torch.zeros(n, dtype=torch.bool)
+        if not self.is_healthy():
+            return ret
+        chunks = self._chunks(tokens, mask, kwargs.get("request_configs"),
+                              kwargs.get("hashes"), kwargs.get("offsets"))
+        if not chunks:
+            return ret
+        with self.stats.phase("retrieve.get"):
+            objs = self.storage_manager.batched_get([k for _, _, k in chunks])
+        good, starts, ends = [], [], []
+        for (s, e, _), o in zip(chunks, objs):
+            if o is None:
+                break  # prefix semantics: stop at the first miss
+            good.append(o)
+            starts.append(s)
+            ends.append(e)
+        for o in objs[len(good):]:
+            if o is not None:
+                o.ref_count_down()
+        if good:
+            with self.stats.phase("retrieve.to_gpu"):
+                self.gpu_connector.batched_to_gpu(good, starts, ends,
+                                                  slot_mapping=kwargs["slot_mapping"])
+            for o in good:
+                o.ref_count_down()
+            for s, e in zip(starts, ends):
+                ret[s:e] = True
+        self.stats.inc("retrieved_tokens", int(ret.sum()))
+        return ret
+
+    # ----------------------------------------------------------- lookup
+    def lookup(self, tokens: Optional[torch.Tensor] = None,
+               search_range: Optional[List[str]] = None, lookup_id: Any = None,
+               pin: bool = False, request_configs: Optional[dict] = None,
+               hashes: Optional[List[int]] = None, offsets: Optional[List[int]] = None
+               ) -> int:
+        """Number of prefix tokens whose chunks are cached (pinned if asked)."""
+        with self._engine_state_lock:
+            end = 0
+            pinned = []
+            for s, e, k in self._chunks(tokens, None, request_configs, hashes, offsets):
+                if self.storage_manager.contains(k, search_range, pin=pin) is None:
+                    break
+                if pin:
+                    pinned.append(k)
+                end = e
+            if pin and lookup_id is not None:
+                self._lookup_pins.setdefault(lookup_id, []).extend(pinned)
+            self.stats.inc("lookup_hit_tokens", end)
+            return end
+
+    def lookup_unpin(self, lookup_id: Any) -> None:
+        with self._engine_state_lock:
+            for k in self._lookup_pins.pop(lookup_id, []):
+                self.storage_manager.unpin(k)
+
+    # -------------------------------------------------------- layerwise
+    def store_layer(self, tokens: torch.Tensor, mask: Optional[torch.Tensor] = None,
+                    **kwargs) -> Generator[None, None, None]:
+        """Generator: yields num_layers + 1 times; resume after each layer's KV
+        is written so that layer is gathered while the next one computes."""
+        conn = self.gpu_connector
+        if not self.is_healthy() or self._passive():
+            for _ in range(conn.layout.num_layers + 1):
+                yield
+            return
+        chunks = [(s, e, k) for s, e, k in self._chunks(tokens, mask)
+                  if self.storage_manager.contains(k) is None]
+        L = conn.layout.num_layers
+        dtype = conn.layout.dtype
+        fmt = getattr(conn, "memory_format", MemoryFormat.KV_2LTD)
+        per_layer: List[List[MemoryObj]] = []
+        for layer in range(L):
+            row = []
+            for s, e, k in chunks:
+                o = self.storage_manager.allocate(conn.get_shape(e - s), dtype, fmt)
+                if o is None:
+                    raise RuntimeError("store_layer: out of CPU cache memory")
+                row.append(o)
+            per_layer.append(row)
+        starts = [s for s, _, _ in chunks]
+        ends = [e for _, e, _ in chunks]
+        gen = conn.batched_from_gpu(per_layer, starts, ends,
+                                    slot_mapping=kwargs["slot_mapping"])
+        next(gen)
+        for layer in range(L):
+            yield
+            next(gen, None)
+        for layer in range(L):
+            lkeys = [k.split_layers(L)[layer] for _, _, k in chunks]
+            self.storage_manager.batched_put(lkeys, per_layer[layer])
+            for o in per_layer[layer]:
+                o.ref_count_down()
+        yield
+
+    def retrieve_layer(self, tokens: torch.Tensor, mask: Optional[torch.Tensor] = None,
+                       **kwargs) -> Generator[Optional[torch.Tensor], None, None]:
+        """Generator: yields num_layers + 2 times.  The first yield returns
+        after lookup; each following resume loads one layer; the last yield
+        returns the retrieved-token mask."""
+        conn = self.gpu_connector
+        L = conn.layout.num_layers
+        n = len(tokens)
+        ret = torch.zeros(n, dtype=torch.bool)
+        chunks = self._chunks(tokens, mask)
+        per_layer: List[List[MemoryObj]] = []
+        hit = 0
+        for s, e, k in chunks:
+            lkeys = k.split_layers(L)
+            objs = [self.storage_manager.get(lk) for lk in lkeys]
+            if any(o is None for o in objs):
+                for o in objs:
+                    if o is not None:
+                        o.ref_count_down()
+                break
+            if not per_layer:
+                per_layer = [[] for _ in range(L)]
+            for layer, o in enumerate(objs):
+                per_layer[layer].append(o)
+            hit += 1
+        chunks = chunks[:hit]
+        starts = [s for s, _, _ in chunks]
+        ends = [e for _, e, _ in chunks]
+        yield None
+        if hit:
+            gen = conn.batched_to_gpu(None, starts, ends, slot_mapping=kwargs["slot_mapping"])
+            next(gen)
+            gen.send(per_layer)
+            for layer in range(1, L):
+                yield None
+                next(gen)
+            yield None
+            next(gen, None)
+            for row in per_layer:
+                for o in row:
+                    o.ref_count_down()
+            for s, e in zip(starts, ends):
+                ret[s:e] = True
+        else:
+            for _ in range(L):
+                yield None
+        yield ret
+
+    # ------------------------------------------------------------- misc
+    def prefetch(self, tokens: torch.Tensor, mask: Optional[torch.Tensor] = None) -> None:
+        """Promote cached chunks from lower tiers into the CPU tier."""
+        for _, _, k in self._chunks(tokens, mask):
+            obj = self.storage_manager.get(k)
+            if obj is None:
+                break
+            obj.ref_count_down()
+
+    def remove(self, tokens: torch.Tensor, locations: Optional[List[str]] = None) -> int:
+        n = 0
+        for _, _, k in self._chunks(tokens):
+            n += self.storage_manager.remove(k, locations)
+        return n
+
+    def clear(self, locations: Optional[List[str]] = None) -> int:
+        n = 0
+        for name, b in self.storage_manager.backends.items():
+            if locations is not None and name not in locations:
+                continue
+            for k in b.keys():
+                n += int(b.remove(k))
+        return n
+
+    def get_kv_events(self) -> List[CacheStoreEvent]:
+        return self.kv_events.drain()
+
+    def close(self) -> None:
+        if self._closed:
+            return
+        if self._worker is not None:
+            self.wait_for_pending_stores(timeout=self.config.blocking_timeout_secs)
+            self._store_queue.put(None)
+            self._worker.join(timeout=5)
+        self._closed = True
+        self.storage_manager.close()
+        close = getattr(self.gpu_connector, "close", None)
+        if close:
+            close()
+
+
+class LMCacheEngineBuilder:
+    """Process-wide registry of engines by instance id (upstream builder)."""
+
+    _engines: Dict[str, LMCacheEngine] = {}
+    _lock = threading.Lock()
+
+    @classmethod
+    def get_or_create(cls, instance_id: str, config: LMCacheEngineConfig,
+                      metadata: LMCacheEngineMetadata,
+                      gpu_connector: GPUConnectorInterface, **kw) -> LMCacheEngine:
+        with cls._lock:
+            eng = cls._engines.get(instance_id)
+            if eng is None:
+                eng = LMCacheEngine(config, metadata, gpu_connector, **kw)
+                cls._engines[instance_id] = eng
+            return eng
+
+    @classmethod
+    def get(cls, instance_id: str) -> Optional[LMCacheEngine]:
+        return cls._engines.get(instance_id)
+
+    @classmethod
+    def destroy(cls, instance_id: str) -> None:
+        with cls._lock:
+            eng = cls._engines.pop(instance_id, None)
+        if eng is not None:
+            eng.close()
