@@ -1,0 +1,326 @@
+#!/usr/bin/env python
+"""Headline benchmark: prefill->decode KV push (GB/s), Qwen3-32B-shaped.
+
+1 prefiller at TP4 -> 1 decoder at TP4 on 8 GPUs,
+Qwen3-32B KV (64 layers, 8 KV heads split over TP4 = 2 heads per rank,
+head_dim 128, block_size 128, bf16), 16384-token requests pushed layer by
+layer from the prefiller's paged blocks into the decoder's paged blocks.
+
+Scaling (weak): each GPU pair carries one TP4 shard (2 KV heads) of one
+16k-token request per step.  N GPUs = N/2 pairs (rank r -> rank r + N/2);
+N=1 runs the same kernel in loopback (prefiller and decoder caches on one
+GPU, bound by HBM instead of NVLink).  ``value`` is the whole-job aggregate
+GB/s over all pairs; ``e2e`` repeats the measurement through the public push
+API with per-step host->device slot-mapping copies and a device->host
+completion-status read.
+
+Launch: ``python bench.py`` (N=1) or
+``torchrun --nproc-per-node N bench.py --gpus N``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+PUBLISHED_GBPS = None  # the reference publishes no KV-push number
+NVLINK_GBPS = 770.0    # measured peer-copy bandwidth per direction (profiling recipe)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "nccl", "reference"])
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--layers", type=int, default=64)
+    ap.add_argument("--heads", type=int, default=2, help="KV heads per rank (TP4 shard)")
+    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--block-size", type=int, default=128)
+    ap.add_argument("--grid", type=int, default=0)
+    ap.add_argument("--tile", type=int, default=128)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def out(d):
+    print(json.dumps(d), flush=True)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+        self.path = f"/tmp/lmc_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def block_table_slots(T, block_size, num_blocks, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    nblk = (T + block_size - 1) // block_size
+    blocks = torch.randperm(num_blocks, generator=g)[:nblk]
+    t = torch.arange(T)
+    return (blocks[t // block_size] * block_size + t % block_size).to(torch.int32).to(device)
+
+
+def make_cache(L, num_blocks, block_size, H, D, device, seed):
+    """vLLM SEPARATE_KV layout: per layer (K, V) each [NB, BS, H, D] bf16."""
+    torch.manual_seed(seed)
+    kv = []
+    for _ in range(L):
+        k = torch.randn(num_blocks, block_size, H, D, device=device, dtype=torch.bfloat16)
+        v = torch.randn(num_blocks, block_size, H, D, device=device, dtype=torch.bfloat16)
+        kv.append((k, v))
+    return kv
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = {"model": "Qwen3-32B (KV shape: 64 layers, 8 KV heads, head_dim 128)",
+           "global_batch": max(1, world // 2), "seq_len": a.tokens,
+           "parallelism": ("pd-loopback-1gpu" if world == 1 else
+                           f"1P(TP{world // 2})->1D(TP{world // 2})"),
+           "kv_heads_per_rank": a.heads, "block_size": a.block_size, "layers": a.layers,
+           "l2": "inputs larger than L2 (1 GiB of KV read per rank per step)"}
+    if a.impl == "reference":
+        if rank == 0:
+            out({"impl": "reference", "unavailable":
+                 "LMCache-Ascend needs CANN/torch_npu and an Ascend NPU: its setup.py stops "
+                 "with 'No available NPU found' (pip install from /root/reference fails)"})
+        return
+    if not torch.cuda.is_available():
+        if rank == 0:
+            out({"metric": "kv_push_gbps", "unavailable": "no CUDA device"})
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+
+    gloo = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
+        if world % 2:
+            raise SystemExit("bench needs an even number of GPUs (prefiller/decoder pairs)")
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from lmcache_ascend_b200 import ops
+    from lmcache_ascend_b200.parallel.pd_push import PushReceiver, PushSender, ReceiverDesc
+    from lmcache_ascend_b200.v1.kv_format import PagedKVLayout
+
+    ops.native()
+    L, T, H, D, BS = a.layers, a.tokens, a.heads, a.head_dim, a.block_size
+    nblocks = 2 * ((T + BS - 1) // BS)
+    pairs = 1 if world == 1 else world // 2
+    role_p = world == 1 or rank < world // 2
+    role_d = world == 1 or rank >= world // 2
+    bytes_per_pair = T * L * 2 * H * D * 2  # K and V rows, bf16
+
+    src_cache = make_cache(L, nblocks, BS, H, D, dev, 1 + rank) if role_p else None
+    dst_cache = make_cache(L, nblocks, BS, H, D, dev, 1000 + rank) if role_d else None
+    src_slots = block_table_slots(T, BS, nblocks, 11, dev)
+    dst_slots = block_table_slots(T, BS, nblocks, 22, dev)
+
+    sender = receiver = None
+    if role_d:
+        receiver = PushReceiver(PagedKVLayout(dst_cache))
+    if role_p:
+        sender = PushSender(PagedKVLayout(src_cache))
+    if world == 1:
+        sender.connect([receiver.desc])
+    else:
+        descs = [None] * world
+        dist.all_gather_object(descs, receiver.desc.to_dict() if receiver else None, group=gloo)
+        if role_p:
+            sender.connect([ReceiverDesc.from_dict(descs[rank + world // 2])])
+        dist.barrier(group=gloo)
+
+    # ---------------------------------------------------------- impl bodies
+    def step_ours(targets):
+        if sender is not None:
+            sender.push(src_slots, dst_slots, tile_tokens=a.tile, grid=a.grid)
+        if receiver is not None:
+            receiver.wait(targets, timeout_s=5.0)
+
+    peer = (rank + world // 2) % world if world > 1 else 0
+
+    def step_nccl(_targets):
+        # baseline: per layer, index_select -> NCCL send/recv -> index_copy_
+        for l in range(L):
+            if role_p:
+                k, v = src_cache[l]
+                buf = torch.stack([k.view(-1, H * D).index_select(0, src_slots.long()),
+                                   v.view(-1, H * D).index_select(0, src_slots.long())])
+            if world == 1:
+                rows = buf
+            elif role_p:
+                dist.send(buf, dst=peer)
+                continue
+            else:
+                rows = torch.empty(2, T, H * D, device=dev, dtype=torch.bfloat16)
+                dist.recv(rows, src=peer)
+            k, v = dst_cache[l]
+            k.view(-1, H * D).index_copy_(0, dst_slots.long(), rows[0])
+            v.view(-1, H * D).index_copy_(0, dst_slots.long(), rows[1])
+
+    step = step_ours if a.impl == "ours" else step_nccl
+    n_targets = a.warmup + a.steps + (a.steps if not a.no_e2e else 0)
+    targets = ([receiver.expect(T, tile_tokens=a.tile) for _ in range(n_targets)]
+               if (receiver is not None and a.impl == "ours") else [None] * n_targets)
+    ti = 0
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=gloo)
+        torch.cuda.synchronize()
+
+    for _ in range(a.warmup):
+        step(targets[ti]); ti += 1
+    barrier()
+    if receiver is not None and a.impl == "ours":
+        receiver.check()
+    if sender is not None and a.impl == "ours":
+        sender.check()
+
+    clocks = ClockSampler(local)
+    if rank == 0:
+        clocks.start()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step(targets[ti]); ti += 1
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    barrier()
+    ck = clocks.stop() if rank == 0 else None
+    if a.impl == "ours":
+        if receiver is not None:
+            receiver.check()
+        if sender is not None:
+            sender.check()
+
+    # max over ranks
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = bytes_per_pair * pairs / (ms / 1e3) / 1e9
+
+    # ------------------------------------------------------------ e2e arm
+    e2e = None
+    if not a.no_e2e and a.impl == "ours":
+        h_src = src_slots.cpu().pin_memory()
+        h_dst = dst_slots.cpu().pin_memory()
+        d_src = torch.empty_like(src_slots)
+        d_dst = torch.empty_like(dst_slots)
+        h_status = torch.empty(4, dtype=torch.int64).pin_memory()
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(a.steps):
+            if sender is not None:
+                d_src.copy_(h_src, non_blocking=True)
+                d_dst.copy_(h_dst, non_blocking=True)
+                sender.push(d_src, d_dst, tile_tokens=a.tile, grid=a.grid)
+                h_status.copy_(sender.status.tensor, non_blocking=True)
+            if receiver is not None:
+                receiver.wait(targets[ti], timeout_s=5.0)
+                h_status.copy_(receiver.status.tensor, non_blocking=True)
+            ti += 1
+            torch.cuda.current_stream().synchronize()
+            if int(h_status[0]) != 0:
+                raise RuntimeError(f"push reported status {h_status.tolist()}")
+        t1.record()
+        torch.cuda.synchronize()
+        ems = torch.tensor([t0.elapsed_time(t1) / a.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        ems = float(ems.item())
+        e2e = {"value": round(bytes_per_pair * pairs / (ems / 1e3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(ems, 4),
+               "h2d_bytes_per_step": (src_slots.numel() + dst_slots.numel()) * 4 * pairs,
+               "d2h_bytes_per_step": 32 * world,
+               "api": "lmcache_ascend_b200.parallel.pd_push.PushSender.push / PushReceiver.wait"}
+
+    if rank == 0:
+        per_pair = value / pairs
+        if world == 1:
+            roof = {"bound": "HBM (loopback read+write)",
+                    "frac_of_measured_hbm": round(2 * per_pair / 6554.9, 4)}
+        else:
+            roof = {"bound": "NVLink per direction (measured 770 GB/s)",
+                    "frac_of_nvlink_per_pair": round(per_pair / NVLINK_GBPS, 4)}
+        launches = (a.steps * (2 if world == 1 else world)) if a.impl == "ours" else 0
+        out({"metric": "kv_push_gbps", "value": round(value, 2), "unit": "GB/s",
+             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
+             "higher_is_better": True, "scaling": "weak",
+             "vs_baseline": None, "impl": a.impl, "dtype": "bf16",
+             "data": "synthetic (random-init bf16 KV of the Qwen3-32B TP4 shard shape, "
+                     "random block tables)",
+             "config": cfg, "bytes_per_pair_per_step": bytes_per_pair,
+             "per_pair_gbps": round(per_pair, 2), "roofline": roof,
+             "clocks": ck, "e2e": e2e, "gpu_launches": launches})
+    if sender is not None:
+        sender.close()
+    if world > 1:
+        dist.barrier(group=gloo)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -28,8 +28,8 @@ GetAddressRangeFn address_range_fn() {
   static GetAddressRangeFn fn = [] {
     void *f = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault,
-                                &q) != cudaSuccess ||
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000,
+                                         cudaEnableDefault, &q) != cudaSuccess ||
         q != cudaDriverEntryPointSuccess)
       f = nullptr;
     return reinterpret_cast<GetAddressRangeFn>(f);

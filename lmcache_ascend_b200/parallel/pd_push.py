@@ -1,0 +1,144 @@
+"""Disaggregated-prefill KV push over NVLink (host side of the K9 kernel).
+
+Roles:
+* ``PushReceiver`` (decoder rank): describes its paged KV cache and a small
+  flag array (one cumulative counter per layer, in its own HBM) as CUDA IPC
+  descriptors, and waits for pushed layers with a bounded device-side spin.
+* ``PushSender`` (prefiller rank): maps the receiver's planes and flags into
+  its address space and launches ``pd_push``: one kernel that reads the
+  prefiller's paged rows and stores them into the decoder's paged blocks
+  through peer addresses (NVLink / NVSwitch), then releases each layer's flag.
+
+The exchange of descriptors is left to the caller (torch.distributed object
+collectives in the benchmark, the PD backend's ZMQ handshake in serving).
+Fan-out to several receivers (TP-replicated MLA latent) is one launch with
+``replicas`` destination tables; the rows are read once.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from .. import ops
+from ..v1.kv_format import PagedKVLayout
+from .ipc import IpcDesc, PeerMappings, export_local
+
+
+@dataclass
+class ReceiverDesc:
+    num_layers: int
+    block_size: int
+    num_slots: int
+    block_stride: List[int]
+    slot_stride: List[int]
+    row_bytes: List[int]
+    planes: List[List[dict]]  # [layer][plane] -> IpcDesc dict
+    flags: dict               # IpcDesc dict of the flag array
+    device: int
+
+    def to_dict(self) -> dict:
+        return self.__dict__.copy()
+
+    @staticmethod
+    def from_dict(d: dict) -> "ReceiverDesc":
+        return ReceiverDesc(**d)
+
+
+class PushReceiver:
+    def __init__(self, layout: PagedKVLayout, max_layers: Optional[int] = None):
+        self.layout = layout
+        self.device = layout.device
+        dev = self.device.index or 0
+        n = max(layout.num_layers, max_layers or 0)
+        self._flags_buf = ops.native().device_buffer(4 * max(n, 1), dev)
+        self.flags = self._flags_buf.view(torch.int32)
+        self.expected = [0] * n  # cumulative flag target per layer
+        self.status = ops.DeviceStatus(self.device)
+        planes = []
+        for layer in range(layout.num_layers):
+            row = []
+            for p in layout.planes:
+                row.append(export_local(p.views[layer].data_ptr(), dev).to_dict())
+            planes.append(row)
+        es = layout.elem_size
+        self.desc = ReceiverDesc(
+            num_layers=layout.num_layers, block_size=layout.block_size,
+            num_slots=layout.num_slots,
+            block_stride=[p.views[0].stride(0) * es for p in layout.planes],
+            slot_stride=[p.views[0].stride(1) * es for p in layout.planes],
+            row_bytes=layout.row_bytes, planes=planes,
+            flags=export_local(self._flags_buf.data_ptr(), dev).to_dict(), device=dev)
+
+    def expect(self, num_tokens: int, layer_begin: int = 0,
+               num_layers: Optional[int] = None, tile_tokens: int = 128) -> torch.Tensor:
+        """Record one incoming push; returns the device targets for ``wait``."""
+        nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
+        units = ops.native().push_units_per_layer(num_tokens, self.layout.num_planes,
+                                                  tile_tokens)
+        tg = []
+        for l in range(layer_begin, layer_begin + nl):
+            self.expected[l] = (self.expected[l] + units) & 0xFFFFFFFF
+            tg.append(self.expected[l] - (1 << 32) if self.expected[l] >= (1 << 31)
+                      else self.expected[l])
+        return torch.tensor(tg, dtype=torch.int32).to(self.device, non_blocking=True)
+
+    def wait(self, targets: torch.Tensor, layer_begin: int = 0,
+             timeout_s: float = 10.0) -> None:
+        """Enqueue a bounded wait on the current stream (no host sync)."""
+        ops.native().pd_wait_flags(self._flags_buf.data_ptr(), targets, layer_begin,
+                                   timeout_s, self.status.tensor)
+
+    def check(self) -> None:
+        self.status.check("pd push receiver")
+
+
+class PushSender:
+    def __init__(self, layout: PagedKVLayout):
+        self.layout = layout
+        self.device = layout.device
+        self.peers = PeerMappings(self.device.index or 0)
+        self.status = ops.DeviceStatus(self.device)
+        self._dst = None
+        self._flag_ptrs: List[int] = []
+        self.replicas = 0
+
+    def connect(self, receivers: Sequence[ReceiverDesc]) -> None:
+        """Map one or more receivers (same layout, fan-out) for pushing."""
+        mod = ops.native()
+        r0 = receivers[0]
+        for r in receivers:
+            if (r.row_bytes != self.layout.row_bytes or r.num_layers != r0.num_layers
+                    or r.block_size != r0.block_size or r.block_stride != r0.block_stride
+                    or r.slot_stride != r0.slot_stride):
+                raise ValueError("receiver layouts must match the sender's rows and each other")
+        ptrs = []
+        for r in receivers:
+            for layer in range(r.num_layers):
+                for pd in r.planes[layer]:
+                    ptrs.append(self.peers.resolve(IpcDesc.from_dict(pd)))
+        table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self._dst = mod.PagedLayout(table, r0.block_stride, r0.slot_stride, r0.row_bytes,
+                                    r0.block_size, r0.num_slots)
+        self._dst.set_bases_aligned(all(p % 16 == 0 for p in ptrs))
+        self._flag_ptrs = [self.peers.resolve(IpcDesc.from_dict(r.flags)) for r in receivers]
+        self.replicas = len(receivers)
+
+    def push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, layer_begin: int = 0,
+             num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0) -> None:
+        """Enqueue the push of ``num_layers`` layers on the current stream."""
+        if self._dst is None:
+            raise RuntimeError("PushSender.connect() first")
+        nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
+        ops.native().pd_push(self.layout.native(), self._dst, src_slots, dst_slots,
+                             layer_begin, nl, self.replicas, self._flag_ptrs, tile_tokens,
+                             grid, self.status.tensor)
+
+    def check(self) -> None:
+        self.status.check("pd push sender")
+
+    def close(self) -> None:
+        self.peers.close()
+        self._dst = None

@@ -1,0 +1,112 @@
+"""K9 PD push: byte-exact paged->paged push, per-layer flags, bounded wait.
+
+Single-GPU tests run the push in loopback (sender and receiver caches on one
+device; same kernel, local instead of peer addresses).  The timeout test
+waits on a flag that nothing sets and checks the reported status: the wait is
+bounded (0.2 s) and the context stays usable.
+"""
+
+import pytest
+import torch
+
+from lmcache_ascend_b200.parallel.pd_push import PushReceiver, PushSender
+from lmcache_ascend_b200.v1.kv_format import PagedKVLayout
+
+from .utils import block_slots, make_mla_kv, make_separate_kv, random_slots
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rows(kv, slots):
+    s = slots.long()
+    out = []
+    for layer in kv:
+        for t in layer:
+            out.append(t.view(t.shape[0] * t.shape[1], -1)[s])
+    return out
+
+
+@pytest.mark.parametrize("pattern", ["blocks", "random"])
+@pytest.mark.parametrize("tile", [32, 128])
+def test_loopback_push_exact(pattern, tile):
+    L, NB, BS = 6, 32, 128
+    src = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=1)
+    dst = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=2)
+    T = 1000
+    if pattern == "blocks":
+        ss = block_slots(T, BS, NB, seed=3, device=DEV, dtype=torch.int32)
+        ds = block_slots(T, BS, NB, seed=4, device=DEV, dtype=torch.int32)
+    else:
+        ss = random_slots(T, NB * BS, seed=5, device=DEV, dtype=torch.int32)
+        ds = random_slots(T, NB * BS, seed=6, device=DEV, dtype=torch.int32)
+    recv = PushReceiver(PagedKVLayout(dst))
+    send = PushSender(PagedKVLayout(src))
+    send.connect([recv.desc])
+    tg = recv.expect(T, tile_tokens=tile)
+    send.push(ss, ds, tile_tokens=tile)
+    recv.wait(tg, timeout_s=2.0)
+    torch.cuda.synchronize()
+    send.check()
+    recv.check()
+    for a, b in zip(_rows(src, ss), _rows(dst, ds)):
+        assert torch.equal(a, b)
+    # flags: units per layer = planes * ceil(T / tile)
+    per_layer = 2 * ((T + tile - 1) // tile)
+    assert recv.flags[:L].tolist() == [per_layer] * L
+
+
+def test_layerwise_push_and_partial_wait():
+    L, NB, BS = 4, 16, 128
+    src = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=7)
+    dst = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=8)
+    T = 512
+    ss = block_slots(T, BS, NB, seed=9, device=DEV, dtype=torch.int32)
+    ds = block_slots(T, BS, NB, seed=10, device=DEV, dtype=torch.int32)
+    recv = PushReceiver(PagedKVLayout(dst))
+    send = PushSender(PagedKVLayout(src))
+    send.connect([recv.desc])
+    for layer in range(L):
+        tg = recv.expect(T, layer_begin=layer, num_layers=1)
+        send.push(ss, ds, layer_begin=layer, num_layers=1)
+        recv.wait(tg, layer_begin=layer, timeout_s=2.0)
+    torch.cuda.synchronize()
+    recv.check()
+    for a, b in zip(_rows(src, ss), _rows(dst, ds)):
+        assert torch.equal(a, b)
+
+
+def test_fanout_two_replicas_mla():
+    L, NB, BS = 3, 16, 64
+    src = make_mla_kv(L, NB, BS, 512, 64, torch.bfloat16, DEV, seed=11)
+    d1 = make_mla_kv(L, NB, BS, 512, 64, torch.bfloat16, DEV, seed=12)
+    d2 = make_mla_kv(L, NB, BS, 512, 64, torch.bfloat16, DEV, seed=13)
+    T = 300
+    ss = random_slots(T, NB * BS, seed=14, device=DEV, dtype=torch.int64)
+    ds = random_slots(T, NB * BS, seed=15, device=DEV, dtype=torch.int64)
+    r1 = PushReceiver(PagedKVLayout(d1, use_mla=True))
+    r2 = PushReceiver(PagedKVLayout(d2, use_mla=True))
+    send = PushSender(PagedKVLayout(src, use_mla=True))
+    send.connect([r1.desc, r2.desc])
+    t1, t2 = r1.expect(T), r2.expect(T)
+    send.push(ss, ds)
+    r1.wait(t1, timeout_s=2.0)
+    r2.wait(t2, timeout_s=2.0)
+    torch.cuda.synchronize()
+    r1.check()
+    r2.check()
+    for a, b, c in zip(_rows(src, ss), _rows(d1, ds), _rows(d2, ds)):
+        assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_wait_times_out_with_status():
+    dst = make_separate_kv(2, 4, 16, 1, 64, torch.bfloat16, DEV)
+    recv = PushReceiver(PagedKVLayout(dst))
+    tg = recv.expect(64)  # nothing will ever push
+    recv.wait(tg, timeout_s=0.2)
+    torch.cuda.synchronize()
+    st = recv.status.read()
+    assert st["name"] == "flag_timeout"
+    # the context is still usable
+    x = torch.ones(4, device=DEV) * 2
+    assert float(x.sum()) == 8.0

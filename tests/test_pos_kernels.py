@@ -1,0 +1,42 @@
+"""K8 fused RoPE re-rotation vs an fp32 PyTorch reference (reference test
+shapes: tests/v1/test_pos_kernels.py:319-342 -- D in {64, 128}, theta 500000,
+neox both, bf16/fp32, T in {512, 1024, 4096})."""
+
+import pytest
+import torch
+
+from lmcache_ascend_b200 import ops
+from lmcache_ascend_b200.ops import reference as R
+
+
+def test_reference_delta_equals_reapply():
+    # rotating rope(old) by (new - old) == rope(new) of the raw key (fp32/fp64)
+    T, H, D = 64, 4, 64
+    cache = R.make_cos_sin_cache(4096, D, base=10000.0, dtype=torch.float64)
+    k = torch.randn(T, H * D, dtype=torch.float64)
+    old = torch.randint(0, 4000, (T,))
+    new = torch.randint(0, 4000, (T,))
+    for neox in (True, False):
+        at_old = R.rope_apply_ref(old, k, D, cache, neox).double()
+        moved = R.rope_delta_ref(old, new, at_old, D, cache, neox).double()
+        direct = R.rope_apply_ref(new, k, D, cache, neox).double()
+        assert torch.allclose(moved, direct, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("head_size", [64, 128])
+@pytest.mark.parametrize("neox", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T", [512, 1024, 4096])
+def test_fused_rope_gpu(head_size, neox, dtype, T):
+    H = 8
+    cache = R.make_cos_sin_cache(8192 + T, head_size, base=500000.0).cuda()
+    k = torch.randn(T, H * head_size, device="cuda").to(dtype)
+    old = torch.randint(0, 8192, (T,), device="cuda")
+    new = old + torch.randint(0, T, (T,), device="cuda")
+    ref = R.rope_delta_ref(old.cpu(), new.cpu(), k.cpu(), head_size, cache.cpu(), neox)
+    kk = k.clone()
+    ops.native().rotary_embedding_k_fused(old, new, kk, head_size, cache, neox)
+    torch.cuda.synchronize()
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert torch.allclose(kk.float().cpu(), ref, atol=tol * 4, rtol=tol)
