@@ -35,6 +35,10 @@ struct CopyJob {
   // Graph-capturable: when set, only the first min(*num_tokens_dev,
   // num_tokens) entries are processed (device-side count).
   const int32_t *num_tokens_dev;
+  // Paged -> paged (same-GPU push / block copy): when dst_slots is set the
+  // destination is dst_paged at dst_slots[t] instead of the chunk view.
+  PagedDesc dst_paged;
+  const void *dst_slots;
 };
 
 // Effective token count (reads the device-side count when present).
@@ -50,6 +54,18 @@ __device__ __forceinline__ int64_t load_idx(const CopyJob &j, int t) {
                        : static_cast<int64_t>(static_cast<const int32_t *>(j.chunk_idx)[t]);
 }
 
+// Select element p (0..2) of a 3-array with constant indices: runtime
+// indexing of kernel-parameter arrays would copy the whole struct to local
+// memory.
+template <typename T>
+__device__ __forceinline__ T sel3(const T (&a)[kMaxPlanes], int p) {
+  return p == 0 ? a[0] : (p == 1 ? a[1] : a[2]);
+}
+
+__device__ __forceinline__ PlaneDesc plane_of(const PagedDesc &pd, int p) {
+  return p == 0 ? pd.plane[0] : (p == 1 ? pd.plane[1] : pd.plane[2]);
+}
+
 __device__ __forceinline__ int64_t load_slot(const CopyJob &j, int t) {
   return j.slot_is_i64 ? static_cast<const int64_t *>(j.slots)[t]
                        : static_cast<int64_t>(static_cast<const int32_t *>(j.slots)[t]);
@@ -60,7 +76,8 @@ __device__ __forceinline__ char *paged_addr(const PagedDesc &pd, int layer,
   const int64_t blk = slot / pd.block_size;
   const int64_t off = slot - blk * pd.block_size;
   char *base = reinterpret_cast<char *>(pd.ptrs[layer * pd.num_planes + p]);
-  return base + blk * pd.plane[p].block_stride + off * pd.plane[p].slot_stride;
+  const PlaneDesc pl = plane_of(pd, p);
+  return base + blk * pl.block_stride + off * pl.slot_stride;
 }
 
 __device__ __forceinline__ char *chunk_addr(const ChunkView &cv, int layer,
@@ -77,8 +94,8 @@ __device__ __forceinline__ char *chunk_addr(const ChunkView &cv, int layer,
     tc = cv.ntok;
     base = cv.base;
   }
-  return base + p * cv.plane_stride_t[p] * tc + layer * cv.layer_stride_t * tc +
-         tl * cv.token_stride[p] + cv.col_off[p];
+  return base + p * sel3(cv.plane_stride_t, p) * tc + layer * cv.layer_stride_t * tc +
+         tl * sel3(cv.token_stride, p) + sel3(cv.col_off, p);
 }
 
 // Work decomposition: unit = (layer, plane, tile of tokens).  Tile size per
@@ -95,7 +112,7 @@ __device__ __forceinline__ UnitMap make_unit_map(const CopyJob &j,
   m.units_per_layer = 0;
   for (int p = 0; p < kMaxPlanes; ++p) {
     if (p < j.paged.num_planes) {
-      int tt = stage_bytes / j.paged.plane[p].row_bytes;
+      int tt = stage_bytes / plane_of(j.paged, p).row_bytes;
       tt = tt > 64 ? 64 : (tt < 1 ? 1 : tt);
       m.tile[p] = tt;
       m.ntiles[p] = (j.num_tokens + tt - 1) / tt;
@@ -121,13 +138,18 @@ __device__ __forceinline__ Unit decode_unit(const CopyJob &j, const UnitMap &m,
   r.layer = u / m.units_per_layer;
   int rem = u - r.layer * m.units_per_layer;
   int p = 0;
-  while (p < kMaxPlanes - 1 && rem >= m.ntiles[p]) {
-    rem -= m.ntiles[p];
+  if (rem >= m.ntiles[0]) {
+    rem -= m.ntiles[0];
     ++p;
+    if (rem >= m.ntiles[1]) {
+      rem -= m.ntiles[1];
+      ++p;
+    }
   }
   r.plane = p;
-  r.t0 = rem * m.tile[p];
-  r.n = min(m.tile[p], j.num_tokens - r.t0);
+  const int tile = sel3(m.tile, p);
+  r.t0 = rem * tile;
+  r.n = min(tile, j.num_tokens - r.t0);
   return r;
 }
 
@@ -142,7 +164,7 @@ struct LaneRuns {
 __device__ __forceinline__ LaneRuns plan_runs(const CopyJob &j, const Unit &u,
                                               int lane, int total_tokens) {
   LaneRuns r;
-  const int rb = j.paged.plane[u.plane].row_bytes;
+  const int rb = plane_of(j.paged, u.plane).row_bytes;
   bool valid[2];
   for (int h = 0; h < 2; ++h) {
     const int i = h * 32 + lane;
@@ -155,9 +177,21 @@ __device__ __forceinline__ LaneRuns plan_runs(const CopyJob &j, const Unit &u,
         if (slot >= j.paged.num_slots) {
           report_status(j.status, kStatusBadSlot, t, slot, j.paged.num_slots);
         } else {
-          const int64_t ct = load_idx(j, t);
-          if (ct < 0 || (j.chunk_idx != nullptr && ct >= j.chunk_idx_limit)) {
-            report_status(j.status, kStatusBadIndex, t, ct, j.chunk_idx_limit);
+          const int64_t ct = j.dst_slots != nullptr
+                                 ? (j.slot_is_i64 ? static_cast<const int64_t *>(j.dst_slots)[t]
+                                                  : static_cast<const int32_t *>(j.dst_slots)[t])
+                                 : load_idx(j, t);
+          const int64_t limit = j.dst_slots != nullptr ? j.dst_paged.num_slots
+                                                       : j.chunk_idx_limit;
+          if (ct < 0 && j.dst_slots != nullptr) {
+            // destination slot -1: skip the token
+          } else if (ct < 0 || ((j.chunk_idx != nullptr || j.dst_slots != nullptr) &&
+                                ct >= limit)) {
+            report_status(j.status, kStatusBadIndex, t, ct, limit);
+          } else if (j.dst_slots != nullptr) {
+            r.src[h] = paged_addr(j.paged, j.layer_begin + u.layer, u.plane, slot);
+            r.dst[h] = paged_addr(j.dst_paged, j.chunk_layer_begin + u.layer, u.plane, ct);
+            valid[h] = true;
           } else {
             char *pa = paged_addr(j.paged, j.layer_begin + u.layer, u.plane, slot);
             char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + u.layer, u.plane,

@@ -25,26 +25,34 @@ namespace lmc {
 // ---------------------------------------------------------------------------
 // TMA engine: one warp per CTA, ring of `stages` shared-memory buffers.
 // ---------------------------------------------------------------------------
+constexpr int kTmaBarBytes = 1024;  // mbarrier area at the start of smem
+
 __device__ __forceinline__ unsigned warp_sum(unsigned v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
-__global__ void __launch_bounds__(32)
+// Each warp of the CTA is an independent pipeline with its own ring of
+// `stages` buffers and mbarriers, so instruction latency of one warp's
+// address planning overlaps the others' copies.
+__global__ void __launch_bounds__(256)
     tma_rows_kernel(CopyJob j, int stage_bytes, int stages,
                     unsigned long long budget_ns) {
   extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-  unsigned char *ring = smem + 128;
-  const int lane = threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * stages;
+  unsigned char *ring = smem + kTmaBarBytes + static_cast<size_t>(warp) * stages * stage_bytes;
 
   j.num_tokens = effective_tokens(j);
   const UnitMap m = make_unit_map(j, stage_bytes);
   const int total_units = m.units_per_layer * j.num_layers;
-  if (static_cast<int>(blockIdx.x) >= total_units) return;
-  const int n_iter =
-      (total_units - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
+  const int gw = blockIdx.x * nwarps + warp;
+  const int nw = gridDim.x * nwarps;
+  if (gw >= total_units) return;
+  const int n_iter = (total_units - gw + nw - 1) / nw;
 
   if (lane == 0) {
     for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
@@ -53,10 +61,10 @@ __global__ void __launch_bounds__(32)
   __syncwarp();
 
   auto issue_loads = [&](int k) {
-    const Unit u = decode_unit(j, m, blockIdx.x + k * gridDim.x);
+    const Unit u = decode_unit(j, m, gw + k * nw);
     const int s = k % stages;
     const LaneRuns r = plan_runs(j, u, lane, j.num_tokens);
-    const unsigned rb = j.paged.plane[u.plane].row_bytes;
+    const unsigned rb = plane_of(j.paged, u.plane).row_bytes;
     const unsigned total = warp_sum((r.len[0] + r.len[1]) * rb);
     if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
     __syncwarp();
@@ -68,10 +76,10 @@ __global__ void __launch_bounds__(32)
   };
 
   auto issue_stores = [&](int k) {
-    const Unit u = decode_unit(j, m, blockIdx.x + k * gridDim.x);
+    const Unit u = decode_unit(j, m, gw + k * nw);
     const int s = k % stages;
     const LaneRuns r = plan_runs(j, u, lane, j.num_tokens);
-    const unsigned rb = j.paged.plane[u.plane].row_bytes;
+    const unsigned rb = plane_of(j.paged, u.plane).row_bytes;
     unsigned char *buf = ring + static_cast<size_t>(s) * stage_bytes;
 #pragma unroll
     for (int h = 0; h < 2; ++h)
@@ -86,7 +94,7 @@ __global__ void __launch_bounds__(32)
     const unsigned parity = (k / stages) & 1;
     if (!mbar_wait_bounded(&bars[s], parity, budget_ns)) {
       if (lane == 0)
-        report_status(j.status, kStatusMbarTimeout, blockIdx.x, k, n_iter);
+        report_status(j.status, kStatusMbarTimeout, gw, k, n_iter);
       break;
     }
     issue_stores(k);
@@ -153,6 +161,19 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
         report_status(j.status, kStatusBadSlot, t, slot, j.paged.num_slots);
       continue;
     }
+    if (j.dst_slots != nullptr) {
+      const int64_t ds = j.slot_is_i64 ? static_cast<const int64_t *>(j.dst_slots)[t]
+                                       : static_cast<const int32_t *>(j.dst_slots)[t];
+      if (ds < 0) continue;
+      if (ds >= j.dst_paged.num_slots) {
+        if (lane == 0) report_status(j.status, kStatusBadIndex, t, ds, j.dst_paged.num_slots);
+        continue;
+      }
+      warp_copy_row(paged_addr(j.dst_paged, j.chunk_layer_begin + l, p, ds),
+                    paged_addr(j.paged, j.layer_begin + l, p, slot),
+                    plane_of(j.paged, p).row_bytes, lane);
+      continue;
+    }
     const int64_t ct = load_idx(j, t);
     if (ct < 0 || (j.chunk_idx != nullptr && ct >= j.chunk_idx_limit)) {
       if (lane == 0)
@@ -161,7 +182,7 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
     }
     char *pa = paged_addr(j.paged, j.layer_begin + l, p, slot);
     char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + l, p, ct, j.num_tokens);
-    const int rb = j.paged.plane[p].row_bytes;
+    const int rb = plane_of(j.paged, p).row_bytes;
     if (j.to_chunk)
       warp_copy_row(ca, pa, rb, lane);
     else
@@ -250,13 +271,15 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
   bool use_tma = (mode == 1) || (mode == 0 && chunk_on_device && aligned);
   if (mode == 1) TORCH_CHECK(aligned, "TMA mode needs 16-byte aligned rows");
   if (use_tma) {
-    const int stage_bytes = env_int("LMC_TMA_STAGE_BYTES", 16384);
-    const int stages = env_int("LMC_TMA_STAGES", 6);
+    const int stage_bytes = env_int("LMC_TMA_STAGE_BYTES", 8192);
+    const int stages = std::max(2, env_int("LMC_TMA_STAGES", 2));
+    const int warps = std::min(8, std::max(1, env_int("LMC_TMA_WARPS", 2)));
     int max_rb = 0;
     for (int p = 0; p < j.paged.num_planes; ++p)
       max_rb = std::max(max_rb, static_cast<int>(j.paged.plane[p].row_bytes));
     const int sb = std::max(stage_bytes, max_rb);
-    const size_t smem = 128 + static_cast<size_t>(sb) * stages;
+    TORCH_CHECK(warps * stages * 8 <= kTmaBarBytes, "too many TMA stages");
+    const size_t smem = kTmaBarBytes + static_cast<size_t>(sb) * stages * warps;
     TORCH_CHECK(smem <= 227 * 1024, "TMA ring too large: ", smem);
     static bool attr_set[64] = {false};
     if (!attr_set[device & 63]) {
@@ -265,7 +288,6 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
                            227 * 1024);
       attr_set[device & 63] = true;
     }
-    // units: recompute on host to size the grid
     long long units = 0;
     for (int p = 0; p < j.paged.num_planes; ++p) {
       int tt = sb / j.paged.plane[p].row_bytes;
@@ -275,9 +297,10 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
     units *= j.num_layers;
     const int per_sm = std::max(1, static_cast<int>((228 * 1024) / (smem + 1024)));
     const int grid_cap = env_int("LMC_TMA_GRID", num_sms(device) * per_sm);
-    const int grid = static_cast<int>(std::min<long long>(units, grid_cap));
+    const long long ctas = (units + warps - 1) / warps;
+    const int grid = static_cast<int>(std::max(1LL, std::min<long long>(ctas, grid_cap)));
     const unsigned long long budget_ns = 2000000000ull;  // 2 s
-    tma_rows_kernel<<<grid, 32, smem, stream>>>(j, sb, stages, budget_ns);
+    tma_rows_kernel<<<grid, 32 * warps, smem, stream>>>(j, sb, stages, budget_ns);
   } else {
     const long long rows = static_cast<long long>(j.num_layers) *
                            j.paged.num_planes * j.num_tokens;
@@ -362,6 +385,60 @@ void kv_transfer(const PagedLayout &paged, const c10::optional<at::Tensor> &chun
   launch_copy(j, chunk_on_device, aligned, mode,
               at::cuda::getCurrentCUDAStream(slots.device().index()).stream(),
               slots.device().index());
+}
+
+// Adds `inc` to flags[layer_begin .. layer_begin + n) with release semantics
+// (stream-ordered after the copy kernel that precedes it).
+__global__ void bump_flags_kernel(unsigned *flags, int layer_begin, int n, unsigned inc) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    fence_acq_rel_sys();
+    red_release_sys_add(flags + layer_begin + i, inc);
+  }
+}
+
+// Paged -> paged copy on this GPU (same-device PD push, block copies):
+//   dst[l'][p][dst_slots[t]] = src[l][p][src_slots[t]]
+// optionally followed by a per-layer flag release (`flags_ptr`, `flag_inc`).
+void paged_copy(const PagedLayout &src, const PagedLayout &dst, const at::Tensor &src_slots,
+                const at::Tensor &dst_slots, int64_t layer_begin, int64_t dst_layer_begin,
+                int64_t num_layers, int64_t mode, const c10::optional<at::Tensor> &status,
+                int64_t flags_ptr, int64_t flag_inc) {
+  TORCH_CHECK(src_slots.is_cuda() && dst_slots.is_cuda(), "slot mappings must be on the device");
+  TORCH_CHECK(src_slots.scalar_type() == dst_slots.scalar_type() &&
+                  src_slots.numel() == dst_slots.numel(),
+              "src/dst slot mappings must match in dtype and length");
+  TORCH_CHECK(src_slots.is_contiguous() && dst_slots.is_contiguous(), "contiguous slots");
+  TORCH_CHECK(src.desc().num_planes == dst.desc().num_planes, "plane count mismatch");
+  for (int p = 0; p < src.desc().num_planes; ++p)
+    TORCH_CHECK(src.desc().plane[p].row_bytes == dst.desc().plane[p].row_bytes,
+                "row size mismatch on plane ", p);
+  TORCH_CHECK(layer_begin >= 0 && layer_begin + num_layers <= src.desc().num_layers &&
+                  dst_layer_begin >= 0 && dst_layer_begin + num_layers <= dst.desc().num_layers,
+              "layer range out of the caches");
+  const c10::cuda::CUDAGuard guard(src_slots.device());
+  CopyJob j;
+  std::memset(&j, 0, sizeof(j));
+  j.paged = src.desc();
+  j.dst_paged = dst.desc();
+  j.slots = src_slots.data_ptr();
+  j.dst_slots = dst_slots.data_ptr();
+  j.slot_is_i64 = src_slots.scalar_type() == at::kLong;
+  j.num_tokens = static_cast<int32_t>(src_slots.numel());
+  j.layer_begin = static_cast<int32_t>(layer_begin);
+  j.chunk_layer_begin = static_cast<int32_t>(dst_layer_begin);
+  j.num_layers = static_cast<int32_t>(num_layers);
+  j.to_chunk = 1;
+  j.status = status_ptr(status);
+  const int dev = src_slots.device().index();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev).stream();
+  launch_copy(j, true, src.aligned() && dst.aligned(), mode, stream, dev);
+  if (flags_ptr != 0 && num_layers > 0) {
+    bump_flags_kernel<<<(static_cast<int>(num_layers) + 127) / 128, 128, 0, stream>>>(
+        reinterpret_cast<unsigned *>(flags_ptr), static_cast<int>(dst_layer_begin),
+        static_cast<int>(num_layers), static_cast<unsigned>(flag_inc));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
 }  // namespace lmc

@@ -63,4 +63,9 @@ void kv_transfer(const PagedLayout &paged, const c10::optional<at::Tensor> &chun
                  int64_t chunk_idx_limit,
                  const c10::optional<at::Tensor> &num_tokens_dev);
 
+void paged_copy(const PagedLayout &src, const PagedLayout &dst, const at::Tensor &src_slots,
+                const at::Tensor &dst_slots, int64_t layer_begin, int64_t dst_layer_begin,
+                int64_t num_layers, int64_t mode, const c10::optional<at::Tensor> &status,
+                int64_t flags_ptr, int64_t flag_inc);
+
 }  // namespace lmc

@@ -35,7 +35,7 @@
 namespace lmc {
 
 constexpr int kMaxReplicas = 4;
-constexpr int kPushWarps = 8;
+constexpr int kPushWarps = 4;
 
 struct PushJob {
   PagedDesc src;
@@ -57,84 +57,100 @@ __device__ __forceinline__ int64_t push_slot(const void *p, int is64, int t) {
               : static_cast<int64_t>(static_cast<const int32_t *>(p)[t]);
 }
 
-__device__ __forceinline__ char *dst_addr(const PagedDesc &pd, int rep,
-                                          int layer, int p, int64_t slot) {
-  const int64_t blk = slot / pd.block_size;
-  const int64_t off = slot - blk * pd.block_size;
-  char *base = reinterpret_cast<char *>(
-      pd.ptrs[(static_cast<int64_t>(rep) * pd.num_layers + layer) * pd.num_planes + p]);
-  return base + blk * pd.plane[p].block_stride + off * pd.plane[p].slot_stride;
+// One CTA (kPushWarps warps) per unit = (layer, plane, tile of tokens).
+// The CTA streams the unit's rows as a flat array of 16-byte vectors: each
+// thread resolves the rows of its vectors directly (slot loads are warp
+// broadcasts; 32-bit slot arithmetic), keeps kVecPerThread independent loads
+// in flight and then stores them to every replica.  One barrier + one
+// system-scope release per unit publishes the unit to the decoder.  Small
+// CTAs keep several units per SM in flight so one CTA's release latency is
+// hidden behind the others' copies.
+constexpr int kMaxTile = 1024;
+constexpr int kVecPerThread = 8;
+
+__device__ __forceinline__ unsigned row_off(const PagedDesc &pd, const PlaneDesc &pl,
+                                            unsigned slot) {
+  const unsigned bs = static_cast<unsigned>(pd.block_size);
+  const unsigned b = slot / bs;
+  return static_cast<unsigned>(static_cast<int64_t>(b) * pl.block_stride +
+                               static_cast<int64_t>(slot - b * bs) * pl.slot_stride);
 }
 
-// One CTA (8 warps) per unit = (layer, plane, tile).  Each warp moves tokens
-// t0 + w, t0 + w + 8, ...; four tokens are in flight per warp when the row is
-// 512 B (Qwen3-32B TP4 shard: 2 heads x 128 x bf16).
 __global__ void __launch_bounds__(kPushWarps * 32)
     pd_push_kernel(PushJob j) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
   const int np = j.src.num_planes;
   const int tiles = (j.num_tokens + j.tile_tokens - 1) / j.tile_tokens;
   const int units_per_layer = np * tiles;
   const int total = units_per_layer * j.num_layers;
+  const int tid = threadIdx.x;
+  constexpr int kThreads = kPushWarps * 32;
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
     const int li = u / units_per_layer;
     const int rem = u - li * units_per_layer;
     const int p = rem / tiles;
     const int tile = rem - p * tiles;
     const int layer = j.layer_begin + li;
-    const int rb = j.src.plane[p].row_bytes;
+    const PlaneDesc spl = j.src.plane[p];
+    const PlaneDesc dpl = j.dst.plane[p];
+    const int rb = spl.row_bytes;
     const int t0 = tile * j.tile_tokens;
-    const int t1 = min(j.num_tokens, t0 + j.tile_tokens);
-    const bool v16 = (rb & 15) == 0;
-    for (int tb = t0 + warp * 4; tb < t1; tb += kPushWarps * 4) {
-      // gather addresses for up to 4 tokens
-      const char *s[4];
-      int64_t ds[4];
+    const int n = min(j.num_tokens - t0, j.tile_tokens);
+    const char *sbase = reinterpret_cast<const char *>(j.src.ptrs[layer * np + p]);
+    if ((rb & 15) == 0) {
+      const int vpr = rb >> 4;  // vectors per row
+      const int nv = n * vpr;
+      for (int base = 0; base < nv; base += kThreads * kVecPerThread) {
+        int4 v[kVecPerThread];
+        unsigned so[kVecPerThread], dp[kVecPerThread];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int t = tb + q;
-        s[q] = nullptr;
-        ds[q] = -1;
-        if (t < t1) {
-          const int64_t ss = push_slot(j.src_slots, j.slot_is_i64, t);
-          const int64_t dd = push_slot(j.dst_slots, j.slot_is_i64, t);
-          if (ss >= 0 && dd >= 0) {
-            if (ss >= j.src.num_slots || dd >= j.dst.num_slots) {
-              if (lane == 0)
-                report_status(j.status, kStatusBadSlot, t, ss, dd);
-            } else {
-              s[q] = paged_addr(j.src, layer, p, ss);
-              ds[q] = dd;
+        for (int k = 0; k < kVecPerThread; ++k) {
+          const int g = base + k * kThreads + tid;
+          so[k] = ~0u;
+          if (g < nv) {
+            const int ti = g / vpr;
+            const unsigned vb = static_cast<unsigned>(g - ti * vpr) * 16u;
+            const int64_t ss = push_slot(j.src_slots, j.slot_is_i64, t0 + ti);
+            const int64_t dd = push_slot(j.dst_slots, j.slot_is_i64, t0 + ti);
+            if (ss >= 0 && dd >= 0) {
+              if (ss >= j.src.num_slots || dd >= j.dst.num_slots) {
+                if (vb == 0) report_status(j.status, kStatusBadSlot, t0 + ti, ss, dd);
+              } else {
+                so[k] = row_off(j.src, spl, static_cast<unsigned>(ss)) + vb;
+                dp[k] = row_off(j.dst, dpl, static_cast<unsigned>(dd)) + vb;
+              }
             }
           }
         }
-      }
-      if (v16) {
-        for (int off = lane * 16; off < rb; off += 512) {
-          int4 v[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (s[q]) v[q] = ld_nc_v4(s[q] + off);
-          for (int r = 0; r < j.replicas; ++r) {
+        for (int k = 0; k < kVecPerThread; ++k)
+          if (so[k] != ~0u) v[k] = ld_nc_v4(sbase + so[k]);
+        for (int r = 0; r < j.replicas; ++r) {
+          char *db = reinterpret_cast<char *>(
+              j.dst.ptrs[(static_cast<int64_t>(r) * j.dst.num_layers + layer) * np + p]);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (s[q]) st_cs_v4(dst_addr(j.dst, r, layer, p, ds[q]) + off, v[q]);
-          }
+          for (int k = 0; k < kVecPerThread; ++k)
+            if (so[k] != ~0u) st_cs_v4(db + dp[k], v[k]);
         }
-      } else {
-        for (int q = 0; q < 4; ++q) {
-          if (!s[q]) continue;
-          for (int r = 0; r < j.replicas; ++r) {
-            char *d = dst_addr(j.dst, r, layer, p, ds[q]);
-            for (int off = lane; off < rb; off += 32) d[off] = s[q][off];
-          }
+      }
+    } else {
+      for (int g = tid; g < n * rb; g += kThreads) {
+        const int ti = g / rb;
+        const int bi = g - ti * rb;
+        const int64_t ss = push_slot(j.src_slots, j.slot_is_i64, t0 + ti);
+        const int64_t dd = push_slot(j.dst_slots, j.slot_is_i64, t0 + ti);
+        if (ss < 0 || dd < 0 || ss >= j.src.num_slots || dd >= j.dst.num_slots) continue;
+        const unsigned so = row_off(j.src, spl, static_cast<unsigned>(ss));
+        const unsigned dof = row_off(j.dst, dpl, static_cast<unsigned>(dd));
+        for (int r = 0; r < j.replicas; ++r) {
+          char *db = reinterpret_cast<char *>(
+              j.dst.ptrs[(static_cast<int64_t>(r) * j.dst.num_layers + layer) * np + p]);
+          db[dof + bi] = sbase[so + bi];
         }
       }
     }
-    // publish this unit: all warps' stores are ordered before the release
+    // publish this unit: every thread's stores are ordered before the release
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       fence_acq_rel_sys();
       for (int r = 0; r < j.replicas; ++r)
         if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
@@ -207,6 +223,16 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
   j.layer_begin = static_cast<int32_t>(layer_begin);
   j.num_layers = static_cast<int32_t>(num_layers);
   j.tile_tokens = static_cast<int32_t>(tile_tokens > 0 ? tile_tokens : 128);
+  TORCH_CHECK(j.tile_tokens <= kMaxTile, "tile_tokens must be <= ", kMaxTile);
+  for (int p = 0; p < src.desc().num_planes; ++p) {
+    const auto &sp = src.desc().plane[p];
+    const auto &dp = dst.desc().plane[p];
+    const int64_t sblk = (src.desc().num_slots + src.desc().block_size - 1) / src.desc().block_size;
+    const int64_t dblk = (dst.desc().num_slots + dst.desc().block_size - 1) / dst.desc().block_size;
+    TORCH_CHECK(sblk * sp.block_stride < (1LL << 32) - 1 &&
+                    dblk * dp.block_stride < (1LL << 32) - 1,
+                "pd_push: each layer plane must span less than 4 GiB");
+  }
   j.replicas = static_cast<int32_t>(replicas);
   for (size_t r = 0; r < flag_ptrs.size(); ++r)
     j.flags[r] = reinterpret_cast<unsigned *>(flag_ptrs[r]);
@@ -220,7 +246,7 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
       push_units_per_layer(j.num_tokens, j.src.num_planes, j.tile_tokens) *
       static_cast<long long>(num_layers);
   int g = grid > 0 ? static_cast<int>(grid)
-                   : env_int2("LMC_PUSH_GRID", num_sms(dev) * 2);
+                   : env_int2("LMC_PUSH_GRID", num_sms(dev) * 16);
   g = static_cast<int>(std::max(1LL, std::min<long long>(units, g)));
   pd_push_kernel<<<g, kPushWarps * 32, 0,
                    at::cuda::getCurrentCUDAStream(dev).stream()>>>(j);

@@ -89,6 +89,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("chunk_idx_limit") = 0, py::arg("num_tokens_dev") = py::none(),
         "paged <-> chunk transfer (TMA bulk or SIMT engine)");
   m.def("num_sms", &num_sms);
+  m.def("paged_copy", &paged_copy, py::arg("src"), py::arg("dst"), py::arg("src_slots"),
+        py::arg("dst_slots"), py::arg("layer_begin"), py::arg("dst_layer_begin"),
+        py::arg("num_layers"), py::arg("mode") = 0, py::arg("status") = py::none(),
+        py::arg("flags_ptr") = 0, py::arg("flag_inc") = 0,
+        "paged -> paged copy on one GPU (TMA bulk or SIMT), optional flag release");
 
   m.def("alloc_pinned_ptr", &alloc_pinned_ptr, py::arg("size"), py::arg("device") = -1);
   m.def("free_pinned_ptr", &free_pinned_ptr);

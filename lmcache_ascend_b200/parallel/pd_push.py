@@ -96,7 +96,15 @@ class PushReceiver:
 
 
 class PushSender:
-    def __init__(self, layout: PagedKVLayout):
+    """``engine``: "auto" uses the TMA paged->paged copy (plus a flag release)
+    when the single receiver is this process on the same GPU, and the NVLink
+    push kernel otherwise; "push" always uses the push kernel."""
+
+    def __init__(self, layout: PagedKVLayout, engine: str = "auto"):
+        if engine not in ("auto", "push"):
+            raise ValueError("engine must be 'auto' or 'push'")
+        self.engine = engine
+        self._local = False
         self.layout = layout
         self.device = layout.device
         self.peers = PeerMappings(self.device.index or 0)
@@ -125,6 +133,11 @@ class PushSender:
         self._dst.set_bases_aligned(all(p % 16 == 0 for p in ptrs))
         self._flag_ptrs = [self.peers.resolve(IpcDesc.from_dict(r.flags)) for r in receivers]
         self.replicas = len(receivers)
+        import os
+
+        self._local = (self.engine == "auto" and len(receivers) == 1
+                       and IpcDesc.from_dict(r0.flags).pid == os.getpid()
+                       and r0.device == (self.device.index or 0))
 
     def push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, layer_begin: int = 0,
              num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0) -> None:
@@ -132,6 +145,13 @@ class PushSender:
         if self._dst is None:
             raise RuntimeError("PushSender.connect() first")
         nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
+        if self._local:
+            units = ops.native().push_units_per_layer(src_slots.numel(), self.layout.num_planes,
+                                                      tile_tokens)
+            ops.native().paged_copy(self.layout.native(), self._dst, src_slots, dst_slots,
+                                    layer_begin, layer_begin, nl, 0, self.status.tensor,
+                                    self._flag_ptrs[0], units)
+            return
         ops.native().pd_push(self.layout.native(), self._dst, src_slots, dst_slots,
                              layer_begin, nl, self.replicas, self._flag_ptrs, tile_tokens,
                              grid, self.status.tensor)

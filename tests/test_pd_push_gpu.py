@@ -29,7 +29,8 @@ def _rows(kv, slots):
 
 @pytest.mark.parametrize("pattern", ["blocks", "random"])
 @pytest.mark.parametrize("tile", [32, 128])
-def test_loopback_push_exact(pattern, tile):
+@pytest.mark.parametrize("engine", ["auto", "push"])
+def test_loopback_push_exact(pattern, tile, engine):
     L, NB, BS = 6, 32, 128
     src = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=1)
     dst = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=2)
@@ -41,7 +42,7 @@ def test_loopback_push_exact(pattern, tile):
         ss = random_slots(T, NB * BS, seed=5, device=DEV, dtype=torch.int32)
         ds = random_slots(T, NB * BS, seed=6, device=DEV, dtype=torch.int32)
     recv = PushReceiver(PagedKVLayout(dst))
-    send = PushSender(PagedKVLayout(src))
+    send = PushSender(PagedKVLayout(src), engine=engine)
     send.connect([recv.desc])
     tg = recv.expect(T, tile_tokens=tile)
     send.push(ss, ds, tile_tokens=tile)
@@ -64,7 +65,7 @@ def test_layerwise_push_and_partial_wait():
     ss = block_slots(T, BS, NB, seed=9, device=DEV, dtype=torch.int32)
     ds = block_slots(T, BS, NB, seed=10, device=DEV, dtype=torch.int32)
     recv = PushReceiver(PagedKVLayout(dst))
-    send = PushSender(PagedKVLayout(src))
+    send = PushSender(PagedKVLayout(src), engine="push")
     send.connect([recv.desc])
     for layer in range(L):
         tg = recv.expect(T, layer_begin=layer, num_layers=1)
