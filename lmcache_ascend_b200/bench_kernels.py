@@ -177,13 +177,15 @@ def bench_push(small: bool):
     t = torch.arange(T)
     ss = (torch.randperm(nb, generator=g)[: T // BS][t // BS] * BS + t % BS).int().cuda()
     ds = (torch.randperm(nb, generator=g)[: T // BS][t // BS] * BS + t % BS).int().cuda()
-    recv = PushReceiver(PagedKVLayout(dst))
-    send = PushSender(PagedKVLayout(src))
-    send.connect([recv.desc])
-    ms = _time(lambda: send.push(ss, ds))
     moved = T * L * 2 * H * D * 2
-    _emit("push_loopback", ms, moved, tokens=T, layers=L)
-    send.check()
+    for engine in ("auto", "push"):
+        recv = PushReceiver(PagedKVLayout(dst))
+        send = PushSender(PagedKVLayout(src), engine=engine)
+        send.connect([recv.desc])
+        ms = _time(lambda: send.push(ss, ds))
+        _emit("push_loopback_" + ("tma_copy" if engine == "auto" else "push_kernel"), ms,
+              moved, tokens=T, layers=L)
+        send.check()
 
 
 CASES = {"gather": bench_gather_scatter, "offload": bench_offload, "cachegen": bench_cachegen,

@@ -204,9 +204,11 @@ int num_sms(int device) {
   return cached[device];
 }
 
+// Positive integer from the environment, else `dflt` (0 or unset = default).
 static int env_int(const char *name, int dflt) {
   const char *v = std::getenv(name);
-  return v ? std::atoi(v) : dflt;
+  const int x = v ? std::atoi(v) : 0;
+  return x > 0 ? x : dflt;
 }
 
 PagedLayout::PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
@@ -438,6 +440,41 @@ void paged_copy(const PagedLayout &src, const PagedLayout &dst, const at::Tensor
         reinterpret_cast<unsigned *>(flags_ptr), static_cast<int>(dst_layer_begin),
         static_cast<int>(num_layers), static_cast<unsigned>(flag_inc));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+// N2 `fused_multi_layer_kv_transfer` (reference csrc/mem_kernels.cpp:113-213):
+// all layers between the paged cache and ONE pinned host chunk through a
+// caller-provided device staging buffer, on the current stream.
+//   from_gpu: TMA gather paged -> staging, then D2H copy staging -> host
+//   to_gpu:   H2D copy host -> staging, then TMA scatter staging -> paged
+void fused_multi_layer_kv_transfer(at::Tensor &host_chunk, at::Tensor &staging,
+                                   const PagedLayout &paged, const ChunkLayout &layout,
+                                   const at::Tensor &slots, bool from_gpu, int64_t mode,
+                                   const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(!host_chunk.is_cuda() && host_chunk.is_contiguous(),
+              "host_chunk must be a contiguous host tensor");
+  TORCH_CHECK(host_chunk.dim() == 4, "host_chunk must be a 4-D chunk [P, L, T, E]");
+  TORCH_CHECK(staging.is_cuda() && staging.is_contiguous(), "staging must be on the device");
+  const size_t nbytes = host_chunk.nbytes();
+  TORCH_CHECK(staging.nbytes() >= nbytes, "staging buffer too small: need ", nbytes,
+              " bytes, got ", staging.nbytes());
+  TORCH_CHECK(slots.numel() <= host_chunk.size(2), "more slots than chunk tokens");
+  const c10::cuda::CUDAGuard guard(slots.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(slots.device().index()).stream();
+  auto stage = at::from_blob(staging.data_ptr(), host_chunk.sizes(),
+                             host_chunk.options().device(staging.device()));
+  if (!from_gpu) {
+    cudaError_t e = cudaMemcpyAsync(staging.data_ptr(), host_chunk.data_ptr(), nbytes,
+                                    cudaMemcpyHostToDevice, stream);
+    TORCH_CHECK(e == cudaSuccess, "H2D copy failed: ", cudaGetErrorString(e));
+  }
+  kv_transfer(paged, stage, c10::nullopt, layout, host_chunk.size(2), 0, 0, true, slots, 0, 0,
+              paged.desc().num_layers, from_gpu, mode, status, c10::nullopt, 0, c10::nullopt);
+  if (from_gpu) {
+    cudaError_t e = cudaMemcpyAsync(host_chunk.data_ptr(), staging.data_ptr(), nbytes,
+                                    cudaMemcpyDeviceToHost, stream);
+    TORCH_CHECK(e == cudaSuccess, "D2H copy failed: ", cudaGetErrorString(e));
   }
 }
 

@@ -68,4 +68,9 @@ void paged_copy(const PagedLayout &src, const PagedLayout &dst, const at::Tensor
                 int64_t num_layers, int64_t mode, const c10::optional<at::Tensor> &status,
                 int64_t flags_ptr, int64_t flag_inc);
 
+void fused_multi_layer_kv_transfer(at::Tensor &host_chunk, at::Tensor &staging,
+                                   const PagedLayout &paged, const ChunkLayout &layout,
+                                   const at::Tensor &slots, bool from_gpu, int64_t mode,
+                                   const c10::optional<at::Tensor> &status);
+
 }  // namespace lmc

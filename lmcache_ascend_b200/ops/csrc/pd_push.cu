@@ -172,9 +172,11 @@ __global__ void pd_wait_flags_kernel(const unsigned *flags,
     report_status(status, kStatusFlagTimeout, layer_begin + i, seen, targets[i]);
 }
 
+// Positive integer from the environment, else `dflt` (0 or unset = default).
 static int env_int2(const char *name, int dflt) {
   const char *v = std::getenv(name);
-  return v ? std::atoi(v) : dflt;
+  const int x = v ? std::atoi(v) : 0;
+  return x > 0 ? x : dflt;
 }
 
 int64_t push_units_per_layer(int64_t num_tokens, int64_t num_planes,

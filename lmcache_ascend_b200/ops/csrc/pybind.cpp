@@ -89,6 +89,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("chunk_idx_limit") = 0, py::arg("num_tokens_dev") = py::none(),
         "paged <-> chunk transfer (TMA bulk or SIMT engine)");
   m.def("num_sms", &num_sms);
+  m.def("fused_multi_layer_kv_transfer", &fused_multi_layer_kv_transfer,
+        py::arg("host_chunk"), py::arg("staging"), py::arg("paged"), py::arg("layout"),
+        py::arg("slots"), py::arg("from_gpu"), py::arg("mode") = 0,
+        py::arg("status") = py::none(),
+        "paged <-> pinned host chunk through a device staging buffer");
   m.def("paged_copy", &paged_copy, py::arg("src"), py::arg("dst"), py::arg("src_slots"),
         py::arg("dst_slots"), py::arg("layer_begin"), py::arg("dst_layer_begin"),
         py::arg("num_layers"), py::arg("mode") = 0, py::arg("status") = py::none(),

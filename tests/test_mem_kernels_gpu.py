@@ -159,3 +159,29 @@ def test_bad_slot_reported_and_skipped():
     torch.cuda.synchronize()
     r = st.read()
     assert r["name"] == "bad_slot" and r["a"] == lay.num_slots + 10
+
+
+@pytest.mark.parametrize("fmt", ["separate", "mla"])
+def test_fused_staged_host_transfer(fmt):
+    """from_gpu: gather -> staging -> D2H; to_gpu: H2D -> staging -> scatter."""
+    kv, mla = _kv(fmt)
+    lay = PagedKVLayout(kv, use_mla=mla)
+    T = 256
+    slots = block_slots(T, lay.block_size, lay.num_blocks, seed=8, device=DEV)
+    host = torch.zeros(lay.chunk_shape(T), dtype=lay.dtype).pin_memory()
+    staging = torch.empty(lay.chunk_bytes(T) + 4096, dtype=torch.uint8, device=DEV)
+    ops.native().fused_multi_layer_kv_transfer(host, staging, lay.native(), lay.chunk_native(),
+                                               slots, True)
+    torch.cuda.synchronize()
+    ref = torch.zeros(lay.chunk_shape(T), dtype=lay.dtype, device=DEV)
+    lay.gather_ref(ref, slots)
+    assert torch.equal(host, ref.cpu())
+    kv2 = [tuple(torch.zeros_like(t) for t in l) if isinstance(l, tuple) else torch.zeros_like(l)
+           for l in kv]
+    lay2 = PagedKVLayout(kv2, use_mla=mla)
+    ops.native().fused_multi_layer_kv_transfer(host, staging, lay2.native(), lay2.chunk_native(),
+                                               slots, False)
+    torch.cuda.synchronize()
+    back = torch.zeros_like(ref)
+    lay2.gather_ref(back, slots)
+    assert torch.equal(back, ref)
