@@ -206,6 +206,43 @@ class LMCacheEngine:
         self.stats.inc("stored_tokens", n)
         return n
 
+    # ---------------------------------------------- direct prefill push
+    def _pd_backend(self):
+        pd = self.storage_manager.backends.get("PDBackend")
+        if pd is None:
+            raise RuntimeError("direct prefill push needs enable_pd")
+        return pd
+
+    @nvtx_range("lmc.store_direct_prefill")
+    def store_direct_prefill(self, tokens: Optional[torch.Tensor] = None, *,
+                             slot_mapping: torch.Tensor, dst_slot_mapping: torch.Tensor,
+                             req_id: str, layer_begin: int = 0,
+                             num_layers: Optional[int] = None) -> int:
+        """Prefiller: push this request's KV rows from the local paged cache
+        straight into the decoder's paged blocks (``dst_slot_mapping``, the
+        decoder's block allocation) with the fused NVLink kernel.  Layerwise
+        callers pass ``layer_begin``/``num_layers`` after each layer's KV is
+        written.  Returns the number of tokens pushed (reference
+        cache_engine.py:2634 ``store_direct_prefill``)."""
+        if not self.is_healthy() or self._passive():
+            return 0
+        pd = self._pd_backend()
+        n = int(slot_mapping.numel())
+        dev = pd.push_sender.device if pd.push_sender is not None else None
+        src = slot_mapping.to(dev, non_blocking=True) if dev is not None else slot_mapping
+        dst = dst_slot_mapping.to(dev, non_blocking=True) if dev is not None else dst_slot_mapping
+        if dst.dtype != src.dtype:
+            dst = dst.to(src.dtype)
+        pd.direct_push(src, dst, req_id, layer_begin, num_layers)
+        self.stats.inc("stored_tokens", n)
+        return n
+
+    def wait_direct_prefill(self, req_id: str, timeout_s: Optional[float] = None,
+                            sync: bool = False) -> bool:
+        """Decoder: enqueue the bounded per-layer wait for a direct push on the
+        current stream (``sync`` also checks the device status on the host)."""
+        return self._pd_backend().wait_direct(req_id, timeout_s, sync)
+
     def _emit_events(self, tokens, starts, ends, keys) -> None:
         toks = tokens.tolist() if isinstance(tokens, torch.Tensor) else list(tokens)
         parent = None

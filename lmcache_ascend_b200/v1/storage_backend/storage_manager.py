@@ -36,21 +36,26 @@ class StorageManager:
         self.metadata = metadata
         self.backends: "OrderedDict[str, StorageBackendInterface]" = (
             backends if backends is not None else CreateStorageBackends(config, metadata, **kw))
-        self.allocator_backend = None
-        for b in self.backends.values():
-            ab = b.get_allocator_backend()
-            if ab is not None:
-                self.allocator_backend = ab
-                break
         self._lock = threading.Lock()
         self.stats = get_stats()
 
     # ---------------------------------------------------------- allocation
+    @property
+    def allocator_backend(self):
+        """First backend that provides chunk memory (a PD sender's page pool
+        becomes available only after post_init, so this is not cached)."""
+        for b in self.backends.values():
+            ab = b.get_allocator_backend()
+            if ab is not None:
+                return ab
+        return None
+
     def allocate(self, shape, dtype, fmt: MemoryFormat = MemoryFormat.KV_2LTD,
                  eviction: bool = True) -> Optional[MemoryObj]:
-        if self.allocator_backend is None:
+        ab = self.allocator_backend
+        if ab is None:
             raise RuntimeError("no backend provides an allocator")
-        return self.allocator_backend.allocate(shape, dtype, fmt, eviction=eviction)
+        return ab.allocate(shape, dtype, fmt, eviction=eviction)
 
     def batched_allocate(self, shape, dtype, batch_size: int,
                          fmt: MemoryFormat = MemoryFormat.KV_2LTD,
