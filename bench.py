@@ -216,7 +216,7 @@ def main():
             v.view(-1, H * D).index_copy_(0, dst_slots.long(), rows[1])
 
     step = step_ours if a.impl == "ours" else step_nccl
-    n_targets = a.warmup + a.steps + (a.steps if not a.no_e2e else 0)
+    n_targets = a.warmup + a.steps
     targets = ([receiver.expect(T, tile_tokens=a.tile) for _ in range(n_targets)]
                if (receiver is not None and a.impl == "ours") else [None] * n_targets)
     ti = 0
@@ -261,41 +261,87 @@ def main():
     value = bytes_per_pair * pairs / (ms / 1e3) / 1e9
 
     # ------------------------------------------------------------ e2e arm
+    # Same transfer through the engine's public API: the prefiller calls
+    # LMCacheEngine.store_direct_prefill (PD backend handshake + fused push),
+    # the decoder LMCacheEngine.wait_direct_prefill (ZMQ notification +
+    # bounded device flag wait).  Every step copies the slot mappings
+    # host->device from pinned memory and reads the completion status back.
     e2e = None
     if not a.no_e2e and a.impl == "ours":
+        from lmcache_ascend_b200.config import LMCacheEngineConfig, LMCacheEngineMetadata
+        from lmcache_ascend_b200.v1.cache_engine import LMCacheEngine
+        from lmcache_ascend_b200.v1.gpu_connector import VLLMPagedMemGPUConnector
+
+        base = dict(chunk_size=256, enable_pd=True, transfer_channel="nvlink",
+                    pd_buffer_device="cuda", pd_buffer_size=32 << 20, local_cpu=False,
+                    max_local_cpu_size=0.01, pd_peer_init_port=[0], pd_peer_alloc_port=[0])
+        md = LMCacheEngineMetadata("Qwen3-32B", max(1, world // 2), rank % max(1, world // 2),
+                                   "vllm", torch.bfloat16)
+        eng_r = eng_s = None
+        if role_d:
+            rc = LMCacheEngineConfig.from_defaults(pd_role="receiver", **base)
+            eng_r = LMCacheEngine(rc, md, VLLMPagedMemGPUConnector(rc, kvcaches=dst_cache))
+            eng_r.post_init()
+            urls = eng_r.storage_manager.backends["PDBackend"].endpoints()
+        else:
+            urls = None
+        if world > 1:
+            allu = [None] * world
+            dist.all_gather_object(allu, urls, group=gloo)
+        else:
+            allu = [urls]
+        if role_p:
+            iu, au = allu[rank + world // 2] if world > 1 else allu[0]
+            sc = LMCacheEngineConfig.from_defaults(pd_role="sender", **base)
+            eng_s = LMCacheEngine(sc, md, VLLMPagedMemGPUConnector(sc, kvcaches=src_cache),
+                                  peer_init_url=iu, peer_alloc_url=au)
+            eng_s.post_init()
         h_src = src_slots.cpu().pin_memory()
         h_dst = dst_slots.cpu().pin_memory()
         d_src = torch.empty_like(src_slots)
         d_dst = torch.empty_like(dst_slots)
         h_status = torch.empty(4, dtype=torch.int64).pin_memory()
+
+        def e2e_step(i):
+            if eng_s is not None:
+                d_src.copy_(h_src, non_blocking=True)
+                d_dst.copy_(h_dst, non_blocking=True)
+                eng_s.store_direct_prefill(slot_mapping=d_src, dst_slot_mapping=d_dst,
+                                           req_id=f"bench-{i}")
+                pd = eng_s.storage_manager.backends["PDBackend"]
+                h_status.copy_(pd.push_sender.status.tensor, non_blocking=True)
+            if eng_r is not None:
+                if not eng_r.wait_direct_prefill(f"bench-{i}", timeout_s=10.0):
+                    raise RuntimeError("decoder never saw the push notification")
+                pd = eng_r.storage_manager.backends["PDBackend"]
+                h_status.copy_(pd.push_receiver.status.tensor, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            if int(h_status[0]) != 0:
+                raise RuntimeError(f"push reported status {h_status.tolist()}")
+
+        for i in range(a.warmup):
+            e2e_step(f"w{i}")
         barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
-        for _ in range(a.steps):
-            if sender is not None:
-                d_src.copy_(h_src, non_blocking=True)
-                d_dst.copy_(h_dst, non_blocking=True)
-                sender.push(d_src, d_dst, tile_tokens=a.tile, grid=a.grid)
-                h_status.copy_(sender.status.tensor, non_blocking=True)
-            if receiver is not None:
-                receiver.wait(targets[ti], timeout_s=5.0)
-                h_status.copy_(receiver.status.tensor, non_blocking=True)
-            ti += 1
-            torch.cuda.current_stream().synchronize()
-            if int(h_status[0]) != 0:
-                raise RuntimeError(f"push reported status {h_status.tolist()}")
+        for i in range(a.steps):
+            e2e_step(i)
         t1.record()
         torch.cuda.synchronize()
         ems = torch.tensor([t0.elapsed_time(t1) / a.steps], device=dev)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         ems = float(ems.item())
+        barrier()
         e2e = {"value": round(bytes_per_pair * pairs / (ems / 1e3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(ems, 4),
                "h2d_bytes_per_step": (src_slots.numel() + dst_slots.numel()) * 4 * pairs,
                "d2h_bytes_per_step": 32 * world,
-               "api": "lmcache_ascend_b200.parallel.pd_push.PushSender.push / PushReceiver.wait"}
+               "api": "LMCacheEngine.store_direct_prefill / LMCacheEngine.wait_direct_prefill"}
+        for e in (eng_s, eng_r):
+            if e is not None:
+                e.close()
 
     if rank == 0:
         per_pair = value / pairs

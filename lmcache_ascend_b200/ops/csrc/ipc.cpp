@@ -49,8 +49,17 @@ std::map<uintptr_t, std::string> g_by_base;   // base -> handle bytes
 }  // namespace
 
 // Returns (handle bytes, offset of ptr in its allocation, allocation size).
+// Binds the device's primary context to the calling thread.  Driver-API
+// calls (cuMemGetAddressRange) need a current context, and a thread that
+// made no CUDA runtime call yet (e.g. a control-plane server thread) has none.
+static void bind_device(int64_t device) {
+  cudaError_t e = cudaSetDevice(static_cast<int>(device));
+  TORCH_CHECK(e == cudaSuccess, "cudaSetDevice(", device, ") failed: ", cudaGetErrorString(e));
+}
+
 std::tuple<pybind11::bytes, int64_t, int64_t> ipc_export(int64_t ptr, int64_t device) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  bind_device(device);
   auto fn = address_range_fn();
   TORCH_CHECK(fn != nullptr, "cuMemGetAddressRange is unavailable");
   CUdeviceptr base = 0;
@@ -71,6 +80,7 @@ std::tuple<pybind11::bytes, int64_t, int64_t> ipc_export(int64_t ptr, int64_t de
 int64_t ipc_import(const std::string &handle, int64_t offset, int64_t device) {
   TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  bind_device(device);
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_imports.find(handle);
   if (it == g_imports.end()) {

@@ -39,7 +39,19 @@ class NVLinkChannel(BaseTransferChannel):
             self.stream = torch.cuda.Stream()
         super().__init__(peer_id, buffers)
 
+    def register_buffer(self, buf: BufferConfig) -> str:
+        # export once, on the registering thread (which has a CUDA context);
+        # control-plane threads later only hand out the cached descriptor
+        uid = super().register_buffer(buf)
+        self._exports = getattr(self, "_exports", {})
+        self._exports[uid] = self._export_now(buf)
+        return uid
+
     def _export(self, buf: BufferConfig) -> dict:
+        cached = getattr(self, "_exports", {}).get(buf.uuid)
+        return cached if cached is not None else self._export_now(buf)
+
+    def _export_now(self, buf: BufferConfig) -> dict:
         d = {"uuid": buf.uuid, "kind": buf.kind, "nbytes": buf.nbytes,
              "page_bytes": buf.page_bytes, "pid": os.getpid()}
         if buf.kind == "device":
