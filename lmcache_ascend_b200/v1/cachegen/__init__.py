@@ -1,1 +1,227 @@
-"""v1/cachegen"""
+"""CacheGen compression: per-layer quantisation + aligned prefix-code
+entropy coding of KV chunks (serde for the remote tier).
+
+Pipeline (the structure of upstream LMCache's CacheGen serde that the
+reference drives, docs/cachegen/Cachegen.md:1-50, test usage in
+tests/v1/test_cachegen_kernels.py):
+  KV_2LTD chunk [2, L, T, C] -> per layer quantise to ``bins`` levels with a
+  per-(layer, token) scale -> symbols [2L, T, C] uint8 -> per-(layer,
+  channel) CDF -> encode -> bytes; decode reverses it.  ``bins`` is chosen
+  per layer by ``QuantizationSpec`` ranges (more bins for early layers).
+The entropy coder is the native K7 kernels on CUDA tensors and the
+bit-identical oracle on CPU tensors.
+"""
+
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass, field
+from typing import List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from ...ops import api
+
+MAGIC = b"LMCG"
+VERSION = 1
+_DT = {0: torch.float16, 1: torch.bfloat16, 2: torch.float32}
+_DT_ID = {v: k for k, v in _DT.items()}
+
+
+@dataclass
+class QuantizationSpec:
+    start_layer: int
+    end_layer: int
+    bins: int
+
+
+@dataclass
+class CacheGenConfig:
+    nlayers: int
+    kspecs: List[QuantizationSpec]
+    vspecs: List[QuantizationSpec]
+
+    @staticmethod
+    def from_ranges(nlayers: int, k_ranges, v_ranges) -> "CacheGenConfig":
+        return CacheGenConfig(nlayers, [QuantizationSpec(*r) for r in k_ranges],
+                              [QuantizationSpec(*r) for r in v_ranges])
+
+    @staticmethod
+    def default(nlayers: int, early_bins: int = 32, late_bins: int = 16) -> "CacheGenConfig":
+        """``early_bins`` levels for the first third of the layers, ``late_bins`` after
+        (upstream LMCache uses 32 / 16)."""
+        cut = max(1, nlayers // 3)
+        return CacheGenConfig(nlayers, [QuantizationSpec(0, cut, early_bins),
+                                        QuantizationSpec(cut, nlayers, late_bins)],
+                              [QuantizationSpec(0, cut, early_bins),
+                               QuantizationSpec(cut, nlayers, late_bins)])
+
+    def bins(self, which: str, device=None) -> torch.Tensor:
+        specs = self.kspecs if which == "k" else self.vspecs
+        b = torch.zeros(self.nlayers, dtype=torch.int32)
+        for s in specs:
+            b[s.start_layer:min(s.end_layer, self.nlayers)] = s.bins
+        if bool((b == 0).any()):
+            raise ValueError(f"{which} quantisation specs do not cover every layer")
+        return b.to(device) if device is not None else b
+
+
+def quantize(x: torch.Tensor, bins: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """x [L, T, C] float -> (symbols uint8 [L, T, C], scale fp32 [L, T]).
+    Symmetric: level = round(x / scale) + half, half = bins // 2 - 1."""
+    half = (bins // 2 - 1).to(x.device).view(-1, 1, 1).float()
+    amax = x.float().abs().amax(dim=-1, keepdim=True).clamp_min(1e-8)
+    scale = amax / half
+    q = torch.round(x.float() / scale) + half
+    q = torch.minimum(q.clamp_min(0), 2 * half)
+    return q.to(torch.uint8), scale.squeeze(-1)
+
+
+def dequantize(sym: torch.Tensor, scale: torch.Tensor, bins: torch.Tensor,
+               dtype: torch.dtype) -> torch.Tensor:
+    half = (bins // 2 - 1).to(sym.device).view(-1, 1, 1).float()
+    return ((sym.float() - half) * scale.unsqueeze(-1)).to(dtype)
+
+
+def cdf_from_lengths(lengths: torch.Tensor) -> torch.Tensor:
+    """Aligned CDF from code lengths [..., bins] (uint8, 0..12):
+    start_s = sum_{r<s} 2^(16 - len_r); entry = start | len; last entry 0."""
+    w = torch.pow(2, 16 - lengths.long())
+    starts = torch.cumsum(w, dim=-1) - w
+    ent = (starts & 0xFFF0) | lengths.long()
+    last = torch.zeros(ent.shape[:-1] + (1,), dtype=torch.long, device=ent.device)
+    out = torch.cat([ent, last], dim=-1)
+    return torch.where(out >= 32768, out - 65536, out).to(torch.int16)
+
+
+def _pack_nibbles(x: torch.Tensor) -> bytes:
+    a = x.to(torch.uint8).flatten().cpu()
+    if a.numel() % 2:
+        a = torch.cat([a, torch.zeros(1, dtype=torch.uint8)])
+    return ((a[0::2] << 4) | a[1::2]).numpy().tobytes()
+
+
+def _unpack_nibbles(b: bytes, n: int) -> torch.Tensor:
+    a = torch.frombuffer(bytearray(b), dtype=torch.uint8)
+    out = torch.stack([a >> 4, a & 15], dim=1).flatten()
+    return out[:n]
+
+
+@dataclass
+class CacheGenGroup:
+    """Rows (of the 2L K-then-V layer rows) that share one bin count."""
+
+    rows: List[int]
+    bins: int
+    code_lengths: torch.Tensor  # uint8 [n, C, bins]
+    lengths: torch.Tensor       # int32 [n, C] bytes per stream
+    streams: bytes
+
+
+@dataclass
+class CacheGenEncoded:
+    num_layers: int
+    num_tokens: int
+    channels: int
+    dtype: torch.dtype
+    scales: torch.Tensor     # fp32 [2L, T]
+    k_bins: torch.Tensor     # int32 [L]
+    v_bins: torch.Tensor     # int32 [L]
+    groups: List[CacheGenGroup]
+
+    def to_bytes(self) -> bytes:
+        L, T, C = self.num_layers, self.num_tokens, self.channels
+        parts = [struct.pack("<4sHIIIBH", MAGIC, VERSION, L, T, C, _DT_ID[self.dtype],
+                             len(self.groups))]
+        for t in (self.k_bins, self.v_bins, self.scales):
+            parts.append(t.detach().cpu().contiguous().numpy().tobytes())
+        for g in self.groups:
+            cl = _pack_nibbles(g.code_lengths)
+            parts.append(struct.pack("<HII", g.bins, len(g.rows), len(g.streams)))
+            parts.append(torch.tensor(g.rows, dtype=torch.int32).numpy().tobytes())
+            parts.append(g.lengths.detach().cpu().contiguous().numpy().tobytes())
+            parts.append(cl)
+            parts.append(g.streams)
+        return b"".join(parts)
+
+    @staticmethod
+    def from_bytes(b: bytes) -> "CacheGenEncoded":
+        fmt = "<4sHIIIBH"
+        n = struct.calcsize(fmt)
+        magic, ver, L, T, C, dt, ng = struct.unpack(fmt, b[:n])
+        if magic != MAGIC or ver != VERSION:
+            raise ValueError("not a CacheGen payload")
+        off = n
+
+        def take(count, dtype, shape):
+            nonlocal off
+            a = np.frombuffer(b, dtype=dtype, count=count, offset=off).reshape(shape)
+            off += count * np.dtype(dtype).itemsize
+            return torch.from_numpy(a.copy())
+
+        kb = take(L, np.int32, (L,))
+        vb = take(L, np.int32, (L,))
+        scales = take(2 * L * T, np.float32, (2 * L, T))
+        groups = []
+        for _ in range(ng):
+            bins, nrows, slen = struct.unpack("<HII", b[off:off + 10])
+            off += 10
+            rows = take(nrows, np.int32, (nrows,)).tolist()
+            lens = take(nrows * C, np.int32, (nrows, C))
+            ncl = nrows * C * bins
+            nb = (ncl + 1) // 2
+            cl = _unpack_nibbles(b[off:off + nb], ncl).view(nrows, C, bins)
+            off += nb
+            groups.append(CacheGenGroup(rows, bins, cl, lens, b[off:off + slen]))
+            off += slen
+        return CacheGenEncoded(L, T, C, _DT[dt], scales, kb, vb, groups)
+
+
+def encode_kv(kv: torch.Tensor, config: CacheGenConfig) -> CacheGenEncoded:
+    """kv: KV_2LTD chunk [2, L, T, C] (device or host)."""
+    _, L, T, C = kv.shape
+    dev = kv.device
+    kb, vb = config.bins("k", dev), config.bins("v", dev)
+    ks, kscale = quantize(kv[0], kb)
+    vs, vscale = quantize(kv[1], vb)
+    sym = torch.cat([ks, vs], dim=0)                       # [2L, T, C]
+    row_bins = torch.cat([kb, vb]).cpu().tolist()
+    groups = []
+    cap = (T * 12 + 7) // 8 + 1
+    for bins in sorted(set(row_bins)):
+        rows = [r for r, x in enumerate(row_bins) if x == bins]
+        sg = sym[rows].contiguous()
+        cdf = api.calculate_cdf(sg, bins)
+        out = torch.zeros(len(rows), C, cap, dtype=torch.uint8, device=dev)
+        lens = torch.zeros(len(rows), C, dtype=torch.int32, device=dev)
+        api.encode_fast_new(cdf, sg, out, lens)
+        mask = torch.arange(cap, device=dev).unsqueeze(0) < lens.view(-1, 1)
+        streams = out.view(-1, cap)[mask].cpu().numpy().tobytes()
+        code_len = (cdf[..., :bins].to(torch.int32) & 0xF).to(torch.uint8)
+        groups.append(CacheGenGroup(rows, bins, code_len.cpu(), lens.cpu(), streams))
+    return CacheGenEncoded(L, T, C, kv.dtype, torch.cat([kscale, vscale]).float().cpu(),
+                           kb.cpu(), vb.cpu(), groups)
+
+
+def decode_kv(enc: CacheGenEncoded, device="cpu", out: Optional[torch.Tensor] = None
+              ) -> torch.Tensor:
+    L, T, C = enc.num_layers, enc.num_tokens, enc.channels
+    dev = torch.device(device)
+    sym = torch.zeros(2 * L, T, C, dtype=torch.uint8, device=dev)
+    for g in enc.groups:
+        cdf = cdf_from_lengths(g.code_lengths.to(dev))
+        stream = torch.frombuffer(bytearray(g.streams), dtype=torch.uint8).to(dev) \
+            if g.streams else torch.zeros(1, dtype=torch.uint8, device=dev)
+        cum = g.lengths.view(-1).cumsum(0).to(torch.int32).view(len(g.rows), C).to(dev)
+        sg = torch.zeros(len(g.rows), T, C, dtype=torch.uint8, device=dev)
+        api.decode_fast_prefsum(cdf, stream, cum, sg)
+        sym[torch.tensor(g.rows, device=dev)] = sg
+    sc = enc.scales.to(dev)
+    k = dequantize(sym[:L], sc[:L], enc.k_bins, enc.dtype)
+    v = dequantize(sym[L:], sc[L:], enc.v_bins, enc.dtype)
+    res = torch.stack([k, v])
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
