@@ -365,6 +365,8 @@ class LMCacheEngine:
                 o = self.storage_manager.allocate(conn.get_shape(e - s), dtype, fmt)
                 if o is None:
                     raise RuntimeError("store_layer: out of CPU cache memory")
+                # positions the keys were rotated for (CacheBlend re-positions them)
+                o.meta.cached_positions = torch.arange(s, e)
                 row.append(o)
             per_layer.append(row)
         starts = [s for s, _, _ in chunks]

@@ -356,17 +356,57 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
 
 
 class VLLMBufferLayerwiseGPUConnector(VLLMPagedMemLayerwiseGPUConnector):
-    """Layerwise connector used by CacheBlend: besides scattering into the
-    paged cache it exposes each retrieved layer's K/V as a dense ``[T, H*D]``
-    buffer (``get_kv``) so the blender can compare and re-rotate keys
-    (reference npu_connectors.py:405-786)."""
+    """Layerwise connector used by CacheBlend (reference
+    npu_connectors.py:405-786).  For each layer it assembles the retrieved
+    chunks into one dense ``[2, T, H*D]`` buffer covering the request's
+    token range, re-rotates K from the positions the chunks were stored at
+    to their positions in this request (fused RoPE, K8), zeroes the tokens no
+    chunk covers (segment separators), exposes the buffer to the blender
+    (``get_kv``) and writes it into the paged cache."""
 
-    def get_kv(self, obj: MemoryObj, layer: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
-        t = obj.tensor
-        if self.layout.fmt.uses_2ltd_chunks:
-            return t[0, layer], t[1, layer]
-        k_elems = self.layout.planes[0].row_elems
-        return t[0, layer, :, :k_elems], t[0, layer, :, k_elems:]
+    def __init__(self, *a, **kw):
+        super().__init__(*a, **kw)
+        self.fused_rope = None
+        self._bufs = {}
+
+    def get_kv(self, layer_id: int):
+        buf = self._bufs[layer_id]
+        return buf[0], buf[1]
+
+    def batched_to_gpu(self, memory_objs=None, starts=None, ends=None, slot_mapping=None,
+                       sync=True, **kwargs):
+        from ...ops import api
+
+        objs_per_layer = yield
+        base, stop = starts[0], ends[-1]
+        total = stop - base
+        dev = self.device
+        lay = self.layout
+        e = lay.planes[0].row_elems
+        new_pos = torch.arange(base, stop, device=dev)
+        old_pos = new_pos.clone()
+        covered = torch.zeros(total, dtype=torch.bool, device=dev)
+        for s, en, o in zip(starts, ends, objs_per_layer[0]):
+            cp = o.meta.cached_positions
+            old_pos[s - base:en - base] = (cp.to(dev) if cp is not None else
+                                           torch.arange(0, en - s, device=dev))
+            covered[s - base:en - base] = True
+        need_rope = self.fused_rope is not None and not torch.equal(old_pos, new_pos)
+        slots = slot_mapping[base:stop].to(dev).clone()
+        slots[~covered] = -1
+        self._bufs = {}
+        for layer in range(lay.num_layers):
+            buf = torch.zeros(2, total, e, dtype=lay.dtype, device=dev)
+            for s, en, o in zip(starts, ends, objs_per_layer[layer]):
+                buf[:, s - base:en - base] = o.tensor[:, 0].to(dev, non_blocking=True)
+            if need_rope:
+                self.fused_rope(old_pos, new_pos, buf[0])
+            self._bufs[layer] = buf
+            api.single_layer_kv_transfer(buf, lay, layer, slots, False)
+            yield
+        if dev.type == "cuda" and sync:
+            torch.cuda.current_stream(dev).synchronize()
+        yield
 
 
 class SGLangGPUConnector(VLLMPagedMemGPUConnector):
