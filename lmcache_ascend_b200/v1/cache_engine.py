@@ -328,6 +328,7 @@ class LMCacheEngine:
             end = 0
             pinned = []
             for s, e, k in self._chunks(tokens, None, request_configs, hashes, offsets):
+                k = self._lookup_key(k)
                 if self.storage_manager.contains(k, search_range, pin=pin) is None:
                     break
                 if pin:
@@ -337,6 +338,14 @@ class LMCacheEngine:
                 self._lookup_pins.setdefault(lookup_id, []).extend(pinned)
             self.stats.inc("lookup_hit_tokens", end)
             return end
+
+    def _lookup_key(self, key: CacheEngineKey) -> CacheEngineKey:
+        """Layerwise stores keep one object per layer: probe the last layer,
+        which is written together with the others once the store finished."""
+        if self.config.use_layerwise and getattr(self.gpu_connector, "layout", None) is not None:
+            L = self.gpu_connector.layout.num_layers
+            return key.split_layers(L)[L - 1]
+        return key
 
     def lookup_unpin(self, lookup_id: Any) -> None:
         with self._engine_state_lock:
@@ -485,10 +494,15 @@ class LMCacheEngineBuilder:
                       gpu_connector: GPUConnectorInterface, **kw) -> LMCacheEngine:
         with cls._lock:
             eng = cls._engines.get(instance_id)
-            if eng is None:
+            if eng is None or eng._closed:  # a closed engine is never handed out again
                 eng = LMCacheEngine(config, metadata, gpu_connector, **kw)
                 cls._engines[instance_id] = eng
             return eng
+
+    @classmethod
+    def register(cls, instance_id: str, engine: "LMCacheEngine") -> None:
+        with cls._lock:
+            cls._engines[instance_id] = engine
 
     @classmethod
     def get(cls, instance_id: str) -> Optional[LMCacheEngine]:

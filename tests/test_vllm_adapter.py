@@ -1,0 +1,140 @@
+"""vLLM v1 connector logic driven with light stand-ins for vLLM's scheduler
+objects (CPU tier): request A is prefilled and saved; request B with the same
+prompt is matched by the scheduler, and its KV is loaded into B's blocks by
+the worker; chunked prefill saves chunk by chunk; the lookup channel works
+across a ZMQ IPC socket."""
+
+from types import SimpleNamespace
+
+import torch
+
+from lmcache_ascend_b200.config import LMCacheEngineConfig
+from lmcache_ascend_b200.integration.vllm.adapter import LMCacheConnectorV1Impl
+from lmcache_ascend_b200.integration.vllm.lookup import LookupClient, LookupServer
+
+L, NB, BS, H, D = 2, 128, 16, 2, 32
+
+
+def _kv():
+    torch.manual_seed(0)
+    return {f"model.layers.{i}.self_attn.attn": torch.zeros(2, NB, BS, H, D) for i in range(L)}
+
+
+def _sched_out(new=(), cached=None, scheduled=None, finished=()):
+    cached = cached or SimpleNamespace(req_ids=[], new_token_ids=[], new_block_ids=[],
+                                       num_computed_tokens=[], resumed_req_ids=set())
+    return SimpleNamespace(scheduled_new_reqs=list(new), scheduled_cached_reqs=cached,
+                           num_scheduled_tokens=scheduled or {}, finished_req_ids=set(finished))
+
+
+def _pair(cfg):
+    worker = LMCacheConnectorV1Impl("worker", cfg, "m", BS)
+    kv = _kv()
+    worker.register_kv_caches(kv)
+    sched = LMCacheConnectorV1Impl("scheduler", cfg, "m", BS, engine=worker.engine)
+    return sched, worker, kv
+
+
+def _slots(blocks, n):
+    b = torch.tensor(blocks)
+    t = torch.arange(n)
+    return b[t // BS] * BS + t % BS
+
+
+def _fill(kv, slots, seed):
+    g = torch.Generator().manual_seed(seed)
+    for t in kv.values():
+        t.view(2, NB * BS, -1)[:, slots] = torch.randn(2, len(slots), H * D, generator=g)
+
+
+def _read(kv, slots):
+    return [t.view(2, NB * BS, -1)[:, slots].clone() for t in kv.values()]
+
+
+def _step(worker, meta):
+    worker.bind_connector_metadata(meta)
+    worker.start_load_kv(None)
+    for name in worker._layer_names:
+        worker.wait_for_layer_load(name)
+        worker.save_kv_layer(name, None, None)
+    worker.wait_for_save()
+    worker.clear_connector_metadata()
+
+
+def test_save_then_prefix_hit_loads_into_new_blocks():
+    cfg = LMCacheEngineConfig.from_defaults(chunk_size=256, max_local_cpu_size=0.05)
+    sched, worker, kv = _pair(cfg)
+    prompt = list(range(1000, 1600))  # 600 tokens
+    blocks_a = list(range(0, 38))
+    req_a = SimpleNamespace(request_id="A", prompt_token_ids=prompt)
+    assert sched.get_num_new_matched_tokens(req_a, 0) == (0, False)
+    sched.update_state_after_alloc(req_a, None, 0)
+    new_a = SimpleNamespace(req_id="A", prompt_token_ids=prompt, block_ids=(blocks_a,),
+                            num_computed_tokens=0)
+    meta = sched.build_connector_meta(_sched_out([new_a], scheduled={"A": 600}))
+    assert len(meta.requests) == 1 and meta.requests[0].save_spec is not None
+    sa = _slots(blocks_a, 600)
+    _fill(kv, sa, seed=1)  # the model's forward wrote A's KV
+    want = _read(kv, sa)
+    _step(worker, meta)
+
+    req_b = SimpleNamespace(request_id="B", prompt_token_ids=prompt)
+    need, is_async = sched.get_num_new_matched_tokens(req_b, 0)
+    assert need == 599 and not is_async
+    sched.update_state_after_alloc(req_b, None, need)
+    blocks_b = list(range(40, 78))
+    new_b = SimpleNamespace(req_id="B", prompt_token_ids=prompt, block_ids=(blocks_b,),
+                            num_computed_tokens=0)
+    meta = sched.build_connector_meta(_sched_out([new_b], scheduled={"B": 1}))
+    r = meta.requests[0]
+    assert r.load_spec is not None and r.load_spec.lmcache_cached_tokens == 600
+    _step(worker, meta)
+    got = _read(kv, _slots(blocks_b, 600))
+    for a, b in zip(want, got):
+        assert torch.equal(a, b)
+    sched.request_finished(req_b, blocks_b)
+    worker.shutdown()
+    worker.engine.close()
+
+
+def test_chunked_prefill_saves_per_chunk_and_layerwise():
+    cfg = LMCacheEngineConfig.from_defaults(chunk_size=128, max_local_cpu_size=0.05,
+                                            use_layerwise=True)
+    sched, worker, kv = _pair(cfg)
+    prompt = list(range(300))
+    blocks = list(range(0, 19))
+    req = SimpleNamespace(request_id="C", prompt_token_ids=prompt)
+    sched.get_num_new_matched_tokens(req, 0)
+    new = SimpleNamespace(req_id="C", prompt_token_ids=prompt, block_ids=(blocks,),
+                          num_computed_tokens=0)
+    s = _slots(blocks, 300)
+    _fill(kv, s, seed=2)
+    meta = sched.build_connector_meta(_sched_out([new], scheduled={"C": 200}))
+    assert meta.requests[0].token_ids.numel() == 128  # one full chunk so far
+    _step(worker, meta)
+    cached = SimpleNamespace(req_ids=["C"], new_token_ids=[[]], new_block_ids=[None],
+                             num_computed_tokens=[200], resumed_req_ids=set())
+    meta = sched.build_connector_meta(_sched_out(cached=cached, scheduled={"C": 100}))
+    assert meta.requests[0].save_spec.skip_leading_tokens == 128
+    assert meta.requests[0].token_ids.numel() == 300  # last prefill saves the tail
+    _step(worker, meta)
+    assert worker.engine.lookup(torch.tensor(prompt)) == 300  # found through the layer keys
+    worker.shutdown()
+    worker.engine.close()
+
+
+def test_lookup_over_ipc():
+    cfg = LMCacheEngineConfig.from_defaults(chunk_size=64, max_local_cpu_size=0.01,
+                                            lmcache_instance_id="ipc-test")
+    worker = LMCacheConnectorV1Impl("worker", cfg, "m", BS)
+    kv = _kv()
+    worker.register_kv_caches(kv)
+    toks = torch.arange(128)
+    worker.engine.store(toks, slot_mapping=_slots(list(range(8)), 128))
+    client = LookupClient(worker.lookup_url)
+    assert client.lookup(toks.tolist(), "r1") == 128
+    client.unpin("r1")
+    assert client.lookup(list(range(500, 564)), "r2") == 0
+    client.close()
+    worker.shutdown()
+    worker.engine.close()
