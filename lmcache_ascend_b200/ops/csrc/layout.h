@@ -28,7 +28,11 @@ struct PlaneDesc {
   int64_t block_stride;  // bytes between consecutive blocks of this plane
   int64_t slot_stride;   // bytes between consecutive slots inside a block
   int32_t row_bytes;     // bytes moved per token for this plane
-  int32_t pad_;
+  // Segmented rows (head-major "HND" caches): a token's row is
+  // row_bytes / seg_bytes segments of seg_bytes, seg_stride bytes apart in
+  // the paged cache (contiguous in chunks).  seg_bytes == 0: contiguous row.
+  int32_t seg_bytes;
+  int64_t seg_stride;
 };
 
 struct PagedDesc {

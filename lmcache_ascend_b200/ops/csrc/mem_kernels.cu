@@ -169,9 +169,27 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
         if (lane == 0) report_status(j.status, kStatusBadIndex, t, ds, j.dst_paged.num_slots);
         continue;
       }
-      warp_copy_row(paged_addr(j.dst_paged, j.chunk_layer_begin + l, p, ds),
-                    paged_addr(j.paged, j.layer_begin + l, p, slot),
-                    plane_of(j.paged, p).row_bytes, lane);
+      const PlaneDesc sp = plane_of(j.paged, p);
+      const PlaneDesc dp = plane_of(j.dst_paged, p);
+      char *sa = paged_addr(j.paged, j.layer_begin + l, p, slot);
+      char *da = paged_addr(j.dst_paged, j.chunk_layer_begin + l, p, ds);
+      const bool sseg = sp.seg_bytes > 0 && sp.seg_bytes < sp.row_bytes;
+      const bool dseg = dp.seg_bytes > 0 && dp.seg_bytes < dp.row_bytes;
+      if (!sseg && !dseg) {
+        warp_copy_row(da, sa, sp.row_bytes, lane);
+      } else {
+        // copy in units that never straddle a segment on either side
+        const int u = sseg && dseg ? min(sp.seg_bytes, dp.seg_bytes)
+                                   : (sseg ? sp.seg_bytes : dp.seg_bytes);
+        for (int off = 0; off < sp.row_bytes; off += u) {
+          const int64_t so = sseg ? (off / sp.seg_bytes) * sp.seg_stride + off % sp.seg_bytes
+                                  : off;
+          const int64_t doff = dseg ? (off / dp.seg_bytes) * dp.seg_stride +
+                                          off % dp.seg_bytes
+                                    : off;
+          warp_copy_row(da + doff, sa + so, u, lane);
+        }
+      }
       continue;
     }
     const int64_t ct = load_idx(j, t);
@@ -182,11 +200,22 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
     }
     char *pa = paged_addr(j.paged, j.layer_begin + l, p, slot);
     char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + l, p, ct, j.num_tokens);
-    const int rb = plane_of(j.paged, p).row_bytes;
-    if (j.to_chunk)
+    const PlaneDesc pl = plane_of(j.paged, p);
+    const int rb = pl.row_bytes;
+    if (pl.seg_bytes > 0 && pl.seg_bytes < rb) {
+      // head-major cache: the row is strided segments on the paged side
+      for (int off = 0, sg = 0; off < rb; off += pl.seg_bytes, ++sg) {
+        char *ps = pa + static_cast<int64_t>(sg) * pl.seg_stride;
+        if (j.to_chunk)
+          warp_copy_row(ca + off, ps, pl.seg_bytes, lane);
+        else
+          warp_copy_row(ps, ca + off, pl.seg_bytes, lane);
+      }
+    } else if (j.to_chunk) {
       warp_copy_row(ca, pa, rb, lane);
-    else
+    } else {
       warp_copy_row(pa, ca, rb, lane);
+    }
   }
 }
 
@@ -214,7 +243,8 @@ static int env_int(const char *name, int dflt) {
 PagedLayout::PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
                          std::vector<int64_t> slot_stride,
                          std::vector<int64_t> row_bytes, int64_t block_size,
-                         int64_t num_slots)
+                         int64_t num_slots, std::vector<int64_t> seg_bytes,
+                         std::vector<int64_t> seg_stride)
     : ptrs_(ptrs) {
   TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.is_contiguous(),
               "PagedLayout: ptrs must be a contiguous int64 tensor");
@@ -237,6 +267,15 @@ PagedLayout::PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
     desc_.plane[p].row_bytes = static_cast<int32_t>(row_bytes[p]);
     TORCH_CHECK(row_bytes[p] > 0, "PagedLayout: row_bytes must be > 0");
     if ((block_stride[p] | slot_stride[p] | row_bytes[p]) & 15) aligned16_ = false;
+    if (p < static_cast<int>(seg_bytes.size()) && seg_bytes[p] > 0 &&
+        seg_bytes[p] < row_bytes[p]) {
+      TORCH_CHECK(row_bytes[p] % seg_bytes[p] == 0 &&
+                      p < static_cast<int>(seg_stride.size()),
+                  "PagedLayout: row must be a whole number of segments");
+      desc_.plane[p].seg_bytes = static_cast<int32_t>(seg_bytes[p]);
+      desc_.plane[p].seg_stride = seg_stride[p];
+      segmented_ = true;
+    }
   }
   TORCH_CHECK(ptrs.is_cuda(), "PagedLayout: ptrs table must live on the device");
   // Alignment of the plane base pointers is checked by the Python layer,

@@ -19,9 +19,12 @@ class PagedLayout {
  public:
   PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
               std::vector<int64_t> slot_stride, std::vector<int64_t> row_bytes,
-              int64_t block_size, int64_t num_slots);
+              int64_t block_size, int64_t num_slots,
+              std::vector<int64_t> seg_bytes = {}, std::vector<int64_t> seg_stride = {});
+  bool segmented() const { return segmented_; }
   const PagedDesc &desc() const { return desc_; }
-  bool aligned() const { return aligned16_ && bases_aligned_; }
+  // TMA bulk copies need 16-byte aligned, contiguous rows on the paged side
+  bool aligned() const { return aligned16_ && bases_aligned_ && !segmented_; }
   void set_bases_aligned(bool v) { bases_aligned_ = v; }
   int64_t num_layers() const { return desc_.num_layers; }
   int64_t num_planes() const { return desc_.num_planes; }
@@ -32,6 +35,7 @@ class PagedLayout {
   PagedDesc desc_;
   bool aligned16_ = true;
   bool bases_aligned_ = true;
+  bool segmented_ = false;
 };
 
 // Chunk-object layout (strides are per chunk token, see kv_copy.cuh).

@@ -76,6 +76,15 @@ __device__ __forceinline__ unsigned row_off(const PagedDesc &pd, const PlaneDesc
                                static_cast<int64_t>(slot - b * bs) * pl.slot_stride);
 }
 
+// Byte offset of row byte `vb` inside the paged row: identity for
+// contiguous rows, (vb / seg) * seg_stride + vb % seg for head-major rows.
+__device__ __forceinline__ unsigned seg_off(const PlaneDesc &pl, unsigned vb) {
+  if (pl.seg_bytes <= 0 || pl.seg_bytes >= pl.row_bytes) return vb;
+  const unsigned sb = static_cast<unsigned>(pl.seg_bytes);
+  const unsigned q = vb / sb;
+  return static_cast<unsigned>(q * pl.seg_stride) + (vb - q * sb);
+}
+
 __global__ void __launch_bounds__(kPushWarps * 32)
     pd_push_kernel(PushJob j) {
   const int np = j.src.num_planes;
@@ -115,8 +124,8 @@ __global__ void __launch_bounds__(kPushWarps * 32)
               if (ss >= j.src.num_slots || dd >= j.dst.num_slots) {
                 if (vb == 0) report_status(j.status, kStatusBadSlot, t0 + ti, ss, dd);
               } else {
-                so[k] = row_off(j.src, spl, static_cast<unsigned>(ss)) + vb;
-                dp[k] = row_off(j.dst, dpl, static_cast<unsigned>(dd)) + vb;
+                so[k] = row_off(j.src, spl, static_cast<unsigned>(ss)) + seg_off(spl, vb);
+                dp[k] = row_off(j.dst, dpl, static_cast<unsigned>(dd)) + seg_off(dpl, vb);
               }
             }
           }
@@ -144,7 +153,7 @@ __global__ void __launch_bounds__(kPushWarps * 32)
         for (int r = 0; r < j.replicas; ++r) {
           char *db = reinterpret_cast<char *>(
               j.dst.ptrs[(static_cast<int64_t>(r) * j.dst.num_layers + layer) * np + p]);
-          db[dof + bi] = sbase[so + bi];
+          db[dof + seg_off(dpl, bi)] = sbase[so + seg_off(spl, bi)];
         }
       }
     }
@@ -206,9 +215,13 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
   TORCH_CHECK(layer_begin >= 0 && layer_begin + num_layers <= src.desc().num_layers &&
                   layer_begin + num_layers <= dst_layers,
               "layer range out of the caches");
-  for (int p = 0; p < src.desc().num_planes; ++p)
+  for (int p = 0; p < src.desc().num_planes; ++p) {
     TORCH_CHECK(src.desc().plane[p].row_bytes == dst.desc().plane[p].row_bytes,
                 "src/dst row size mismatch on plane ", p);
+    for (const PlaneDesc *pl : {&src.desc().plane[p], &dst.desc().plane[p]})
+      TORCH_CHECK(pl->seg_bytes == 0 || pl->seg_bytes % 16 == 0,
+                  "pd_push: row segments must be 16-byte multiples");
+  }
   TORCH_CHECK(flag_ptrs.empty() || static_cast<int64_t>(flag_ptrs.size()) == replicas,
               "flag_ptrs: one per replica (or none)");
   if (src_slots.numel() == 0 || num_layers == 0) return;

@@ -65,9 +65,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   py::class_<PagedLayout>(m, "PagedLayout")
       .def(py::init<at::Tensor, std::vector<int64_t>, std::vector<int64_t>,
-                    std::vector<int64_t>, int64_t, int64_t>(),
+                    std::vector<int64_t>, int64_t, int64_t, std::vector<int64_t>,
+                    std::vector<int64_t>>(),
            py::arg("ptrs"), py::arg("block_stride"), py::arg("slot_stride"),
-           py::arg("row_bytes"), py::arg("block_size"), py::arg("num_slots"))
+           py::arg("row_bytes"), py::arg("block_size"), py::arg("num_slots"),
+           py::arg("seg_bytes") = std::vector<int64_t>{},
+           py::arg("seg_stride") = std::vector<int64_t>{})
+      .def_property_readonly("segmented", &PagedLayout::segmented)
       .def("set_bases_aligned", &PagedLayout::set_bases_aligned)
       .def_property_readonly("aligned", &PagedLayout::aligned)
       .def_property_readonly("num_layers", &PagedLayout::num_layers)

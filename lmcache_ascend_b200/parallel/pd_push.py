@@ -38,6 +38,8 @@ class ReceiverDesc:
     planes: List[List[dict]]  # [layer][plane] -> IpcDesc dict
     flags: dict               # IpcDesc dict of the flag array
     device: int
+    seg_bytes: List[int] = field(default_factory=list)   # head-major rows (0: contiguous)
+    seg_stride: List[int] = field(default_factory=list)
 
     def to_dict(self) -> dict:
         return self.__dict__.copy()
@@ -70,7 +72,9 @@ class PushReceiver:
             block_stride=[p.views[0].stride(0) * es for p in layout.planes],
             slot_stride=[p.views[0].stride(1) * es for p in layout.planes],
             row_bytes=layout.row_bytes, planes=planes,
-            flags=export_local(self._flags_buf.data_ptr(), dev).to_dict(), device=dev)
+            flags=export_local(self._flags_buf.data_ptr(), dev).to_dict(), device=dev,
+            seg_bytes=[p.seg_elems * es if p.segmented else 0 for p in layout.planes],
+            seg_stride=[p.seg_stride * es if p.segmented else 0 for p in layout.planes])
 
     def expect(self, num_tokens: int, layer_begin: int = 0,
                num_layers: Optional[int] = None, tile_tokens: int = 128) -> torch.Tensor:
@@ -120,7 +124,8 @@ class PushSender:
         for r in receivers:
             if (r.row_bytes != self.layout.row_bytes or r.num_layers != r0.num_layers
                     or r.block_size != r0.block_size or r.block_stride != r0.block_stride
-                    or r.slot_stride != r0.slot_stride):
+                    or r.slot_stride != r0.slot_stride or r.seg_bytes != r0.seg_bytes
+                    or r.seg_stride != r0.seg_stride):
                 raise ValueError("receiver layouts must match the sender's rows and each other")
         ptrs = []
         for r in receivers:
@@ -129,7 +134,8 @@ class PushSender:
                     ptrs.append(self.peers.resolve(IpcDesc.from_dict(pd)))
         table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         self._dst = mod.PagedLayout(table, r0.block_stride, r0.slot_stride, r0.row_bytes,
-                                    r0.block_size, r0.num_slots)
+                                    r0.block_size, r0.num_slots, list(r0.seg_bytes),
+                                    list(r0.seg_stride))
         self._dst.set_bases_aligned(all(p % 16 == 0 for p in ptrs))
         self._flag_ptrs = [self.peers.resolve(IpcDesc.from_dict(r.flags)) for r in receivers]
         self.replicas = len(receivers)

@@ -118,27 +118,54 @@ class KVCacheFormat(Enum):
 
 @dataclass
 class Plane:
-    """One component of a layer's paged cache as a [NB, BS, E] strided view."""
+    """One component of a layer's paged cache.
 
-    views: List[torch.Tensor]  # per layer: [num_blocks, block_size, E]
+    ``views`` per layer: [NB, BS, E] when a slot's row is contiguous, or
+    [NB, BS, H, D] when the cache stores heads apart (head-major "HND"
+    storage behind a token-major shape; vLLM uses it for some attention
+    backends).  In the latter case a row is H segments of D elements,
+    ``seg_stride`` elements apart.
+    """
+
+    views: List[torch.Tensor]
     row_elems: int
     elem_size: int
+    seg_elems: int = 0   # 0: contiguous rows
+    seg_stride: int = 0  # elements between a row's segments
 
     @property
     def row_bytes(self) -> int:
         return self.row_elems * self.elem_size
 
+    @property
+    def segmented(self) -> bool:
+        return 0 < self.seg_elems < self.row_elems
 
-def _as_rows(t: torch.Tensor) -> torch.Tensor:
-    """[NB, BS, ...] -> [NB, BS, E] view; the row must be contiguous."""
-    nb, bs = t.shape[0], t.shape[1]
-    e = 1
-    for s in t.shape[2:]:
-        e *= s
-    rows = t.reshape(nb, bs, e) if t.ndim > 3 else t
-    if rows.stride(2) != 1 or (e > 1 and rows.data_ptr() != t.data_ptr()):
-        raise ValueError("paged KV rows must be contiguous within a slot")
-    return rows
+    def rows(self, layer: int, blk, off) -> torch.Tensor:
+        r = self.views[layer][blk, off]
+        return r.reshape(r.shape[0], -1) if self.segmented else r
+
+    def set_rows(self, layer: int, blk, off, rows: torch.Tensor) -> None:
+        v = self.views[layer]
+        v[blk, off] = rows.view(rows.shape[0], *v.shape[2:]) if self.segmented else rows
+
+
+def _as_rows(t: torch.Tensor):
+    """[NB, BS, ...] -> (view, seg_elems, seg_stride): a contiguous [NB, BS, E]
+    row view, or the [NB, BS, H, D] tensor when heads are stored apart."""
+    if t.stride(-1) != 1:
+        raise ValueError("the last KV dimension must be contiguous")
+    if t.ndim == 3:
+        return t, 0, 0
+    if t.ndim != 4:
+        raise ValueError(f"unsupported paged KV tensor rank {t.ndim}")
+    nb, bs, h, d = t.shape
+    if h == 1 or t.stride(2) == d:
+        rows = t.reshape(nb, bs, h * d)
+        if rows.data_ptr() != t.data_ptr() or rows.stride(2) != 1:
+            raise ValueError("paged KV rows must be addressable in place")
+        return rows, 0, 0
+    return t, d, t.stride(2)
 
 
 class PagedKVLayout:
@@ -194,8 +221,11 @@ class PagedKVLayout:
         nplanes = len(per_layer[0])
         planes = []
         for p in range(nplanes):
-            views = [_as_rows(layer[p]) for layer in per_layer]
-            planes.append(Plane(views, views[0].shape[2], views[0].element_size()))
+            got = [_as_rows(layer[p]) for layer in per_layer]
+            views = [g[0] for g in got]
+            v0 = views[0]
+            row = v0.shape[2] * (v0.shape[3] if v0.ndim == 4 else 1)
+            planes.append(Plane(views, row, v0.element_size(), got[0][1], got[0][2]))
         return planes
 
     # ----------------------------------------------------------- chunk format
@@ -255,8 +285,11 @@ class PagedKVLayout:
             es = self.elem_size
             block_stride = [p.views[0].stride(0) * es for p in self.planes]
             slot_stride = [p.views[0].stride(1) * es for p in self.planes]
+            seg_bytes = [p.seg_elems * es if p.segmented else 0 for p in self.planes]
+            seg_stride = [p.seg_stride * es if p.segmented else 0 for p in self.planes]
             self._native = mod.PagedLayout(table, block_stride, slot_stride,
-                                           self.row_bytes, self.block_size, self.num_slots)
+                                           self.row_bytes, self.block_size, self.num_slots,
+                                           seg_bytes, seg_stride)
             self._native.set_bases_aligned(aligned)
         return self._native
 
@@ -288,7 +321,7 @@ class PagedKVLayout:
         blk, off = s // self.block_size, s % self.block_size
         for li in range(num_layers):
             for p, plane in enumerate(self.planes):
-                src = plane.views[layer_begin + li][blk, off]
+                src = plane.rows(layer_begin + li, blk, off)
                 dst = self._row_view(chunk, chunk_layer_begin + li, p)
                 dst[idx.to(dst.device) + tok_off] = src.to(dst.device, dst.dtype)
 
@@ -305,4 +338,4 @@ class PagedKVLayout:
             for p, plane in enumerate(self.planes):
                 src = self._row_view(chunk, chunk_layer_begin + li, p)
                 rows = src[idx.to(src.device) + tok_off].to(self.device, self.dtype)
-                plane.views[layer_begin + li][blk, off] = rows
+                plane.set_rows(layer_begin + li, blk, off, rows)

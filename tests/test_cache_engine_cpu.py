@@ -28,7 +28,7 @@ def _rows(layout: PagedKVLayout, slots):
     """[L, T, sum(E)] copy of the rows at `slots` (planes concatenated)."""
     s = slots.long()
     blk, off = s // layout.block_size, s % layout.block_size
-    return torch.stack([torch.cat([p.views[l][blk, off] for p in layout.planes], dim=-1)
+    return torch.stack([torch.cat([p.rows(l, blk, off) for p in layout.planes], dim=-1)
                         for l in range(layout.num_layers)])
 
 
@@ -188,4 +188,22 @@ def test_kv_events_and_unhealthy():
     eng.mark_unhealthy("test")
     eng.store(torch.arange(500, 628), slot_mapping=random_slots(128, 512))
     assert eng.lookup(torch.arange(500, 628)) == 0
+    eng.close()
+
+
+def test_head_major_cache_round_trip():
+    """vLLM can store heads apart behind a token-major shape (HND)."""
+    g = torch.Generator().manual_seed(3)
+    kv = [torch.randn(16, 2, 2, 16, 32, generator=g).permute(0, 1, 3, 2, 4) for _ in range(2)]
+    eng, conn = _engine(kv, chunk=64)
+    assert conn.layout.planes[0].segmented
+    tokens = torch.arange(100)
+    slots = random_slots(100, 256, seed=1)
+    exp = _rows(conn.layout, slots)
+    eng.store(tokens, slot_mapping=slots)
+    fresh = [torch.zeros(16, 2, 2, 16, 32).permute(0, 1, 3, 2, 4) for _ in range(2)]
+    conn.register_kv_caches(fresh)
+    slots2 = random_slots(100, 256, seed=2)
+    assert bool(eng.retrieve(tokens, slot_mapping=slots2).all())
+    assert torch.equal(_rows(conn.layout, slots2), exp)
     eng.close()

@@ -185,3 +185,58 @@ def test_fused_staged_host_transfer(fmt):
     back = torch.zeros_like(ref)
     lay2.gather_ref(back, slots)
     assert torch.equal(back, ref)
+
+
+def _hnd_cache(L, NB, BS, H, D, seed):
+    """flashinfer-style [NB, 2, BS, H, D] view over head-major [NB, 2, H, BS, D] storage"""
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(NB, 2, H, BS, D, generator=g).to(torch.bfloat16).to(DEV)
+            .permute(0, 1, 3, 2, 4) for _ in range(L)]
+
+
+@pytest.mark.parametrize("mode", [0, SIMT])
+def test_head_major_layout_gather_scatter(mode):
+    kv = _hnd_cache(3, 32, 16, 4, 64, seed=11)
+    lay = PagedKVLayout(kv)
+    assert lay.planes[0].segmented and lay.native().segmented
+    T = 200
+    slots = random_slots(T, lay.num_slots, seed=12, device=DEV)
+    got = torch.zeros(lay.chunk_shape(T), dtype=lay.dtype, device=DEV)
+    ref = torch.zeros_like(got)
+    _xfer(lay, got, slots, True, mode)
+    lay.gather_ref(ref, slots)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    kv2 = [torch.zeros_like(t) for t in kv]
+    lay2 = PagedKVLayout(kv2)
+    _xfer(lay2, got, slots, False, mode)
+    torch.cuda.synchronize()
+    back = torch.zeros_like(ref)
+    lay2.gather_ref(back, slots)
+    assert torch.equal(back, ref)
+
+
+@pytest.mark.parametrize("engine", ["auto", "push"])
+def test_head_major_push(engine):
+    from lmcache_ascend_b200.parallel.pd_push import PushReceiver, PushSender
+
+    src = _hnd_cache(2, 16, 16, 4, 64, seed=13)
+    dst = [torch.zeros_like(t) for t in src]
+    T = 150
+    ss = random_slots(T, 256, seed=14, device=DEV, dtype=torch.int32)
+    ds = random_slots(T, 256, seed=15, device=DEV, dtype=torch.int32)
+    recv = PushReceiver(PagedKVLayout(dst))
+    send = PushSender(PagedKVLayout(src), engine=engine)
+    send.connect([recv.desc])
+    tg = recv.expect(T)
+    send.push(ss, ds)
+    recv.wait(tg, timeout_s=2.0)
+    torch.cuda.synchronize()
+    send.check()
+    recv.check()
+    ls, ld = PagedKVLayout(src), PagedKVLayout(dst)
+    a = torch.zeros(ls.chunk_shape(T), dtype=ls.dtype, device=DEV)
+    b = torch.zeros_like(a)
+    ls.gather_ref(a, ss)
+    ld.gather_ref(b, ds)
+    assert torch.equal(a, b)
