@@ -1,0 +1,175 @@
+"""P2P backend: share cached chunks between serving instances.
+
+Behaviour of the reference's ``P2PBackend`` (lmcache_ascend/v1/storage_backend/
+p2p_backend.py:106-985): chunks stored locally are announced to the
+controller (and withdrawn when the CPU tier evicts them); a lookup miss in
+the local tiers asks the controller which instance holds the key; a get pulls
+the chunk from that instance's peer server, retrying other holders (up to
+``p2p_max_retries``) when a peer fails or times out.  The peer server answers
+from its own CPU tier.  Chunk bytes travel as naive-serde messages over ZMQ
+(host-resident chunks; on one box the copy is PCIe/host-memory bound anyway).
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+import uuid as _uuid
+from typing import Any, Dict, List, Optional, Sequence, Tuple
+
+import msgpack
+import zmq
+
+from ...config import LMCacheEngineConfig
+from ...utils.keys import CacheEngineKey
+from ...utils.logging import init_logger
+from ...utils.metrics import get_stats
+from ..memory_management import MemoryObj
+from .abstract_backend import StorageBackendInterface
+from .serde import NaiveSerde
+
+logger = init_logger(__name__)
+
+
+class P2PBackend(StorageBackendInterface):
+    name = "P2PBackend"
+
+    def __init__(self, config: LMCacheEngineConfig, metadata, local_cpu, **kw):
+        self.config = config
+        self.local = local_cpu
+        self.instance = f"{config.lmcache_instance_id}-{metadata.worker_id if metadata else 0}" \
+                        f"-{_uuid.uuid4().hex[:6]}"
+        self.timeout_ms = int(config.blocking_timeout_secs * 1000)
+        self.ctx = zmq.Context.instance()
+        self.serde = NaiveSerde()
+        self.stats = get_stats()
+        self._stop = threading.Event()
+        self._ctl_lock = threading.Lock()
+        self._ctl = None
+        self._loc_cache: Dict[str, Tuple[float, List]] = {}
+        host = config.p2p_host or "127.0.0.1"
+        ports = config.p2p_init_ports or [0]
+        port = ports[(metadata.worker_id if metadata else 0) % len(ports)]
+        self._srv = self.ctx.socket(zmq.REP)
+        self._srv.setsockopt(zmq.LINGER, 0)
+        if port == 0:
+            port = self._srv.bind_to_random_port(f"tcp://{host}")
+        else:
+            self._srv.bind(f"tcp://{host}:{port}")
+        self.peer_url = f"tcp://{host}:{port}"
+        self._t = threading.Thread(target=self._serve, daemon=True, name="lmc-p2p-peer")
+        self._t.start()
+        if not config.controller_url:
+            raise ValueError("enable_p2p needs controller_url")
+        self._ctl_rpc("register", self.peer_url)
+        local_cpu.evict_listeners.append(self._on_evict)
+
+    # ----------------------------------------------------------- controller
+    def _ctl_rpc(self, op: str, payload):
+        with self._ctl_lock:
+            if self._ctl is None:
+                s = self.ctx.socket(zmq.REQ)
+                s.setsockopt(zmq.LINGER, 0)
+                s.setsockopt(zmq.RCVTIMEO, self.timeout_ms)
+                s.setsockopt(zmq.SNDTIMEO, self.timeout_ms)
+                s.connect(self.config.controller_url)
+                self._ctl = s
+            try:
+                self._ctl.send(msgpack.packb([op, self.instance, payload], use_bin_type=True))
+                st, res = msgpack.unpackb(self._ctl.recv(), raw=False)
+            except zmq.Again:
+                self._ctl.close()
+                self._ctl = None
+                raise TimeoutError("P2P controller did not answer")
+        if st != "ok":
+            raise RuntimeError(f"controller error: {res}")
+        return res
+
+    def _on_evict(self, key: CacheEngineKey) -> None:
+        try:
+            self._ctl_rpc("evict", [key.to_string()])
+        except (TimeoutError, RuntimeError):
+            logger.warning("P2P: could not withdraw %s", key)
+
+    # ----------------------------------------------------------- peer server
+    def _serve(self) -> None:
+        poller = zmq.Poller()
+        poller.register(self._srv, zmq.POLLIN)
+        while not self._stop.is_set():
+            if not poller.poll(100):
+                continue
+            try:
+                op, key = msgpack.unpackb(self._srv.recv(), raw=False)
+                data = None
+                if op == "get":
+                    obj = self.local.get_blocking(CacheEngineKey.from_string(key))
+                    if obj is not None:
+                        try:
+                            data = self.serde.serialize(obj)
+                        finally:
+                            obj.ref_count_down()
+                self._srv.send(msgpack.packb(["ok", data], use_bin_type=True))
+            except Exception as e:
+                self._srv.send(msgpack.packb(["err", str(e)], use_bin_type=True))
+        self._srv.close()
+
+    # ------------------------------------------------------- storage API
+    def batched_submit_put_task(self, keys: Sequence[CacheEngineKey], objs: Sequence[MemoryObj],
+                                transfer_spec: Any = None):
+        # the CPU tier keeps the data; announce where it can be found
+        if keys:
+            try:
+                self._ctl_rpc("admit", [k.to_string() for k in keys])
+            except (TimeoutError, RuntimeError) as e:
+                logger.warning("P2P admit failed: %s", e)
+        return None
+
+    def _holders(self, key: str) -> List:
+        now = time.monotonic()
+        ent = self._loc_cache.get(key)
+        if ent is not None and now - ent[0] < 1.0:
+            return ent[1]
+        try:
+            res = self._ctl_rpc("lookup", key)
+        except (TimeoutError, RuntimeError):
+            res = []
+        self._loc_cache[key] = (now, res)
+        return res
+
+    def contains(self, key: CacheEngineKey, pin: bool = False) -> bool:
+        return bool(self._holders(key.to_string()))
+
+    def get_blocking(self, key: CacheEngineKey) -> Optional[MemoryObj]:
+        k = key.to_string()
+        holders = self._holders(k)[: max(1, self.config.p2p_max_retries)]
+        for inst, url in holders:
+            s = self.ctx.socket(zmq.REQ)
+            s.setsockopt(zmq.LINGER, 0)
+            s.setsockopt(zmq.RCVTIMEO, self.timeout_ms)
+            s.setsockopt(zmq.SNDTIMEO, self.timeout_ms)
+            s.connect(url)
+            try:
+                s.send(msgpack.packb(["get", k], use_bin_type=True))
+                st, data = msgpack.unpackb(s.recv(), raw=False)
+            except zmq.Again:
+                logger.warning("P2P peer %s timed out for %s; trying the next holder", inst, k)
+                self.stats.inc("p2p_retries")
+                continue
+            finally:
+                s.close()
+            if st == "ok" and data is not None:
+                self.stats.inc("p2p_get_bytes", len(data))
+                return self.serde.deserialize(data, self.local)
+            self.stats.inc("p2p_retries")
+        self._loc_cache.pop(k, None)
+        return None
+
+    def close(self) -> None:
+        try:
+            self._ctl_rpc("deregister", None)
+        except (TimeoutError, RuntimeError):
+            pass
+        self._stop.set()
+        self._t.join(timeout=2)
+        if self._ctl is not None:
+            self._ctl.close()
