@@ -12,6 +12,7 @@ from ...config import LMCacheEngineConfig, LMCacheEngineMetadata
 from .connector import (
     GPUConnectorInterface,
     SGLangGPUConnector,
+    SGLangLayerwiseGPUConnector,
     VLLMBufferLayerwiseGPUConnector,
     VLLMPagedMemGPUConnector,
     VLLMPagedMemLayerwiseGPUConnector,
@@ -23,8 +24,9 @@ def CreateGPUConnector(config: LMCacheEngineConfig,
                        engine: str = "vllm", device=None) -> GPUConnectorInterface:
     use_mla = bool(metadata.use_mla) if metadata is not None else False
     if engine == "sglang":
-        return SGLangGPUConnector(config, device=device, use_mla=use_mla,
-                                  layerwise=config.use_layerwise)
+        if config.use_layerwise:
+            return SGLangLayerwiseGPUConnector(config, device=device, use_mla=use_mla)
+        return SGLangGPUConnector(config, device=device, use_mla=use_mla)
     if config.enable_blending:
         return VLLMBufferLayerwiseGPUConnector(config, device=device, use_mla=use_mla)
     if config.use_layerwise:
@@ -36,6 +38,7 @@ __all__ = [
     "CreateGPUConnector",
     "GPUConnectorInterface",
     "SGLangGPUConnector",
+    "SGLangLayerwiseGPUConnector",
     "VLLMBufferLayerwiseGPUConnector",
     "VLLMPagedMemGPUConnector",
     "VLLMPagedMemLayerwiseGPUConnector",

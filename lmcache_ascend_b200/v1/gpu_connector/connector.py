@@ -409,18 +409,27 @@ class VLLMBufferLayerwiseGPUConnector(VLLMPagedMemLayerwiseGPUConnector):
         yield
 
 
-class SGLangGPUConnector(VLLMPagedMemGPUConnector):
-    """SGLang token-pool caches: ``[K_all, V_all]`` each ``[L, NB, BS, H, D]``
-    or per-layer token pools (``BS`` = 1) (reference npu_connectors.py:8093-8376)."""
-
-    def __init__(self, config=None, device=None, use_mla=False, layerwise=False, **kw):
-        super().__init__(config, device=device, use_mla=use_mla, **kw)
-        self.layerwise = layerwise
+class _SGLangPools:
+    """SGLang caches: ``[K_all, V_all]`` each ``[L, NB, BS, H, D]``, per-layer
+    token pools ``[L, size, H, D]`` (page size 1), or per-layer (K, V)
+    tuples (reference npu_connectors.py:8093-8376)."""
 
     def register_kv_caches(self, kvcaches, fmt=None) -> None:
         if isinstance(kvcaches, (list, tuple)) and len(kvcaches) == 2 and \
                 isinstance(kvcaches[0], torch.Tensor) and kvcaches[0].dim() == 4:
-            # per-layer token pool [L, size, H, D] -> add a block dim of 1
-            k, v = kvcaches
+            k, v = kvcaches  # per-layer token pool [L, size, H, D] -> block dim of 1
             kvcaches = [k.unsqueeze(2), v.unsqueeze(2)]
         super().register_kv_caches(list(kvcaches), fmt or KVCacheFormat.SEPARATE_KV)
+
+
+class SGLangGPUConnector(_SGLangPools, VLLMPagedMemGPUConnector):
+    def __init__(self, config=None, device=None, use_mla=False, layerwise=False, **kw):
+        VLLMPagedMemGPUConnector.__init__(self, config, device=device, use_mla=use_mla, **kw)
+        self.layerwise = layerwise
+
+
+class SGLangLayerwiseGPUConnector(_SGLangPools, VLLMPagedMemLayerwiseGPUConnector):
+    def __init__(self, config=None, device=None, use_mla=False, **kw):
+        VLLMPagedMemLayerwiseGPUConnector.__init__(self, config, device=device, use_mla=use_mla,
+                                                   **kw)
+        self.layerwise = True
