@@ -37,6 +37,10 @@ class LMCacheEngineConfig:
     store_async: bool = False
     store_async_max_queue_size: int = 64
     blocking_timeout_secs: float = 10.0
+    # layerwise stores: bound on puts in flight to slower tiers
+    layerwise_put_max_bytes: int = 4 << 30
+    layerwise_put_max_batches: int = 64
+    layerwise_put_timeout_secs: float = 60.0
     save_only_first_rank: bool = False  # MLA: replicated latent, rank 0 stores
     gpu_transfer_mode: str = "auto"     # auto | tma | simt
     cpu_transfer_mode: str = "copy_engine"  # copy_engine | zero_copy

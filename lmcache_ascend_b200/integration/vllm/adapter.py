@@ -251,6 +251,13 @@ class LMCacheConnectorV1Impl:
 
         self._layer_names = sorted(kv_caches, key=layer_index)
         caches = [kv_caches[n] for n in self._layer_names]
+        from ...v1.kv_layer_groups import KVLayerGroupsManager
+
+        self.layer_groups = KVLayerGroupsManager()
+        self.layer_groups.build_kv_layer_groups({n: kv_caches[n] for n in self._layer_names})
+        if self.layer_groups.num_groups > 1:
+            raise ValueError("layers with different KV cache shapes/dtypes "
+                             f"({self.layer_groups.num_groups} groups) need one engine per group")
         eng = self._ensure_engine()
         first = caches[0]
         if self.metadata.kv_dtype is None:

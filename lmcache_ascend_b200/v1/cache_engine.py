@@ -386,12 +386,41 @@ class LMCacheEngine:
         for layer in range(L):
             yield
             next(gen, None)
+        q = self.layerwise_put_queue
+        req_id = kwargs.get("req_id", "")
         for layer in range(L):
             lkeys = [k.split_layers(L)[layer] for _, _, k in chunks]
-            self.storage_manager.batched_put(lkeys, per_layer[layer])
+            size = sum(o.get_size() for o in per_layer[layer])
+            q.reserve(size)
+            try:
+                futs = self.storage_manager.batched_put(lkeys, per_layer[layer])
+            except BaseException as e:
+                q.fail(e)
+                raise
+            q.add(size, futs, req_id=req_id, keys=lkeys)
             for o in per_layer[layer]:
                 o.ref_count_down()
         yield
+
+    @property
+    def layerwise_put_queue(self):
+        """Bound on layerwise puts in flight to asynchronous tiers."""
+        if getattr(self, "_put_queue", None) is None:
+            from .layerwise_cpu_fill import LayerwisePutQueue
+
+            c = self.config
+            self._put_queue = LayerwisePutQueue(c.layerwise_put_max_bytes,
+                                                c.layerwise_put_max_batches,
+                                                c.layerwise_put_timeout_secs)
+        return self._put_queue
+
+    def wait_layerwise_puts(self, req_ids: Optional[List[str]] = None) -> None:
+        """Fence the layerwise puts of ``req_ids`` (all puts when None)."""
+        q = self.layerwise_put_queue
+        if req_ids is None:
+            q.drain()
+        else:
+            q.drain_requests(req_ids)
 
     def retrieve_layer(self, tokens: torch.Tensor, mask: Optional[torch.Tensor] = None,
                        **kwargs) -> Generator[Optional[torch.Tensor], None, None]:
@@ -475,6 +504,11 @@ class LMCacheEngine:
             self.wait_for_pending_stores(timeout=self.config.blocking_timeout_secs)
             self._store_queue.put(None)
             self._worker.join(timeout=5)
+        if getattr(self, "_put_queue", None) is not None:
+            try:
+                self._put_queue.drain()  # fence puts before the allocator goes away
+            except BaseException as e:
+                logger.warning("layerwise puts failed before close: %s", e)
         self._closed = True
         self.storage_manager.close()
         close = getattr(self.gpu_connector, "close", None)

@@ -32,6 +32,7 @@ from ...utils.metrics import get_stats
 from ...utils.nvtx import nvtx_range
 from ..kv_format import KVCacheFormat, PagedKVLayout
 from ..memory_management import MemoryFormat, MemoryObj
+from ..proxy_memory_obj import is_proxy, load_proxies_pipelined
 
 logger = init_logger(__name__)
 
@@ -222,6 +223,9 @@ class VLLMPagedMemGPUConnector(GPUConnectorInterface):
             return
         if slot_mapping is None:
             raise ValueError("slot_mapping is required")
+        if any(is_proxy(o) and not o.resolved for o in memory_objs):
+            self._load_proxies(memory_objs, starts, ends, slot_mapping)
+            return
         if self.device.type != "cuda":
             for obj, s, e in zip(memory_objs, starts, ends):
                 self.layout.scatter_ref(obj.tensor, slot_mapping[s:e])
@@ -249,6 +253,28 @@ class VLLMPagedMemGPUConnector(GPUConnectorInterface):
         if sync:
             self.load_stream.synchronize()
         self.stats.inc("to_gpu_bytes", sum(o.get_size() for o in memory_objs))
+
+    def _load_proxies(self, objs, starts, ends, slot_mapping) -> None:
+        """Chunks still on a peer: read them bank by bank into the transfer
+        context's bounce buffers and scatter each bank while the next one is
+        read (reference npu_connectors.py proxy ping-pong pipeline)."""
+        def scatter(batch, s, e):
+            self.batched_to_gpu(batch, s, e, slot_mapping, sync=False)
+            if self.device.type != "cuda":
+                return None
+            ev = torch.cuda.Event()
+            ev.record(self.load_stream)
+            return ev
+
+        plain = [i for i, o in enumerate(objs) if not is_proxy(o)]
+        if plain:
+            self.batched_to_gpu([objs[i] for i in plain], [starts[i] for i in plain],
+                                [ends[i] for i in plain], slot_mapping, sync=False)
+        px = [i for i, o in enumerate(objs) if is_proxy(o)]
+        load_proxies_pipelined([objs[i] for i in px], [starts[i] for i in px],
+                               [ends[i] for i in px], scatter)
+        if self.device.type == "cuda":
+            self.load_stream.synchronize()
 
     def _load_via_staging(self, objs, starts, ends, slots) -> None:
         max_bytes = max(o.get_size() for o in objs)

@@ -65,12 +65,18 @@ class StorageManager:
 
     # ---------------------------------------------------------------- puts
     def batched_put(self, keys: Sequence[CacheEngineKey], objs: Sequence[MemoryObj],
-                    transfer_spec=None, location: Optional[str] = None) -> None:
+                    transfer_spec=None, location: Optional[str] = None) -> list:
+        """Hand the chunks to every backend; returns the futures of the puts
+        that complete asynchronously."""
+        futs: list = []
         for name, b in self.backends.items():
             if location is not None and name != location:
                 continue
-            b.batched_submit_put_task(keys, objs, transfer_spec=transfer_spec)
+            r = b.batched_submit_put_task(keys, objs, transfer_spec=transfer_spec)
+            if r:
+                futs.extend(f for f in r if f is not None)
         self.stats.inc("stored_chunks", len(keys))
+        return futs
 
     def put(self, key: CacheEngineKey, obj: MemoryObj) -> None:
         self.batched_put([key], [obj])
