@@ -11,8 +11,10 @@ Cases (BASELINE shapes):
 * ``offload_store`` / ``offload_load``: the connector's store/retrieve of the
   same request to/from pinned host chunks (copy-engine pipeline and
   zero-copy kernel).
-* ``cachegen``: CDF + encode + decode of a Llama-3-8B 256-token chunk.
-* ``rope``: K re-rotation, 8192 tokens x 8 heads x 128.
+* ``cachegen``: quantise + CDF + encode + decode + dequantise of stacked
+  Llama-3-8B 256-token chunks (8-bit early / 4-bit late layers).
+* ``rope``: K re-rotation, 65536 tokens x 8 heads x 128.
+* ``c8``: DeepSeek-V3.2 indexer C8 cache <-> chunk packets, 61 layers.
 * ``push_loopback``: K9 on one GPU (Qwen3-32B TP4 shard, 16k tokens).
 """
 
@@ -35,7 +37,12 @@ def _peak_hbm() -> float:
         return 6650.0  # fallback figure of this pool
 
 
-def _time(fn, iters=10, warmup=3):
+_ITERS = {"iters": 10, "warmup": 3}
+
+
+def _time(fn, iters=None, warmup=None):
+    iters = _ITERS["iters"] if iters is None else iters
+    warmup = _ITERS["warmup"] if warmup is None else warmup
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -121,45 +128,109 @@ def bench_offload(small: bool):
 
 
 def bench_cachegen(small: bool):
-    from . import ops
+    """Llama-3-8B chunks (256 tokens x 32 layers x 8 heads x
+    128), bf16 N(0,1) x per-channel U(0.5, 2); 8-bit (256 bins) for the first
+    third of the layers, 4-bit (16 bins) after.  ``chunks`` chunks are stacked
+    as rows so every stage's input is larger than L2."""
+    from .ops import api
+    from .v1.cachegen import _group_order
 
-    mod = ops.native()
-    L, T, C = 64, 256, 1024  # K and V of 32 layers stacked, 8 heads x 128
-    bins = 32
-    sym = (torch.randn(L, T, C, device="cuda") * 4 + 16).clamp(0, bins - 1).to(torch.uint8)
-    cdf = mod.calculate_cdf(sym, bins)
-    ms = _time(lambda: mod.calculate_cdf(sym, bins))
-    _emit("cachegen_cdf", ms, sym.numel(), traffic_bytes=sym.numel())
-    cap = 512
-    out = torch.empty(L, C, cap, dtype=torch.uint8, device="cuda")
-    lens = torch.empty(L, C, dtype=torch.int32, device="cuda")
-    ms = _time(lambda: mod.encode_fast_new(cdf, sym, out, lens))
-    _emit("cachegen_encode", ms, sym.numel(), traffic_bytes=sym.numel() + int(lens.sum()),
-          symbols=sym.numel(), ratio=round(sym.numel() / int(lens.sum()), 3))
-    streams = torch.cat([out[l, c, :lens[l, c]] for l in range(2) for c in range(C)]) \
-        if small else None
-    flat = out.view(L * C, cap)
-    lens_flat = lens.view(-1)
-    idx = torch.arange(cap, device="cuda").unsqueeze(0) < lens_flat.unsqueeze(1)
-    streams = flat[idx]
-    cum = lens_flat.cumsum(0).to(torch.int32).view(L, C)
-    dec = torch.empty_like(sym)
-    ms = _time(lambda: mod.decode_fast_prefsum(cdf, streams, cum, dec))
-    assert torch.equal(dec, sym)
-    _emit("cachegen_decode", ms, sym.numel(), traffic_bytes=sym.numel() + streams.numel())
+    mod = api.native()
+    chunks = 4 if small else 8
+    L, T, C = 32, 256, 1024
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ch_scale = torch.rand(1, 1, C, device="cuda", generator=g) * 1.5 + 0.5
+    x = (torch.randn(chunks * 2 * L, T, C, device="cuda", generator=g) * ch_scale).to(
+        torch.bfloat16)
+    layer_bins = [256 if l < L // 3 else 16 for l in range(L)]
+    row_bins = (layer_bins * 2) * chunks
+    order, pos = _group_order(row_bins)
+    rb = torch.tensor(row_bins, dtype=torch.int32, device="cuda")
+    pos_t = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    kv_bytes = x.numel() * 2
+    n = x.numel()
+    sym = torch.empty(x.shape, dtype=torch.uint8, device="cuda")
+    scale = torch.empty(x.shape[:2], dtype=torch.float32, device="cuda")
+    ms = _time(lambda: mod.cachegen_quantize(x, rb, sym, scale, pos_t))
+    _emit("cachegen_quantize", ms, kv_bytes, traffic_bytes=kv_bytes + n, symbols=n)
+    slices, off = [], 0
+    for bins, rows in order:
+        slices.append((bins, sym[off:off + len(rows)]))
+        off += len(rows)
+    cdfs = [mod.calculate_cdf(sg, bins) for bins, sg in slices]
+    ms = _time(lambda: [mod.calculate_cdf(sg, bins) for bins, sg in slices])
+    _emit("cachegen_cdf", ms, kv_bytes, traffic_bytes=n, symbols=n)
+    cap = ((T * 12 + 7) // 8 + 4) // 4 * 4
+    outs = [torch.empty(sg.shape[0], C, cap, dtype=torch.uint8, device="cuda")
+            for _, sg in slices]
+    lens = [torch.empty(sg.shape[0], C, dtype=torch.int32, device="cuda") for _, sg in slices]
+    enc = lambda: [mod.encode_fast_new(cdf, sg, o, ln)
+                   for cdf, (_, sg), o, ln in zip(cdfs, slices, outs, lens)]
+    enc()
+    total = sum(int(ln.sum()) for ln in lens)
+    ms = _time(enc)
+    _emit("cachegen_encode", ms, kv_bytes, traffic_bytes=n + total, symbols=n,
+          bytes_out=total, ratio_vs_bf16=round(kv_bytes / total, 3))
+    streams, cums = [], []
+    for o, ln in zip(outs, lens):
+        flat = o.view(-1, cap)
+        mask = torch.arange(cap, device="cuda").unsqueeze(0) < ln.view(-1, 1)
+        streams.append(flat[mask])
+        cums.append(ln.view(-1).cumsum(0).to(torch.int32).view(ln.shape))
+    dsym = torch.empty_like(sym)
+    dslices, off = [], 0
+    for _, sg in slices:
+        dslices.append(dsym[off:off + sg.shape[0]])
+        off += sg.shape[0]
+    dec = lambda: [mod.decode_fast_prefsum(cdf, st, cu, d)
+                   for cdf, st, cu, d in zip(cdfs, streams, cums, dslices)]
+    ms = _time(dec)
+    assert torch.equal(dsym, sym)
+    _emit("cachegen_decode", ms, kv_bytes, traffic_bytes=n + total, symbols=n)
+    y = torch.empty_like(x)
+    ms = _time(lambda: mod.cachegen_dequantize(dsym, scale, rb, y, pos_t))
+    err = (y.float() - x.float())
+    _emit("cachegen_dequantize", ms, kv_bytes, traffic_bytes=kv_bytes + n,
+          max_abs_err=round(float(err.abs().max()), 4),
+          rel_rms_err=round(float(err.pow(2).mean().sqrt() / x.float().pow(2).mean().sqrt()), 4))
 
 
 def bench_rope(small: bool):
+    """K re-rotation (BASELINE config 5 pass: theta 10000, deltas 0-8192) on a
+    bf16 K of 65536 tokens x 8 heads x 128 (128 MiB, larger than L2)."""
     from . import ops
     from .ops.reference import make_cos_sin_cache
 
-    T, H, D = 8192, 8, 128
-    cache = make_cos_sin_cache(16384, D, 500000.0).cuda()
+    T, H, D = (8192 if small else 65536), 8, 128
+    cache = make_cos_sin_cache(65536 + 8192, D, 10000.0).cuda()
     k = torch.randn(T, H * D, device="cuda", dtype=torch.bfloat16)
-    old = torch.randint(0, 8192, (T,), device="cuda")
-    new = old + 100
+    old = torch.randint(0, 65536, (T,), device="cuda")
+    new = old + torch.randint(0, 8193, (T,), device="cuda")
     ms = _time(lambda: ops.native().rotary_embedding_k_fused(old, new, k, D, cache, True))
-    _emit("rope_delta", ms, k.numel() * 2)
+    _emit("rope_delta", ms, k.numel() * 2, tokens=T)
+
+
+def bench_c8(small: bool):
+    """Indexer C8 (DeepSeek-V3.2 lightning indexer: int8 keys 128 B/token +
+    fp16 scale) paged cache -> per-chunk device packets, 61 layers, 32k tokens."""
+    from .ops import api
+
+    L, T, chunk = 61, (8192 if small else 32768), 256
+    nb = 2 * T // 128
+    states = [api.IndexerC8State(
+        torch.randint(-128, 127, (nb, 128, 1, 128), dtype=torch.int8, device="cuda"),
+        torch.randn(nb, 128, 1, 1, device="cuda").half()) for _ in range(L)]
+    grp = api.IndexerC8GroupState(states)
+    g = torch.Generator().manual_seed(0)
+    t = torch.arange(T)
+    slots = (torch.randperm(nb, generator=g)[: T // 128][t // 128] * 128 + t % 128).int().cuda()
+    packets = [torch.empty(grp.packet_bytes(chunk), dtype=torch.uint8, device="cuda")
+               for _ in range(T // chunk)]
+    moved = grp.packet_bytes(T)
+    ms = _time(lambda: api.indexer_c8_transfer_prepared(grp, packets, slots, chunk, True))
+    _emit("indexer_c8_to_packets", ms, moved, tokens=T, layers=L)
+    ms = _time(lambda: api.indexer_c8_transfer_prepared(grp, packets, slots, chunk, False))
+    _emit("indexer_c8_from_packets", ms, moved, tokens=T, layers=L)
 
 
 def bench_push(small: bool):
@@ -189,14 +260,18 @@ def bench_push(small: bool):
 
 
 CASES = {"gather": bench_gather_scatter, "offload": bench_offload, "cachegen": bench_cachegen,
-         "rope": bench_rope, "push": bench_push}
+         "rope": bench_rope, "c8": bench_c8, "push": bench_push}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
     ap.add_argument("--small", action="store_true")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3,
+                    help="untimed launches per case (0 with --iters 1 for a profiler capture)")
     a = ap.parse_args()
+    _ITERS.update(iters=max(1, a.iters), warmup=max(0, a.warmup))
     for name, fn in CASES.items():
         if a.only and name not in a.only.split(","):
             continue

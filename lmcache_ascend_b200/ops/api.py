@@ -20,7 +20,7 @@ Ops here:
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import Tuple, List, Optional, Sequence
 
 import torch
 
@@ -151,6 +151,88 @@ def dense_mla_dsa_batched_direct_kv_transfer(chunks: Sequence[torch.Tensor], lay
     ptrs = torch.tensor([c.data_ptr() for c in chunks], dtype=torch.int64, device=layout.device)
     _xfer(layout, None, slot_mapping, direction, chunk_ptrs=ptrs, chunk_tokens=chunk_size,
           chunk_on_device=on_dev, mode=MODE_AUTO if on_dev else MODE_SIMT)
+
+
+class DirectTransferState:
+    """A fixed list of chunk objects with its device pointer table built once
+    (the process-owned state of the reference's ``_prepared`` direct entry
+    points, mem_kernels.cpp:1221-1307); reuse it across calls that move the
+    same chunks."""
+
+    def __init__(self, chunks: Sequence[torch.Tensor], layout, chunk_size: int):
+        if not chunks:
+            raise ValueError("direct transfer needs at least one chunk")
+        self.layout = layout
+        self.chunk_size = int(chunk_size)
+        self.chunks = list(chunks)
+        self.on_device = chunks[0].is_cuda
+        self.ptrs = torch.tensor([c.data_ptr() for c in chunks], dtype=torch.int64,
+                                 device=layout.device)
+
+
+_DIRECT_CACHE: "dict" = {}
+
+
+def dense_mla_dsa_batched_direct_kv_transfer_prepared(state: DirectTransferState,
+                                                      slot_mapping: torch.Tensor,
+                                                      direction: bool) -> None:
+    if state.layout.device.type != "cuda":
+        dense_mla_dsa_batched_direct_kv_transfer(state.chunks, state.layout, slot_mapping,
+                                                 state.chunk_size, direction)
+        return
+    _xfer(state.layout, None, slot_mapping, direction, chunk_ptrs=state.ptrs,
+          chunk_tokens=state.chunk_size, chunk_on_device=state.on_device,
+          mode=MODE_AUTO if state.on_device else MODE_SIMT)
+
+
+def dense_mla_dsa_batched_direct_kv_transfer_fast(chunks: Sequence[torch.Tensor], layout,
+                                                  slot_mapping: torch.Tensor, chunk_size: int,
+                                                  direction: bool) -> None:
+    """Like the batched direct transfer, with the pointer table cached per
+    (layout, chunk addresses) (reference ``_fast``: cached per-layer state)."""
+    key = (id(layout), chunk_size, tuple(c.data_ptr() for c in chunks))
+    st = _DIRECT_CACHE.get(key)
+    if st is None or st.layout is not layout:
+        if len(_DIRECT_CACHE) >= 256:
+            _DIRECT_CACHE.clear()
+        st = _DIRECT_CACHE[key] = DirectTransferState(chunks, layout, chunk_size)
+    dense_mla_dsa_batched_direct_kv_transfer_prepared(st, slot_mapping, direction)
+
+
+def dense_mla_dsa_group_direct_kv_transfer_fast(chunks: Sequence[torch.Tensor], group_layout,
+                                                slot_mapping: torch.Tensor, chunk_size: int,
+                                                direction: bool) -> None:
+    """Every layer of one layer group (a layout over the group's layers) in one
+    launch (reference dense_mla_dsa_group_direct_kv_transfer_fast)."""
+    dense_mla_dsa_batched_direct_kv_transfer_fast(chunks, group_layout, slot_mapping,
+                                                  chunk_size, direction)
+
+
+def mla_dsa_sparse_multi_chunk_kv_transfer(chunks: Sequence[torch.Tensor], layout,
+                                           slot_mapping_packed: torch.Tensor,
+                                           selected_token_idx: torch.Tensor,
+                                           chunk_size: int) -> None:
+    """paged[slot_mapping_packed[i]] = token selected_token_idx[i] of the chunk
+    sequence (token t in chunk t // chunk_size), all layers, straight from
+    pinned host or device chunks (reference mem_kernels.h:82-154 sparse
+    multi-chunk kernels)."""
+    if layout.device.type != "cuda":
+        full = torch.cat(list(chunks), dim=2)
+        rows = full.index_select(2, selected_token_idx.long().cpu())
+        layout.scatter_ref(rows, slot_mapping_packed)
+        return
+    on_dev = chunks[0].is_cuda
+    ptrs = torch.tensor([c.data_ptr() for c in chunks], dtype=torch.int64, device=layout.device)
+    idx = selected_token_idx.to(layout.device, slot_mapping_packed.dtype)
+    _xfer(layout, None, slot_mapping_packed.to(layout.device), False, chunk_ptrs=ptrs,
+          chunk_tokens=chunk_size, chunk_on_device=on_dev, chunk_idx=idx,
+          chunk_idx_limit=len(chunks) * chunk_size,
+          mode=MODE_AUTO if on_dev else MODE_SIMT)
+
+
+def multi_layer_kv_transfer_unilateral(*args, **kwargs):
+    raise NotImplementedError("multi_layer_kv_transfer_unilateral is not implemented "
+                              "(it is not in the reference either)")
 
 
 # ----------------------------------------------------------------- K5 / N7
@@ -349,6 +431,54 @@ def decode_fast_prefsum(cdf, bytestreams, lengths, output) -> None:
         native().decode_fast_prefsum(cdf, bytestreams, lengths, output)
         return
     output.copy_(R.decode_ref(cdf, bytestreams, lengths, output.shape[1]))
+
+
+def cachegen_quantize(x: torch.Tensor, bins: torch.Tensor,
+                      row_dst: Optional[torch.Tensor] = None
+                      ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """x [R, T, C] -> (symbols uint8 [R, T, C], scale fp32 [R, T]); symbol row r
+    lands at row ``row_dst[r]``.  half = bins // 2 - 1, scale = max|x| / half,
+    q = clamp(round(x / scale) + half, 0, 2 half) per (row, token)."""
+    R_, T, C = x.shape
+    if x.is_cuda:
+        sym = torch.empty(R_, T, C, dtype=torch.uint8, device=x.device)
+        scale = torch.empty(R_, T, dtype=torch.float32, device=x.device)
+        native().cachegen_quantize(x.contiguous(), bins.to(x.device, torch.int32), sym, scale,
+                                   None if row_dst is None
+                                   else row_dst.to(x.device, torch.int32))
+        return sym, scale
+    half = (bins // 2 - 1).view(-1, 1, 1).float()
+    amax = x.float().abs().amax(dim=-1, keepdim=True).clamp_min(1e-8)
+    sc = amax / half
+    q = torch.minimum((torch.round(x.float() / sc) + half).clamp_min(0), 2 * half)
+    q = q.to(torch.uint8)
+    if row_dst is not None:
+        out = torch.empty_like(q)
+        out[row_dst.long()] = q
+        q = out
+    return q, sc.squeeze(-1)
+
+
+def cachegen_dequantize(sym: torch.Tensor, scale: torch.Tensor, bins: torch.Tensor,
+                        dtype: torch.dtype, row_src: Optional[torch.Tensor] = None,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Inverse of :func:`cachegen_quantize`: y[r] = (sym[row_src[r]] - half) * scale[r]."""
+    R_, T = scale.shape
+    C = sym.shape[-1]
+    if sym.is_cuda:
+        y = out if out is not None else torch.empty(R_, T, C, dtype=dtype, device=sym.device)
+        native().cachegen_dequantize(sym.contiguous(), scale.contiguous().float(),
+                                     bins.to(sym.device, torch.int32), y,
+                                     None if row_src is None
+                                     else row_src.to(sym.device, torch.int32))
+        return y
+    src = sym if row_src is None else sym[row_src.long()]
+    half = (bins // 2 - 1).view(-1, 1, 1).float()
+    y = ((src.float() - half) * scale.float().unsqueeze(-1)).to(dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
 
 
 def decode_fast_new(*args, **kwargs):

@@ -1,4 +1,5 @@
-// K7: CacheGen entropy coding -- CDF construction, encode and decode.
+// K7: CacheGen quantisation and entropy coding -- quantise / dequantise,
+// CDF construction, encode and decode.
 //
 // Format (kept compatible with the reference's kernel tests,
 // tests/v1/test_cachegen_kernels.py, and its description in
@@ -23,21 +24,34 @@
 // (csrc/cachegen_kernels.cpp:64-107): stream byte lengths are given as an
 // inclusive prefix sum over the row-major (layer, channel) order and the
 // streams are concatenated in that order.
+//
+// Work decomposition (B200): a stream is inherently serial, so the kernels
+// keep one thread per (layer, channel) stream and keep everything else off
+// its critical path, with straight-line code so that the 32 lanes of a warp
+// (each at its own bit position) do not serialise on divergent branches.
+// Encode stages [64 tokens x CH channels] symbol tiles in shared memory with
+// 16-byte loads (double buffered: the next tile's loads are in flight while
+// the current one is coded) and emits 32-bit big-endian words.  Decode
+// resolves every code with one lookup in a per-channel 256-entry table
+// indexed by the window's top byte plus bit arithmetic for codes longer than
+// 8 bits, refilling the window once per two symbols from 16-byte loads issued
+// well ahead.  Shared tables are laid out [entry][channel] so that a warp's
+// lanes hit 32 different banks.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 
 namespace lmc {
 
 constexpr int kCgMaxBins = 256;
-constexpr int kCgChanPerBlock = 32;
+constexpr int kCgChan = 128;     // channels per histogram block
+constexpr int kCgTile = 64;      // tokens per encode shared-memory tile
+constexpr int kCgLut = 256;      // decode table entries (top 8 window bits): 32 KB per block
 
-// ---------------------------------------------------------------------------
-// Aligned CDF assignment for one channel (runs on one thread).
-//   counts[bins] -> start[bins], len[bins]
-// ---------------------------------------------------------------------------
 __host__ __device__ inline int cg_popcount(unsigned x) {
 #ifdef __CUDA_ARCH__
   return __popc(x);
@@ -52,15 +66,38 @@ __host__ __device__ inline int cg_log2(unsigned w) {  // w is a power of two
   return e;
 }
 
-__host__ __device__ inline void cdf_assign(const unsigned *counts, int bins,
-                                           unsigned short *out /* [bins+1] */) {
+__host__ __device__ inline int cg_log2_floor(unsigned v) {  // v >= 1
+#ifdef __CUDA_ARCH__
+  return 31 - __clz(v);
+#else
+  return 31 - __builtin_clz(v);
+#endif
+}
+
+__host__ __device__ inline int cg_msb64(unsigned long long v) {  // v >= 1
+#ifdef __CUDA_ARCH__
+  return 63 - __clzll(static_cast<long long>(v));
+#else
+  return 63 - __builtin_clzll(v);
+#endif
+}
+
+// ---------------------------------------------------------------------------
+// Aligned CDF assignment for one channel (runs on one thread).
+//   counts(s) -> count of symbol s; put(s, entry) stores CDF entry s.
+// Widths are powers of two >= 16 summing to 65536, each as close (in log2)
+// to the smoothed probability as the alignment of the running start allows,
+// with enough room left for the remaining symbols.
+// ---------------------------------------------------------------------------
+template <class Counts, class Put>
+__host__ __device__ inline void cdf_assign(Counts counts, int bins, Put put) {
   if (bins == 1) {
-    out[0] = 0;  // start 0, len 0: the only symbol costs no bits
-    out[1] = 0;
+    put(0, 0);  // start 0, len 0: the only symbol costs no bits
+    put(1, 0);
     return;
   }
   unsigned long long total = 0;
-  for (int s = 0; s < bins; ++s) total += counts[s];
+  for (int s = 0; s < bins; ++s) total += counts(s);
   // smoothed probability p_s = (2 c_s + 1) / (2 N + bins)
   const unsigned long long den = 2ull * total + static_cast<unsigned>(bins);
   unsigned pos = 0;
@@ -71,139 +108,277 @@ __host__ __device__ inline void cdf_assign(const unsigned *counts, int bins,
     if (k == 1) {
       w = R;
     } else {
-      // desired width: power of two nearest (linearly) to p * 65536
-      const unsigned long long x = (2ull * counts[s] + 1ull) * 65536ull;
-      unsigned wd = 16;
+      // desired width: the largest power of two wd in [16, 32768] with
+      // den * 2 wd <= x (a monotone condition: start from an msb estimate and
+      // step to it), then doubled when p * 65536 is nearer the next power
+      const unsigned long long x = (2ull * counts(s) + 1ull) * 65536ull;
+      int g = cg_msb64(x) - cg_msb64(den) - 1;
+      g = g < 4 ? 4 : (g > 15 ? 15 : g);
+      unsigned wd = 1u << g;
+      while (wd > 16u && den * (2ull * wd) > x) wd >>= 1;
       while (wd < 32768u && den * (2ull * wd) <= x) wd <<= 1;
       if (wd < 32768u && 2ull * x >= 3ull * den * wd) wd <<= 1;
       const int ed = cg_log2(wd);
       const unsigned maxw = pos == 0 ? 32768u : (pos & (~pos + 1u));
-      int best_e = -1, best_d = 1 << 30;
-      for (int e = 4; (1u << e) <= maxw; ++e) {
-        const unsigned cand = 1u << e;
-        if (cand >= R) break;
-        const unsigned rem = R - cand;
-        if (cg_popcount(rem) > k - 1) continue;
-        if (static_cast<unsigned>(k - 1) > rem / 16u) continue;
-        const int d = e > ed ? e - ed : ed - e;
-        if (d < best_d || (d == best_d && e > best_e)) {
-          best_d = d;
-          best_e = e;
+      // feasible widths 2^e: aligned at pos, leave room (a sum of at most k-1
+      // powers of two >= 16) for the remaining symbols.  Take the feasible e
+      // closest to ed, the larger one on a tie.
+      int best_e = -1;
+      if (k - 1 >= 16) {
+        // popcount(R - 2^e) <= 16 <= k - 1 always holds, so the feasible e
+        // are the interval [4, emax]: clamp ed into it
+        const long long room = static_cast<long long>(R) - 16ll * (k - 1);
+        if (room >= 16 && R >= 17) {
+          int emax = cg_log2_floor(maxw);
+          emax = min(emax, cg_log2_floor(R - 1));
+          emax = min(emax, cg_log2_floor(static_cast<unsigned>(room)));
+          emax = min(emax, 15);
+          if (emax >= 4) best_e = ed < 4 ? 4 : (ed > emax ? emax : ed);
+        }
+      } else {
+        auto feasible = [&](int e) {
+          if (e < 4 || e > 15) return false;
+          const unsigned cand = 1u << e;
+          if (cand > maxw || cand >= R) return false;
+          const unsigned rem = R - cand;
+          return cg_popcount(rem) <= k - 1 && static_cast<unsigned>(k - 1) <= rem / 16u;
+        };
+        for (int d = 0; d <= 11 && best_e < 0; ++d) {  // outward from ed
+          if (feasible(ed + d)) best_e = ed + d;
+          else if (d > 0 && feasible(ed - d)) best_e = ed - d;
         }
       }
       w = best_e >= 0 ? (1u << best_e) : 16u;  // unreachable fallback
     }
     const int len = 16 - cg_log2(w);
-    out[s] = static_cast<unsigned short>((pos & 0xFFF0u) | static_cast<unsigned>(len));
+    put(s, static_cast<unsigned short>((pos & 0xFFF0u) | static_cast<unsigned>(len)));
     pos += w;
   }
-  out[bins] = 0;  // stands for 0x10000
+  put(bins, 0);  // stands for 0x10000
 }
 
 // ---------------------------------------------------------------------------
-// calculate_cdf: block per (layer, 32-channel tile); histogram in shared mem.
+// calculate_cdf: block per (layer, 128-channel tile).  Each warp takes whole
+// token rows (lane = 4 consecutive channels, one 32-bit load); the shared
+// histogram column of channel c is (c / 4) + 32 * (c % 4), so the 32 lanes'
+// atomics of one step land in 32 different banks.
 // ---------------------------------------------------------------------------
-__global__ void cg_cdf_kernel(const uint8_t *__restrict__ in, int16_t *out,
-                              int L, int T, int C, int bins) {
-  extern __shared__ unsigned hist[];  // [32][bins]
+__device__ __forceinline__ int cg_hcol(int c) { return (c >> 2) | ((c & 3) << 5); }
+
+// Counters: 16-bit halves of 32-bit words, [bins / 2][kCgChan] words, when
+// T < 65536 (half the shared memory: 256 bins fit 3 blocks per SM); 32-bit
+// counters [bins][kCgChan] otherwise (kWide).
+template <bool kWide>
+__global__ void __launch_bounds__(256) cg_cdf_kernel(const uint8_t *__restrict__ in,
+                                                     int16_t *out, int L, int T, int C,
+                                                     int bins, bool vec4) {
+  extern __shared__ unsigned hist[];
   const int l = blockIdx.y;
-  const int c0 = blockIdx.x * kCgChanPerBlock;
-  const int nc = min(kCgChanPerBlock, C - c0);
-  for (int i = threadIdx.x; i < kCgChanPerBlock * bins; i += blockDim.x) hist[i] = 0;
+  const int c0 = blockIdx.x * kCgChan;
+  const int nc = min(kCgChan, C - c0);
+  const int words = (kWide ? bins : (bins + 1) >> 1) * kCgChan;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
   const uint8_t *base = in + static_cast<size_t>(l) * T * C + c0;
-  if (lane < nc) {
+  const int cl = lane * 4;
+  if (cl < nc) {
     for (int t = warp; t < T; t += nwarps) {
-      int s = base[static_cast<size_t>(t) * C + lane];
-      if (s >= bins) s = bins - 1;
-      atomicAdd(&hist[lane * bins + s], 1u);
+      const uint8_t *rp = base + static_cast<size_t>(t) * C + cl;
+      uint32_t v;
+      if (vec4) {
+        v = __ldg(reinterpret_cast<const uint32_t *>(rp));
+      } else {
+        v = 0;
+        for (int j = 0; j < 4 && cl + j < nc; ++j) v |= static_cast<uint32_t>(__ldg(rp + j)) << (8 * j);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (cl + j < nc) {
+          int s = (v >> (8 * j)) & 0xFF;
+          if (s >= bins) s = bins - 1;
+          if (kWide)
+            atomicAdd(&hist[s * kCgChan + cg_hcol(cl + j)], 1u);
+          else
+            atomicAdd(&hist[(s >> 1) * kCgChan + cg_hcol(cl + j)], 1u << ((s & 1) * 16));
+        }
+      }
     }
   }
   __syncthreads();
   if (threadIdx.x < nc) {
-    unsigned short tmp[kCgMaxBins + 1];
-    cdf_assign(&hist[threadIdx.x * bins], bins, tmp);
+    const int col = cg_hcol(threadIdx.x);
     int16_t *o = out + (static_cast<size_t>(l) * C + c0 + threadIdx.x) * (bins + 1);
-    for (int s = 0; s <= bins; ++s) o[s] = static_cast<int16_t>(tmp[s]);
+    cdf_assign(
+        [&](int s) {
+          return kWide ? hist[s * kCgChan + col]
+                       : (hist[(s >> 1) * kCgChan + col] >> ((s & 1) * 16)) & 0xFFFFu;
+        },
+        bins,
+               [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
   }
 }
 
 // ---------------------------------------------------------------------------
-// encode: one lane per (layer, channel) stream; lanes of a warp take 32
-// consecutive channels so symbol reads are coalesced.
+// encode: block per (layer, 128-channel tile), thread per stream.
 // ---------------------------------------------------------------------------
-__global__ void cg_encode_kernel(const int16_t *__restrict__ cdf,
-                                 const uint8_t *__restrict__ sym, uint8_t *out,
-                                 int32_t *out_len, int L, int T, int C, int bins,
-                                 int cap, DeviceStatus *status) {
-  extern __shared__ unsigned short tab[];  // [32][2][bins]: code, len
+__device__ __forceinline__ uint32_t cg_bswap(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
+
+// Append `n` bytes (the top bytes of big-endian word `w`) at op[nbytes..].
+__device__ __forceinline__ void cg_put_bytes(uint8_t *op, int nbytes, int cap, uint32_t w,
+                                             int n, bool &overflow) {
+  for (int j = 0; j < n; ++j) {
+    if (nbytes + j < cap)
+      op[nbytes + j] = static_cast<uint8_t>(w >> (24 - 8 * j));
+    else
+      overflow = true;
+  }
+}
+
+template <int CH>
+__global__ void __launch_bounds__(CH) cg_encode_kernel(
+    const int16_t *__restrict__ cdf, const uint8_t *__restrict__ sym, uint8_t *out,
+    int32_t *out_len, int L, int T, int C, int bins, int cap, bool vec16, bool word_out,
+    DeviceStatus *status) {
+  extern __shared__ __align__(16) uint8_t cg_smem[];
+  const int tab_words = ((bins + 1) >> 1) * CH;
+  uint32_t *tab = reinterpret_cast<uint32_t *>(cg_smem);  // (code << 4) | len, 0xF = invalid
+  uint8_t *tile = cg_smem + ((tab_words * 4 + 15) & ~15);  // [2][kCgTile][CH]
+  constexpr int kTileBytes = kCgTile * CH;
+  constexpr int kRowVecs = CH / 16;  // 16-byte vectors per tile row
   const int l = blockIdx.y;
-  const int c0 = blockIdx.x * kCgChanPerBlock;
-  const int lane = threadIdx.x;
-  const int nc = min(kCgChanPerBlock, C - c0);
-  // build code tables for the 32 channels (one channel per thread)
-  if (lane < nc) {
-    const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + lane) * (bins + 1);
-    unsigned short *code = tab + lane * 2 * bins;
-    unsigned short *len = code + bins;
+  const int c0 = blockIdx.x * CH;
+  const int tid = threadIdx.x;
+  const int nc = min(CH, C - c0);
+  if (tid < nc) {
+    const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
+    unsigned st = static_cast<unsigned short>(cd[0]) & 0xFFF0u;
     for (int s = 0; s < bins; ++s) {
-      const unsigned st = static_cast<unsigned short>(cd[s]) & 0xFFF0u;
       const unsigned en =
           (s + 1 == bins) ? 65536u : (static_cast<unsigned short>(cd[s + 1]) & 0xFFF0u);
       const unsigned w = en > st ? en - st : 0u;
-      if (w == 0) {
-        code[s] = 0;
-        len[s] = 0xFFFF;  // not encodable
-      } else {
-        int e = 31 - __clz(w);  // floor(log2 w)
-        const int ln = 16 - e;
-        len[s] = static_cast<unsigned short>(ln);
-        code[s] = static_cast<unsigned short>(ln == 0 ? 0 : (st >> (16 - ln)));
+      unsigned e = 0xFu;  // not encodable
+      if (w != 0) {
+        const int ln = 16 - (31 - __clz(w));  // 16 - floor(log2 w)
+        e = (static_cast<unsigned>(ln == 0 ? 0 : (st >> (16 - ln))) << 4) |
+            static_cast<unsigned>(ln);
       }
+      uint32_t &tw = tab[(s >> 1) * CH + tid];
+      tw = (s & 1) ? ((tw & 0xFFFFu) | (e << 16)) : ((tw & 0xFFFF0000u) | e);
+      st = en;
     }
   }
-  __syncwarp();
-  if (lane >= nc) return;
-  const unsigned short *code = tab + lane * 2 * bins;
-  const unsigned short *len = code + bins;
-  const int c = c0 + lane;
-  const uint8_t *sp = sym + static_cast<size_t>(l) * T * C + c;
+  const uint8_t *base = sym + static_cast<size_t>(l) * T * C + c0;
+  // tile loader: kCgTile * CH / 16 vectors per tile, 4 per thread
+  uint4 r[4];
+  auto gload = [&](int t0) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = tid + k * CH;
+      const int row = i / kRowVecs, vc = (i % kRowVecs) * 16;
+      const int t = t0 + row;
+      r[k] = (t < T && vc < nc)
+                 ? __ldg(reinterpret_cast<const uint4 *>(base + static_cast<size_t>(t) * C + vc))
+                 : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto sstore = [&](int b) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = tid + k * CH;
+      *reinterpret_cast<uint4 *>(tile + b * kTileBytes + (i / kRowVecs) * CH +
+                                 (i % kRowVecs) * 16) = r[k];
+    }
+  };
+  auto bload = [&](int b, int t0) {  // unaligned rows: byte loads straight into the tile
+    for (int i = tid; i < kTileBytes; i += CH) {
+      const int row = i / CH, c = i % CH;
+      const int t = t0 + row;
+      tile[b * kTileBytes + i] = (t < T && c < nc) ? __ldg(base + static_cast<size_t>(t) * C + c) : 0;
+    }
+  };
+  if (vec16) {
+    gload(0);
+    sstore(0);
+  } else {
+    bload(0, 0);
+  }
+  __syncthreads();
+
+  const int c = c0 + tid;
   uint8_t *op = out + (static_cast<size_t>(l) * C + c) * cap;
-  unsigned long long acc = 0;  // bits, MSB-first, `nb` valid bits at the top
+  uint32_t acc = 0;  // MSB-first, `nb` valid bits at the top, nb < 32
   int nb = 0;
   int nbytes = 0;
   bool overflow = false;
-  for (int t = 0; t < T; ++t) {
-    int s = sp[static_cast<size_t>(t) * C];
-    if (s >= bins) s = bins - 1;
-    const unsigned ln = len[s];
-    if (ln == 0xFFFF) {
-      report_status(status, kStatusBadIndex, l * C + c, t, s);
-      continue;
-    }
-    if (ln) {
-      acc |= static_cast<unsigned long long>(code[s]) << (64 - nb - ln);
-      nb += ln;
-    }
-    while (nb >= 8) {
-      if (nbytes < cap)
-        op[nbytes] = static_cast<uint8_t>(acc >> 56);
-      else
-        overflow = true;
-      ++nbytes;
-      acc <<= 8;
-      nb -= 8;
-    }
-  }
-  if (nb > 0) {
-    if (nbytes < cap)
-      op[nbytes] = static_cast<uint8_t>(acc >> 56);
+  auto emit = [&](uint32_t w) {
+    if (word_out && nbytes + 4 <= cap)
+      *reinterpret_cast<uint32_t *>(op + nbytes) = cg_bswap(w);
     else
-      overflow = true;
-    ++nbytes;
+      cg_put_bytes(op, nbytes, cap, w, 4, overflow);
+    nbytes += 4;
+  };
+  auto append = [&](unsigned e, int t) {
+    const int ln = static_cast<int>(e & 0xFu);
+    if (ln == 0xF) {
+      report_status(status, kStatusBadIndex, l * C + c, t, -1);
+      return;
+    }
+    if (ln == 0) return;
+    const uint32_t code = e >> 4;
+    const int tot = nb + ln;
+    if (tot < 32) {
+      acc |= code << (32 - tot);
+      nb = tot;
+    } else {
+      emit(acc | (code >> (tot - 32)));
+      nb = tot - 32;
+      acc = nb ? (code << (32 - nb)) : 0u;
+    }
+  };
+  auto entry = [&](int sym) {
+    const int q = sym >= bins ? bins - 1 : sym;
+    const uint32_t w = tab[(q >> 1) * CH + tid];
+    return (q & 1) ? (w >> 16) : (w & 0xFFFFu);
+  };
+  const int ntiles = (T + kCgTile - 1) / kCgTile;
+  for (int k = 0; k < ntiles; ++k) {
+    const int b = k & 1;
+    const bool more = k + 1 < ntiles;
+    if (more && vec16) gload((k + 1) * kCgTile);
+    if (tid < nc) {
+      const int rows = min(kCgTile, T - k * kCgTile);
+      const uint8_t *tp = tile + b * kTileBytes + tid;
+      constexpr int kCgChanT = CH;
+      const int t0 = k * kCgTile;
+      int row = 0;
+      for (; row + 4 <= rows; row += 4) {  // four independent lookups, then the chain
+        const unsigned e0 = entry(tp[(row + 0) * kCgChanT]);
+        const unsigned e1 = entry(tp[(row + 1) * kCgChanT]);
+        const unsigned e2 = entry(tp[(row + 2) * kCgChanT]);
+        const unsigned e3 = entry(tp[(row + 3) * kCgChanT]);
+        append(e0, t0 + row);
+        append(e1, t0 + row + 1);
+        append(e2, t0 + row + 2);
+        append(e3, t0 + row + 3);
+      }
+      for (; row < rows; ++row) append(entry(tp[row * kCgChanT]), t0 + row);
+    }
+    if (more) {
+      if (vec16)
+        sstore(b ^ 1);
+      else
+        bload(b ^ 1, (k + 1) * kCgTile);
+    }
+    __syncthreads();
+  }
+  if (tid >= nc) return;
+  if (nb > 0) {
+    const int n = (nb + 7) >> 3;
+    cg_put_bytes(op, nbytes, cap, acc, n, overflow);
+    nbytes += n;
   }
   if (overflow) {
     report_status(status, kStatusBadIndex, l * C + c, nbytes, cap);
@@ -213,64 +388,302 @@ __global__ void cg_encode_kernel(const int16_t *__restrict__ cdf,
 }
 
 // ---------------------------------------------------------------------------
-// decode (prefix-summed lengths): one lane per stream, binary search of the
-// 16-bit window in the channel's interval starts.
+// decode (prefix-summed lengths): block of 32 threads per (layer, 32-channel
+// tile), thread per stream.  Per-channel table lut[256] of 32-bit entries,
+// indexed by the window's top byte p, stored [p][32 channels] (one bank per
+// lane):
+//   bit 31 clear: one symbol covers every value with top byte p:
+//                 bits 0-7 symbol, 8-11 code length (<= 8);
+//   bit 31 set:   several symbols start inside p's range (an interval narrower
+//                 than 256 is aligned to its width, so it starts and ends
+//                 inside one top-byte range, and its start is a multiple of
+//                 16): bits 0-7 the first of them, bits 8-23 a mask of their
+//                 start nibbles (bits 4-7 of the start).  The symbol is the
+//                 first plus the number of starts at or below the window's
+//                 nibble, minus one; its width is the gap to the next start.
+// The window is refilled once per two symbols (codes are at most 12 bits)
+// from a ring of three 16-byte loads, so a load is issued about eight refills
+// before its bits are needed; the same straight-line code runs on every lane.
 // ---------------------------------------------------------------------------
-__global__ void cg_decode_kernel(const int16_t *__restrict__ cdf,
-                                 const uint8_t *__restrict__ bytes,
-                                 const int32_t *__restrict__ cum_len,
-                                 uint8_t *out, int L, int T, int C, int bins) {
-  extern __shared__ unsigned short st_tab[];  // [32][bins] starts, [32][bins] lens
+constexpr int kDecCh = 32;
+
+// 16 bytes at `pos` (a multiple of 16 counted from the 16-aligned `abase`);
+// the buffer is the byte range [lo, hi), bytes outside it read as 0.
+__device__ __forceinline__ uint4 cg_fetch16(const uint8_t *abase, long long pos, long long lo,
+                                            long long hi) {
+  if (pos >= lo && pos + 16 <= hi) return __ldg(reinterpret_cast<const uint4 *>(abase + pos));
+  uint4 v = make_uint4(0, 0, 0, 0);
+  uint8_t *vb = reinterpret_cast<uint8_t *>(&v);
+  for (int j = 0; j < 16; ++j) {
+    const long long q = pos + j;
+    if (q >= lo && q < hi) vb[j] = __ldg(abase + q);
+  }
+  return v;
+}
+
+__device__ __forceinline__ uint32_t cg_word(const uint4 &v, int j) {
+  const uint32_t w = j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+  return cg_bswap(w);
+}
+
+__global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
+    const int16_t *__restrict__ cdf, const uint8_t *__restrict__ bytes,
+    const int32_t *__restrict__ cum_len, long long total_bytes, uint8_t *out, int L, int T,
+    int C, int bins) {
+  __shared__ uint32_t lut[kCgLut * kDecCh];
   const int l = blockIdx.y;
-  const int c0 = blockIdx.x * kCgChanPerBlock;
-  const int lane = threadIdx.x;
-  const int nc = min(kCgChanPerBlock, C - c0);
-  unsigned short *starts = st_tab + lane * bins;
-  unsigned short *lens = st_tab + kCgChanPerBlock * bins + lane * bins;
-  if (lane < nc) {
-    const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + lane) * (bins + 1);
-    for (int s = 0; s < bins; ++s) {
-      const unsigned short v = static_cast<unsigned short>(cd[s]);
-      starts[s] = v & 0xFFF0u;
-      lens[s] = v & 0xFu;
+  const int c0 = blockIdx.x * kDecCh;
+  const int tid = threadIdx.x;
+  if (c0 + tid >= C) return;  // no block-wide barrier below: every thread owns its column
+  const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
+  for (int p = 0; p < kCgLut; ++p) lut[p * kDecCh + tid] = 8u << 8;  // safe default
+  for (int s = 0; s < bins; ++s) {
+    const unsigned e = static_cast<unsigned short>(__ldg(cd + s));
+    const unsigned ln = e & 0xFu;
+    const unsigned st = e & 0xFFF0u;
+    if (ln <= 8) {
+      const unsigned en = min(65536u, st + (1u << (16 - ln)));
+      for (unsigned p = st >> 8; p < (en >> 8); ++p)
+        lut[p * kDecCh + tid] = (ln << 8) | static_cast<unsigned>(s);
+    } else {
+      uint32_t &w = lut[(st >> 8) * kDecCh + tid];
+      const uint32_t bit = 1u << (8 + ((st >> 4) & 0xFu));
+      w = (w & 0x80000000u) ? (w | bit) : (0x80000000u | bit | static_cast<unsigned>(s));
     }
   }
-  __syncwarp();
-  if (lane >= nc) return;
-  const int c = c0 + lane;
+  const int c = c0 + tid;
   const size_t idx = static_cast<size_t>(l) * C + c;
-  const int32_t b0 = idx == 0 ? 0 : cum_len[idx - 1];
-  const int32_t b1 = cum_len[idx];
-  const uint8_t *p = bytes + b0;
-  const int n = b1 - b0;
-  int rd = 0;                  // next byte to load
-  unsigned long long win = 0;  // MSB-aligned bit window
-  int nb = 0;
-  uint8_t *op = out + static_cast<size_t>(l) * T * C + c;
-  for (int t = 0; t < T; ++t) {
-    while (nb <= 56) {
-      const unsigned long long byte = rd < n ? __ldg(p + rd) : 0ull;
-      ++rd;
-      win |= byte << (56 - nb);
-      nb += 8;
+  const long long b0 = idx == 0 ? 0 : cum_len[idx - 1];
+  const uint8_t *abase =
+      reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(bytes) & ~uintptr_t(15));
+  const long long lo = bytes - abase;  // 0..15
+  const long long hi = lo + total_bytes;
+  const long long start = lo + b0;
+  long long pos = start & ~15ll;
+  uint4 A = cg_fetch16(abase, pos, lo, hi);
+  uint4 B = cg_fetch16(abase, pos + 16, lo, hi);
+  uint4 D = cg_fetch16(abase, pos + 32, lo, hi);
+  pos += 48;
+  int j = static_cast<int>((start - (start & ~15ll)) >> 2);  // next word of A
+  const int skip = static_cast<int>(start & 3) * 8;
+  unsigned long long win = static_cast<unsigned long long>(cg_word(A, j)) << 32;
+  win <<= skip;
+  int nb = 32 - skip;  // valid bits at the top of win
+  auto next_word = [&]() {
+    if (++j == 4) {
+      A = B;
+      B = D;
+      D = cg_fetch16(abase, pos, lo, hi);
+      pos += 16;
+      j = 0;
     }
+  };
+  next_word();
+  const uint32_t *my = lut + tid;
+  auto decode1 = [&]() -> unsigned {
     const unsigned v = static_cast<unsigned>(win >> 48);
-    // largest s with starts[s] <= v
-    int lo = 0, hi = bins - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (starts[mid] <= v) lo = mid; else hi = mid - 1;
+    const uint32_t e = my[(v >> 8) * kDecCh];
+    unsigned sym, ln;
+    if (!(e & 0x80000000u)) {
+      sym = e & 0xFFu;
+      ln = (e >> 8) & 0xFu;
+    } else {
+      const unsigned nib = (v >> 4) & 0xFu;
+      const unsigned m = (e >> 8) & 0xFFFFu;
+      const unsigned below = (m & ((2u << nib) - 1u)) | 1u;  // bit 0: the first symbol
+      const int cur = 31 - __clz(below);
+      const unsigned above = m & ~((2u << cur) - 1u);
+      const int nxt = above ? __ffs(above) - 1 : 16;
+      sym = (e & 0xFFu) + static_cast<unsigned>(__popc(below) - 1);
+      ln = 12u - static_cast<unsigned>(31 - __clz(static_cast<unsigned>(nxt - cur)));
     }
-    const int ln = lens[lo];
     win <<= ln;
-    nb -= ln;
-    op[static_cast<size_t>(t) * C] = static_cast<uint8_t>(lo);
+    nb -= static_cast<int>(ln);
+    return sym;
+  };
+  uint8_t *op = out + static_cast<size_t>(l) * T * C + c;
+  const size_t step = static_cast<size_t>(C);
+  int t = 0;
+  for (; t + 2 <= T; t += 2) {
+    if (nb <= 32) {  // two codes need at most 24 bits
+      win |= static_cast<unsigned long long>(cg_word(A, j)) << (32 - nb);
+      nb += 32;
+      next_word();
+    }
+    const unsigned s0 = decode1();
+    const unsigned s1 = decode1();
+    op[0] = static_cast<uint8_t>(s0);
+    op[step] = static_cast<uint8_t>(s1);
+    op += 2 * step;
+  }
+  if (t < T) {
+    if (nb <= 32) win |= static_cast<unsigned long long>(cg_word(A, j)) << (32 - nb);
+    op[0] = static_cast<uint8_t>(decode1());
   }
 }
 
 // ---------------------------------------------------------------------------
-// Host launchers (op names of the reference's pybind module).
+// quantise: x [R, T, C] (rows = K layers then V layers of a KV_2LTD chunk) ->
+// symbols [R, T, C] uint8 and scale [R, T] fp32, warp per (row, token):
+//   half = bins / 2 - 1, scale = max(amax |x|, 1e-8) / half,
+//   q = clamp(rint(x / scale) + half, 0, 2 half)
+// with IEEE round-to-nearest division, so it matches the PyTorch expression
+// bit for bit.  Symbol row r goes to row_dst[r] (grouping rows that share a
+// bin count), scales stay in source order.
+// dequantise is the inverse: y = (q - half) * scale, rounded to the dtype.
 // ---------------------------------------------------------------------------
+template <typename T> __device__ __forceinline__ float cg_to_f(T v);
+template <> __device__ __forceinline__ float cg_to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float cg_to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float cg_to_f<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <typename T> __device__ __forceinline__ T cg_from_f(float v);
+template <> __device__ __forceinline__ float cg_from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half cg_from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 cg_from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// rint(x / s) with the quotient rounded to nearest (IEEE), computed as x * (1/s)
+// and redone with the exact division only when the product lies within
+// 1e-6 relative of a rounding tie (k + 0.5): the product is within 2.5 ulp
+// (< 1e-6 relative) of the rounded quotient, so away from a tie both round to
+// the same integer.
+__device__ __forceinline__ float cg_rint_div(float x, float s, float r) {
+  float a = x * r;
+  const float frac = a - floorf(a);
+  if (fabsf(frac - 0.5f) <= fabsf(a) * 1e-6f) a = __fdiv_rn(x, s);
+  return rintf(a);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) cg_quantize_kernel(
+    const T *__restrict__ x, const int32_t *__restrict__ bins, const int32_t *__restrict__ row_dst,
+    uint8_t *__restrict__ sym, float *__restrict__ scale, int R, int Tn, int C, bool vec) {
+  constexpr int kV = 16 / sizeof(T);  // elements per 16-byte vector
+  constexpr int kKeep = 8;            // vectors per lane kept in registers between passes
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int nvec = C / kV;
+  const bool keep = vec && nvec <= 32 * kKeep;
+  for (long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       gw < static_cast<long long>(R) * Tn; gw += nwarps) {
+    const int r = static_cast<int>(gw / Tn), t = static_cast<int>(gw % Tn);
+    const T *row = x + (static_cast<size_t>(r) * Tn + t) * C;
+    float amax = 0.f;
+    uint4 held[kKeep];
+    if (keep) {
+#pragma unroll
+      for (int k = 0; k < kKeep; ++k) {
+        const int v = lane + 32 * k;
+        held[k] = v < nvec ? __ldg(reinterpret_cast<const uint4 *>(row) + v)
+                           : make_uint4(0, 0, 0, 0);
+        const T *e = reinterpret_cast<const T *>(&held[k]);
+#pragma unroll
+        for (int j = 0; j < kV; ++j) amax = fmaxf(amax, fabsf(cg_to_f(e[j])));
+      }
+    } else if (vec) {
+      for (int v = lane; v < nvec; v += 32) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(row) + v);
+        const T *e = reinterpret_cast<const T *>(&u);
+#pragma unroll
+        for (int j = 0; j < kV; ++j) amax = fmaxf(amax, fabsf(cg_to_f(e[j])));
+      }
+    } else {
+      for (int i = lane; i < C; i += 32) amax = fmaxf(amax, fabsf(cg_to_f(row[i])));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float half = static_cast<float>(bins[r] / 2 - 1);
+    const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), half);
+    const float rc = __frcp_rn(sc);
+    const float top = 2.f * half;
+    const int dr = row_dst ? row_dst[r] : r;
+    uint8_t *orow = sym + (static_cast<size_t>(dr) * Tn + t) * C;
+    auto q = [&](float f) {
+      const float v = cg_rint_div(f, sc, rc) + half;
+      return static_cast<uint8_t>(static_cast<int>(fminf(fmaxf(v, 0.f), top)));
+    };
+    auto put = [&](int v, const uint4 &u) {
+      const T *e = reinterpret_cast<const T *>(&u);
+      uint8_t b[kV];
+#pragma unroll
+      for (int j = 0; j < kV; ++j) b[j] = q(cg_to_f(e[j]));
+      if constexpr (kV == 8) {
+        *reinterpret_cast<uint2 *>(orow + v * kV) = *reinterpret_cast<const uint2 *>(b);
+      } else {
+        *reinterpret_cast<uint32_t *>(orow + v * kV) = *reinterpret_cast<const uint32_t *>(b);
+      }
+    };
+    if (keep) {
+#pragma unroll
+      for (int k = 0; k < kKeep; ++k) {
+        const int v = lane + 32 * k;
+        if (v < nvec) put(v, held[k]);
+      }
+    } else if (vec) {
+      for (int v = lane; v < nvec; v += 32) put(v, __ldg(reinterpret_cast<const uint4 *>(row) + v));
+    } else {
+      for (int i = lane; i < C; i += 32) orow[i] = q(cg_to_f(row[i]));
+    }
+    if (lane == 0) scale[static_cast<size_t>(r) * Tn + t] = sc;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) cg_dequantize_kernel(
+    const uint8_t *__restrict__ sym, const float *__restrict__ scale,
+    const int32_t *__restrict__ bins, const int32_t *__restrict__ row_src, T *__restrict__ y,
+    int R, int Tn, int C, bool vec) {
+  constexpr int kV = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       gw < static_cast<long long>(R) * Tn; gw += nwarps) {
+    const int r = static_cast<int>(gw / Tn), t = static_cast<int>(gw % Tn);
+    const float half = static_cast<float>(bins[r] / 2 - 1);
+    const float sc = scale[static_cast<size_t>(r) * Tn + t];
+    const int sr = row_src ? row_src[r] : r;
+    const uint8_t *irow = sym + (static_cast<size_t>(sr) * Tn + t) * C;
+    T *orow = y + (static_cast<size_t>(r) * Tn + t) * C;
+    if (vec) {
+      for (int v = lane; v < C / kV; v += 32) {
+        uint8_t b[kV];
+        if constexpr (kV == 8) {
+          *reinterpret_cast<uint2 *>(b) = *reinterpret_cast<const uint2 *>(irow + v * kV);
+        } else {
+          *reinterpret_cast<uint32_t *>(b) = *reinterpret_cast<const uint32_t *>(irow + v * kV);
+        }
+        uint4 u;
+        T *e = reinterpret_cast<T *>(&u);
+#pragma unroll
+        for (int j = 0; j < kV; ++j)
+          e[j] = cg_from_f<T>(__fmul_rn(static_cast<float>(b[j]) - half, sc));
+        reinterpret_cast<uint4 *>(orow)[v] = u;
+      }
+    } else {
+      for (int i = lane; i < C; i += 32)
+        orow[i] = cg_from_f<T>(__fmul_rn(static_cast<float>(irow[i]) - half, sc));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers (op names of the reference's pybind module, plus the fused
+// quantise / dequantise pair).
+// ---------------------------------------------------------------------------
+static bool cg_aligned(const void *p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+static void cg_smem_attr(const void *fn, size_t smem) {
+  if (smem > 48 * 1024) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+  }
+}
+
 at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
   TORCH_CHECK(input.is_cuda() && input.dim() == 3, "input: device [L, T, C]");
   TORCH_CHECK(input.scalar_type() == at::kByte || input.scalar_type() == at::kChar,
@@ -281,11 +694,21 @@ at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
   const c10::cuda::CUDAGuard guard(in.device());
   auto out = at::zeros({L, C, n_bins + 1}, in.options().dtype(at::kShort));
   if (L == 0 || C == 0) return out;
-  dim3 grid((C + kCgChanPerBlock - 1) / kCgChanPerBlock, L);
-  const size_t smem = sizeof(unsigned) * kCgChanPerBlock * n_bins;
-  cg_cdf_kernel<<<grid, 256, smem, at::cuda::getCurrentCUDAStream().stream()>>>(
-      reinterpret_cast<const uint8_t *>(in.data_ptr()), out.data_ptr<int16_t>(),
-      L, T, C, static_cast<int>(n_bins));
+  dim3 grid((C + kCgChan - 1) / kCgChan, L);
+  const bool wide = T >= 65536;
+  const size_t smem = sizeof(unsigned) * kCgChan * (wide ? n_bins : (n_bins + 1) / 2);
+  const bool vec4 = C % 4 == 0 && cg_aligned(in.data_ptr(), 4);
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  const auto *ip = reinterpret_cast<const uint8_t *>(in.data_ptr());
+  if (wide) {
+    cg_smem_attr(reinterpret_cast<const void *>(cg_cdf_kernel<true>), smem);
+    cg_cdf_kernel<true><<<grid, 256, smem, stream>>>(ip, out.data_ptr<int16_t>(), L, T, C,
+                                                    static_cast<int>(n_bins), vec4);
+  } else {
+    cg_smem_attr(reinterpret_cast<const void *>(cg_cdf_kernel<false>), smem);
+    cg_cdf_kernel<false><<<grid, 256, smem, stream>>>(ip, out.data_ptr<int16_t>(), L, T, C,
+                                                     static_cast<int>(n_bins), vec4);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -314,17 +737,29 @@ void encode_fast_new(const at::Tensor &cdf, const at::Tensor &input_sym,
   auto s = input_sym.contiguous();
   const c10::cuda::CUDAGuard guard(s.device());
   if (L == 0 || C == 0) return;
-  dim3 grid((C + kCgChanPerBlock - 1) / kCgChanPerBlock, L);
-  const size_t smem = sizeof(unsigned short) * kCgChanPerBlock * 2 * bins;
+  const int cap = static_cast<int>(output_buffer.size(2));
+  const bool vec16 = C % 16 == 0 && cg_aligned(s.data_ptr(), 16);
+  const bool word_out = cap % 4 == 0 && cg_aligned(output_buffer.data_ptr(), 4);
   DeviceStatus *st = status.has_value()
                          ? reinterpret_cast<DeviceStatus *>(status->data_ptr())
                          : nullptr;
-  cg_encode_kernel<<<grid, kCgChanPerBlock, smem,
-                     at::cuda::getCurrentCUDAStream().stream()>>>(
-      c.data_ptr<int16_t>(), reinterpret_cast<const uint8_t *>(s.data_ptr()),
-      reinterpret_cast<uint8_t *>(output_buffer.data_ptr()),
-      output_lengths.data_ptr<int32_t>(), L, T, C, bins,
-      static_cast<int>(output_buffer.size(2)), st);
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  auto launch = [&](auto ch) {
+    constexpr int CH = decltype(ch)::value;
+    dim3 grid((C + CH - 1) / CH, L);
+    const size_t tab = ((static_cast<size_t>(bins + 1) / 2) * CH * 4 + 15) & ~size_t(15);
+    const size_t smem = tab + 2 * kCgTile * CH;
+    cg_smem_attr(reinterpret_cast<const void *>(cg_encode_kernel<CH>), smem);
+    cg_encode_kernel<CH><<<grid, CH, smem, stream>>>(
+        c.data_ptr<int16_t>(), reinterpret_cast<const uint8_t *>(s.data_ptr()),
+        reinterpret_cast<uint8_t *>(output_buffer.data_ptr()),
+        output_lengths.data_ptr<int32_t>(), L, T, C, bins, cap, vec16, word_out, st);
+  };
+  // 32 channels per block for large code tables keeps several blocks per SM
+  if (bins > 64)
+    launch(std::integral_constant<int, 32>());
+  else
+    launch(std::integral_constant<int, 128>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -342,19 +777,116 @@ void decode_fast_prefsum(const at::Tensor &cdf, const at::Tensor &bytestreams,
                   lengths.scalar_type() == at::kInt,
               "decode: lengths must be int32 [L, C] (inclusive prefix sum)");
   TORCH_CHECK(output.is_contiguous(), "decode: output must be contiguous");
+  TORCH_CHECK(bytestreams.scalar_type() == at::kByte || bytestreams.scalar_type() == at::kChar,
+              "decode: bytestreams must be uint8");
   const int T = output.size(1);
   auto c = cdf.to(at::kShort).contiguous();
   auto b = bytestreams.contiguous();
   auto len = lengths.contiguous();
   const c10::cuda::CUDAGuard guard(c.device());
   if (L == 0 || C == 0 || T == 0) return;
-  dim3 grid((C + kCgChanPerBlock - 1) / kCgChanPerBlock, L);
-  const size_t smem = sizeof(unsigned short) * kCgChanPerBlock * 2 * bins;
-  cg_decode_kernel<<<grid, kCgChanPerBlock, smem,
-                     at::cuda::getCurrentCUDAStream().stream()>>>(
+  dim3 grid((C + kDecCh - 1) / kDecCh, L);
+  cg_decode_kernel<<<grid, kDecCh, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       c.data_ptr<int16_t>(), reinterpret_cast<const uint8_t *>(b.data_ptr()),
-      len.data_ptr<int32_t>(), reinterpret_cast<uint8_t *>(output.data_ptr()),
-      L, T, C, bins);
+      len.data_ptr<int32_t>(), static_cast<long long>(b.numel()),
+      reinterpret_cast<uint8_t *>(output.data_ptr()), L, T, C, bins);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static int cg_rows_grid(int64_t rows) {
+  int dev = 0, sms = 148;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t blocks = (rows + 7) / 8;  // 8 warps per block
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, sms * 16)));
+}
+
+// x [R, T, C] float -> sym [R, T, C] uint8 (row r written at row_dst[r]),
+// scale [R, T] fp32.
+void cachegen_quantize(const at::Tensor &x, const at::Tensor &bins, at::Tensor &sym,
+                       at::Tensor &scale, const c10::optional<at::Tensor> &row_dst) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 3 && x.is_contiguous(), "quantize: x device [R, T, C]");
+  const int R = x.size(0), Tn = x.size(1), C = x.size(2);
+  TORCH_CHECK(bins.is_cuda() && bins.scalar_type() == at::kInt && bins.numel() == R,
+              "quantize: bins int32 [R] on the device");
+  TORCH_CHECK(sym.is_cuda() && sym.scalar_type() == at::kByte && sym.is_contiguous() &&
+                  sym.numel() == x.numel(),
+              "quantize: sym uint8 [R, T, C]");
+  TORCH_CHECK(scale.is_cuda() && scale.scalar_type() == at::kFloat && scale.is_contiguous() &&
+                  scale.numel() == static_cast<int64_t>(R) * Tn,
+              "quantize: scale fp32 [R, T]");
+  const int32_t *rd = nullptr;
+  if (row_dst.has_value()) {
+    TORCH_CHECK(row_dst->is_cuda() && row_dst->scalar_type() == at::kInt &&
+                    row_dst->numel() == R,
+                "quantize: row_dst int32 [R]");
+    rd = row_dst->data_ptr<int32_t>();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (x.numel() == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  const int grid = cg_rows_grid(static_cast<int64_t>(R) * Tn);
+  const int kV = 16 / static_cast<int>(x.element_size());
+  const bool vec = C % kV == 0 && cg_aligned(x.data_ptr(), 16) && cg_aligned(sym.data_ptr(), 8);
+  auto *sp = reinterpret_cast<uint8_t *>(sym.data_ptr());
+  if (x.scalar_type() == at::kBFloat16) {
+    cg_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(x.data_ptr()), bins.data_ptr<int32_t>(), rd, sp,
+        scale.data_ptr<float>(), R, Tn, C, vec);
+  } else if (x.scalar_type() == at::kHalf) {
+    cg_quantize_kernel<__half><<<grid, 256, 0, stream>>>(
+        reinterpret_cast<const __half *>(x.data_ptr()), bins.data_ptr<int32_t>(), rd, sp,
+        scale.data_ptr<float>(), R, Tn, C, vec);
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kFloat, "quantize: bf16, fp16 or fp32 input");
+    cg_quantize_kernel<float><<<grid, 256, 0, stream>>>(
+        x.data_ptr<float>(), bins.data_ptr<int32_t>(), rd, sp, scale.data_ptr<float>(), R, Tn,
+        C, vec);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// sym (row r read from row_src[r]) + scale [R, T] -> y [R, T, C] in y's dtype.
+void cachegen_dequantize(const at::Tensor &sym, const at::Tensor &scale, const at::Tensor &bins,
+                         at::Tensor &y, const c10::optional<at::Tensor> &row_src) {
+  TORCH_CHECK(y.is_cuda() && y.dim() == 3 && y.is_contiguous(), "dequantize: y device [R, T, C]");
+  const int R = y.size(0), Tn = y.size(1), C = y.size(2);
+  TORCH_CHECK(sym.is_cuda() && sym.scalar_type() == at::kByte && sym.is_contiguous() &&
+                  sym.numel() == y.numel(),
+              "dequantize: sym uint8 [R, T, C]");
+  TORCH_CHECK(scale.is_cuda() && scale.scalar_type() == at::kFloat && scale.is_contiguous() &&
+                  scale.numel() == static_cast<int64_t>(R) * Tn,
+              "dequantize: scale fp32 [R, T]");
+  TORCH_CHECK(bins.is_cuda() && bins.scalar_type() == at::kInt && bins.numel() == R,
+              "dequantize: bins int32 [R]");
+  const int32_t *rs = nullptr;
+  if (row_src.has_value()) {
+    TORCH_CHECK(row_src->is_cuda() && row_src->scalar_type() == at::kInt &&
+                    row_src->numel() == R,
+                "dequantize: row_src int32 [R]");
+    rs = row_src->data_ptr<int32_t>();
+  }
+  const c10::cuda::CUDAGuard guard(y.device());
+  if (y.numel() == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  const int grid = cg_rows_grid(static_cast<int64_t>(R) * Tn);
+  const int kV = 16 / static_cast<int>(y.element_size());
+  const bool vec = C % kV == 0 && cg_aligned(y.data_ptr(), 16) && cg_aligned(sym.data_ptr(), 8);
+  const auto *sp = reinterpret_cast<const uint8_t *>(sym.data_ptr());
+  if (y.scalar_type() == at::kBFloat16) {
+    cg_dequantize_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        sp, scale.data_ptr<float>(), bins.data_ptr<int32_t>(), rs,
+        reinterpret_cast<__nv_bfloat16 *>(y.data_ptr()), R, Tn, C, vec);
+  } else if (y.scalar_type() == at::kHalf) {
+    cg_dequantize_kernel<__half><<<grid, 256, 0, stream>>>(
+        sp, scale.data_ptr<float>(), bins.data_ptr<int32_t>(), rs,
+        reinterpret_cast<__half *>(y.data_ptr()), R, Tn, C, vec);
+  } else {
+    TORCH_CHECK(y.scalar_type() == at::kFloat, "dequantize: bf16, fp16 or fp32 output");
+    cg_dequantize_kernel<float><<<grid, 256, 0, stream>>>(
+        sp, scale.data_ptr<float>(), bins.data_ptr<int32_t>(), rs, y.data_ptr<float>(), R, Tn,
+        C, vec);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

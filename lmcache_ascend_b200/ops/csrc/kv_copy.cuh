@@ -39,13 +39,28 @@ struct CopyJob {
   // destination is dst_paged at dst_slots[t] instead of the chunk view.
   PagedDesc dst_paged;
   const void *dst_slots;
+  // Planes moved by this launch (bit p = plane p); 0 = every plane.  Lets one
+  // transfer run its 16-byte-aligned planes on the TMA engine and the others
+  // (e.g. 2-byte scale rows) on the SIMT engine.
+  uint32_t plane_mask;
 };
+
+__device__ __forceinline__ bool plane_selected(const CopyJob &j, int p) {
+  return j.plane_mask == 0 || ((j.plane_mask >> p) & 1u);
+}
 
 // Effective token count (reads the device-side count when present).
 __device__ __forceinline__ int effective_tokens(const CopyJob &j) {
   if (j.num_tokens_dev == nullptr) return j.num_tokens;
   const int n = *j.num_tokens_dev;
   return n < 0 ? 0 : (n < j.num_tokens ? n : j.num_tokens);
+}
+
+// Tokens of the chunk sequence a chunk-pointer table addresses: the slot count
+// for dense transfers, the index bound for sparse ones (the last chunk may be
+// partial, so its token count is derived from this total).
+__device__ __forceinline__ int chunk_seq_tokens(const CopyJob &j) {
+  return j.chunk_idx != nullptr ? static_cast<int>(j.chunk_idx_limit) : j.num_tokens;
 }
 
 __device__ __forceinline__ int64_t load_idx(const CopyJob &j, int t) {
@@ -111,7 +126,7 @@ __device__ __forceinline__ UnitMap make_unit_map(const CopyJob &j,
   UnitMap m;
   m.units_per_layer = 0;
   for (int p = 0; p < kMaxPlanes; ++p) {
-    if (p < j.paged.num_planes) {
+    if (p < j.paged.num_planes && plane_selected(j, p)) {
       int tt = stage_bytes / plane_of(j.paged, p).row_bytes;
       tt = tt > 64 ? 64 : (tt < 1 ? 1 : tt);
       m.tile[p] = tt;

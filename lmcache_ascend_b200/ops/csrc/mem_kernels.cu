@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(256)
   auto issue_loads = [&](int k) {
     const Unit u = decode_unit(j, m, gw + k * nw);
     const int s = k % stages;
-    const LaneRuns r = plan_runs(j, u, lane, j.num_tokens);
+    const LaneRuns r = plan_runs(j, u, lane, chunk_seq_tokens(j));
     const unsigned rb = plane_of(j.paged, u.plane).row_bytes;
     const unsigned total = warp_sum((r.len[0] + r.len[1]) * rb);
     if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256)
   auto issue_stores = [&](int k) {
     const Unit u = decode_unit(j, m, gw + k * nw);
     const int s = k % stages;
-    const LaneRuns r = plan_runs(j, u, lane, j.num_tokens);
+    const LaneRuns r = plan_runs(j, u, lane, chunk_seq_tokens(j));
     const unsigned rb = plane_of(j.paged, u.plane).row_bytes;
     unsigned char *buf = ring + static_cast<size_t>(s) * stage_bytes;
 #pragma unroll
@@ -109,6 +109,26 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
+// Planes chosen by the job's plane mask, without runtime-indexed arrays (which
+// would live in local memory).
+__device__ __forceinline__ int num_selected_planes(const CopyJob &j) {
+  int n = 0;
+#pragma unroll
+  for (int q = 0; q < kMaxPlanes; ++q) n += (q < j.paged.num_planes && plane_selected(j, q));
+  return n;
+}
+__device__ __forceinline__ int kth_selected_plane(const CopyJob &j, int k) {
+  int c = -1, p = 0;
+#pragma unroll
+  for (int q = 0; q < kMaxPlanes; ++q) {
+    if (q < j.paged.num_planes && plane_selected(j, q)) {
+      ++c;
+      if (c == k) p = q;
+    }
+  }
+  return p;
+}
+
 // SIMT engine: warp per (layer, plane, token) row, 16 B vectors when aligned.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void warp_copy_row(char *dst, const char *src,
@@ -147,13 +167,14 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
   const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x +
                           threadIdx.x) >> 5;
   const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
-  const long long rows = static_cast<long long>(j.num_layers) *
-                         j.paged.num_planes * j.num_tokens;
+  const int nsel = num_selected_planes(j);
+  const long long rows = static_cast<long long>(j.num_layers) * nsel * j.num_tokens;
   for (long long r = warp; r < rows; r += nwarps) {
     const int t = static_cast<int>(r % j.num_tokens);
     const long long lp = r / j.num_tokens;
-    const int p = static_cast<int>(lp % j.paged.num_planes);
-    const int l = static_cast<int>(lp / j.paged.num_planes);
+    const int k = static_cast<int>(lp % nsel);
+    const int p = kth_selected_plane(j, k);
+    const int l = static_cast<int>(lp / nsel);
     const int64_t slot = load_slot(j, t);
     if (slot < 0) continue;
     if (slot >= j.paged.num_slots) {
@@ -199,7 +220,7 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
       continue;
     }
     char *pa = paged_addr(j.paged, j.layer_begin + l, p, slot);
-    char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + l, p, ct, j.num_tokens);
+    char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + l, p, ct, chunk_seq_tokens(j));
     const PlaneDesc pl = plane_of(j.paged, p);
     const int rb = pl.row_bytes;
     if (pl.seg_bytes > 0 && pl.seg_bytes < rb) {
@@ -216,6 +237,59 @@ __global__ void __launch_bounds__(256) simt_rows_kernel(CopyJob j) {
     } else {
       warp_copy_row(pa, ca, rb, lane);
     }
+  }
+}
+
+// SIMT engine for rows of at most 16 bytes (fp16 scale planes and the like):
+// one thread per (layer, plane, token) row instead of one warp.
+__device__ __forceinline__ void thread_copy_small(char *dst, const char *src, int rb) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) |
+                      static_cast<uintptr_t>(rb);
+  if ((a & 7) == 0) {
+    for (int o = 0; o < rb; o += 8)
+      *reinterpret_cast<long long *>(dst + o) = *reinterpret_cast<const long long *>(src + o);
+  } else if ((a & 3) == 0) {
+    for (int o = 0; o < rb; o += 4)
+      *reinterpret_cast<int *>(dst + o) = *reinterpret_cast<const int *>(src + o);
+  } else if ((a & 1) == 0) {
+    for (int o = 0; o < rb; o += 2)
+      *reinterpret_cast<short *>(dst + o) = *reinterpret_cast<const short *>(src + o);
+  } else {
+    for (int o = 0; o < rb; ++o) dst[o] = src[o];
+  }
+}
+
+__global__ void __launch_bounds__(256) simt_small_rows_kernel(CopyJob j) {
+  j.num_tokens = effective_tokens(j);
+  if (j.num_tokens == 0) return;
+  const int nsel = num_selected_planes(j);
+  const long long rows = static_cast<long long>(j.num_layers) * nsel * j.num_tokens;
+  const long long nth = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long r = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; r < rows;
+       r += nth) {
+    const int t = static_cast<int>(r % j.num_tokens);
+    const long long lp = r / j.num_tokens;
+    const int k = static_cast<int>(lp % nsel);
+    const int p = kth_selected_plane(j, k);
+    const int l = static_cast<int>(lp / nsel);
+    const int64_t slot = load_slot(j, t);
+    if (slot < 0) continue;
+    if (slot >= j.paged.num_slots) {
+      report_status(j.status, kStatusBadSlot, t, slot, j.paged.num_slots);
+      continue;
+    }
+    const int64_t ct = load_idx(j, t);
+    if (ct < 0 || (j.chunk_idx != nullptr && ct >= j.chunk_idx_limit)) {
+      report_status(j.status, kStatusBadIndex, t, ct, j.chunk_idx_limit);
+      continue;
+    }
+    char *pa = paged_addr(j.paged, j.layer_begin + l, p, slot);
+    char *ca = chunk_addr(j.chunk, j.chunk_layer_begin + l, p, ct, chunk_seq_tokens(j));
+    const int rb = plane_of(j.paged, p).row_bytes;
+    if (j.to_chunk)
+      thread_copy_small(ca, pa, rb);
+    else
+      thread_copy_small(pa, ca, rb);
   }
 }
 
@@ -266,9 +340,11 @@ PagedLayout::PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
     desc_.plane[p].slot_stride = slot_stride[p];
     desc_.plane[p].row_bytes = static_cast<int32_t>(row_bytes[p]);
     TORCH_CHECK(row_bytes[p] > 0, "PagedLayout: row_bytes must be > 0");
-    if ((block_stride[p] | slot_stride[p] | row_bytes[p]) & 15) aligned16_ = false;
+    plane16_[p] = ((block_stride[p] | slot_stride[p] | row_bytes[p]) & 15) == 0;
+    if (!plane16_[p]) aligned16_ = false;
     if (p < static_cast<int>(seg_bytes.size()) && seg_bytes[p] > 0 &&
         seg_bytes[p] < row_bytes[p]) {
+      plane16_[p] = false;
       TORCH_CHECK(row_bytes[p] % seg_bytes[p] == 0 &&
                       p < static_cast<int>(seg_stride.size()),
                   "PagedLayout: row must be a whole number of segments");
@@ -331,6 +407,7 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
     }
     long long units = 0;
     for (int p = 0; p < j.paged.num_planes; ++p) {
+      if (j.plane_mask != 0 && !((j.plane_mask >> p) & 1u)) continue;
       int tt = sb / j.paged.plane[p].row_bytes;
       tt = std::min(64, std::max(1, tt));
       units += (j.num_tokens + tt - 1) / tt;
@@ -343,15 +420,27 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
     const unsigned long long budget_ns = 2000000000ull;  // 2 s
     tma_rows_kernel<<<grid, 32 * warps, smem, stream>>>(j, sb, stages, budget_ns);
   } else {
-    const long long rows = static_cast<long long>(j.num_layers) *
-                           j.paged.num_planes * j.num_tokens;
-    const long long warps_needed = rows;
+    int nsel = 0;
+    bool small = j.dst_slots == nullptr;
+    for (int p = 0; p < j.paged.num_planes; ++p) {
+      if (j.plane_mask != 0 && !((j.plane_mask >> p) & 1u)) continue;
+      ++nsel;
+      const PlaneDesc &pl = j.paged.plane[p];
+      if (pl.row_bytes > 16 || (pl.seg_bytes > 0 && pl.seg_bytes < pl.row_bytes)) small = false;
+    }
+    const long long rows = static_cast<long long>(j.num_layers) * nsel * j.num_tokens;
     const int threads = 256;
-    long long blocks = (warps_needed * 32 + threads - 1) / threads;
     const long long cap = static_cast<long long>(num_sms(device)) *
                           env_int("LMC_SIMT_BLOCKS_PER_SM", 8);
-    blocks = std::max(1LL, std::min(blocks, cap));
-    simt_rows_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(j);
+    if (small) {  // thread per row
+      long long blocks = (rows + threads - 1) / threads;
+      blocks = std::max(1LL, std::min(blocks, cap));
+      simt_small_rows_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(j);
+    } else {  // warp per row
+      long long blocks = (rows * 32 + threads - 1) / threads;
+      blocks = std::max(1LL, std::min(blocks, cap));
+      simt_rows_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(j);
+    }
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -397,10 +486,26 @@ void kv_transfer(const PagedLayout &paged, const c10::optional<at::Tensor> &chun
     chunk_on_device = chunk->is_cuda();
     if (reinterpret_cast<uintptr_t>(j.chunk.base) & 15) aligned = false;
   }
+  // Chunk-side alignment of plane p: layer and plane offsets scale with the
+  // chunk's token count, so check them at every count this launch uses (the
+  // full chunk and a partial last one), plus the per-token stride and column.
+  int64_t tcs[2] = {0, 0};
+  int ntc = 0;
+  if (chunk_ptrs.has_value()) {
+    const int64_t total = chunk_idx.has_value() ? chunk_idx_limit : slots.numel();
+    tcs[ntc++] = chunk_tokens;
+    if (total % chunk_tokens) tcs[ntc++] = total % chunk_tokens;
+  } else {
+    tcs[ntc++] = chunk_ntok;
+  }
+  auto chunk_plane_ok = [&](int p) {
+    if ((j.chunk.col_off[p] | j.chunk.token_stride[p]) & 15) return false;
+    for (int i = 0; i < ntc; ++i)
+      if (((j.chunk.layer_stride_t | j.chunk.plane_stride_t[p]) * tcs[i]) & 15) return false;
+    return true;
+  };
   for (int p = 0; p < j.paged.num_planes; ++p)
-    if ((j.chunk.plane_stride_t[p] | j.chunk.col_off[p] | j.chunk.token_stride[p]) & 15)
-      aligned = false;
-  if (j.chunk.layer_stride_t & 15) aligned = false;
+    if (!chunk_plane_ok(p)) aligned = false;
   j.slots = slots.data_ptr();
   j.slot_is_i64 = slots.scalar_type() == at::kLong;
   j.num_tokens = static_cast<int32_t>(slots.numel());
@@ -423,9 +528,28 @@ void kv_transfer(const PagedLayout &paged, const c10::optional<at::Tensor> &chun
                 "num_tokens_dev: device int32 tensor");
     j.num_tokens_dev = num_tokens_dev->data_ptr<int32_t>();
   }
-  launch_copy(j, chunk_on_device, aligned, mode,
-              at::cuda::getCurrentCUDAStream(slots.device().index()).stream(),
-              slots.device().index());
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream(slots.device().index()).stream();
+  const int dev = slots.device().index();
+  if (mode == 0 && chunk_on_device && !aligned) {
+    // split by plane: aligned planes on the TMA engine, the rest on SIMT
+    const bool base_ok = chunk_ptrs.has_value() ||
+                         (reinterpret_cast<uintptr_t>(j.chunk.base) & 15) == 0;
+    uint32_t tma_mask = 0, simt_mask = 0;
+    for (int p = 0; p < j.paged.num_planes; ++p) {
+      const bool ok = base_ok && paged.plane_aligned(p) && chunk_plane_ok(p);
+      (ok ? tma_mask : simt_mask) |= 1u << p;
+    }
+    if (tma_mask != 0 && simt_mask != 0) {
+      CopyJob a = j;
+      a.plane_mask = tma_mask;
+      launch_copy(a, true, true, 0, stream, dev);
+      CopyJob b = j;
+      b.plane_mask = simt_mask;
+      launch_copy(b, true, false, 2, stream, dev);
+      return;
+    }
+  }
+  launch_copy(j, chunk_on_device, aligned, mode, stream, dev);
 }
 
 // Adds `inc` to flags[layer_begin .. layer_begin + n) with release semantics

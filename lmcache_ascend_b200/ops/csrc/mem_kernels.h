@@ -25,6 +25,8 @@ class PagedLayout {
   const PagedDesc &desc() const { return desc_; }
   // TMA bulk copies need 16-byte aligned, contiguous rows on the paged side
   bool aligned() const { return aligned16_ && bases_aligned_ && !segmented_; }
+  // the same condition for one plane
+  bool plane_aligned(int p) const { return plane16_[p] && bases_aligned_; }
   void set_bases_aligned(bool v) { bases_aligned_ = v; }
   int64_t num_layers() const { return desc_.num_layers; }
   int64_t num_planes() const { return desc_.num_planes; }
@@ -34,6 +36,7 @@ class PagedLayout {
   at::Tensor ptrs_;
   PagedDesc desc_;
   bool aligned16_ = true;
+  bool plane16_[kMaxPlanes] = {false, false, false};
   bool bases_aligned_ = true;
   bool segmented_ = false;
 };

@@ -67,22 +67,113 @@ __global__ void rope_delta_kernel(const PT *__restrict__ old_pos,
   }
 }
 
+// Vector path: one warp per token (grid-stride); a unit is VE = 16 / sizeof(KT)
+// consecutive rotary dims of one head, moved with 16-byte loads and stores.
+// neox: the unit's first halves at [i0, i0 + VE) and partners at half + i0;
+// GPT-J: the unit holds VE / 2 adjacent (2p, 2p + 1) pairs.  Same arithmetic
+// as rope_delta_kernel, so both paths give identical results.
+template <typename KT, typename CT, typename PT, bool kNeox>
+__global__ void __launch_bounds__(256) rope_delta_vec_kernel(
+    const PT *__restrict__ old_pos, const PT *__restrict__ new_pos, KT *key,
+    const CT *__restrict__ cache, int num_tokens, int num_heads, int head_size, int rot_dim,
+    int64_t key_stride) {
+  constexpr int VE = 16 / sizeof(KT);
+  const int half = rot_dim / 2;
+  const int per_head = kNeox ? half / VE : rot_dim / VE;
+  const int units = num_heads * per_head;
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tokens; t += nw) {
+    const int64_t po = static_cast<int64_t>(old_pos[t]);
+    const int64_t pn = static_cast<int64_t>(new_pos[t]);
+    const CT *co = cache + po * rot_dim;
+    const CT *cn = cache + pn * rot_dim;
+    KT *kt = key + static_cast<int64_t>(t) * key_stride;
+    for (int u = lane; u < units; u += 32) {
+      const int h = u / per_head;
+      const int g = u - h * per_head;
+      KT *kh = kt + static_cast<int64_t>(h) * head_size;
+      if (kNeox) {
+        const int i0 = g * VE;
+        uint4 a = *reinterpret_cast<const uint4 *>(kh + i0);
+        uint4 b = *reinterpret_cast<const uint4 *>(kh + half + i0);
+        KT *x1 = reinterpret_cast<KT *>(&a);
+        KT *x2 = reinterpret_cast<KT *>(&b);
+#pragma unroll
+        for (int j = 0; j < VE; ++j) {
+          const int i = i0 + j;
+          const float ca = to_f(cn[i]), sa = to_f(cn[half + i]);
+          const float cb = to_f(co[i]), sb = to_f(co[half + i]);
+          const float cd = ca * cb + sa * sb;
+          const float sd = sa * cb - ca * sb;
+          const float v1 = to_f(x1[j]), v2 = to_f(x2[j]);
+          x1[j] = from_f<KT>(v1 * cd - v2 * sd);
+          x2[j] = from_f<KT>(v2 * cd + v1 * sd);
+        }
+        *reinterpret_cast<uint4 *>(kh + i0) = a;
+        *reinterpret_cast<uint4 *>(kh + half + i0) = b;
+      } else {
+        const int e0 = g * VE;
+        uint4 a = *reinterpret_cast<const uint4 *>(kh + e0);
+        KT *x = reinterpret_cast<KT *>(&a);
+#pragma unroll
+        for (int j = 0; j < VE / 2; ++j) {
+          const int i = e0 / 2 + j;
+          const float ca = to_f(cn[i]), sa = to_f(cn[half + i]);
+          const float cb = to_f(co[i]), sb = to_f(co[half + i]);
+          const float cd = ca * cb + sa * sb;
+          const float sd = sa * cb - ca * sb;
+          const float v1 = to_f(x[2 * j]), v2 = to_f(x[2 * j + 1]);
+          x[2 * j] = from_f<KT>(v1 * cd - v2 * sd);
+          x[2 * j + 1] = from_f<KT>(v2 * cd + v1 * sd);
+        }
+        *reinterpret_cast<uint4 *>(kh + e0) = a;
+      }
+    }
+  }
+}
+
+template <typename KT, typename CT, typename PT>
+static void launch_rope_t(const PT *op, const PT *np, at::Tensor &key, const at::Tensor &cache,
+                          int T, int H, int D, int rot, int64_t stride, bool neox,
+                          cudaStream_t s) {
+  constexpr int VE = 16 / sizeof(KT);
+  const int half = rot / 2;
+  const bool vec = (reinterpret_cast<uintptr_t>(key.data_ptr()) % 16 == 0) &&
+                   (stride * static_cast<int64_t>(sizeof(KT))) % 16 == 0 &&
+                   (D * static_cast<int>(sizeof(KT))) % 16 == 0 &&
+                   (neox ? half % VE == 0 : rot % VE == 0);
+  auto *kp = reinterpret_cast<KT *>(key.data_ptr());
+  const auto *cp = reinterpret_cast<const CT *>(cache.data_ptr());
+  if (vec) {
+    int dev = 0, sms = 148;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int blocks = std::max(1, std::min((T + 7) / 8, sms * 8));
+    if (neox)
+      rope_delta_vec_kernel<KT, CT, PT, true><<<blocks, 256, 0, s>>>(op, np, kp, cp, T, H, D,
+                                                                     rot, stride);
+    else
+      rope_delta_vec_kernel<KT, CT, PT, false><<<blocks, 256, 0, s>>>(op, np, kp, cp, T, H, D,
+                                                                      rot, stride);
+    return;
+  }
+  const int threads = std::min(1024, std::max(32, ((H * rot / 2) + 31) / 32 * 32));
+  const int blocks = std::min(T, 148 * 16);
+  rope_delta_kernel<KT, CT, PT><<<blocks, threads, 0, s>>>(op, np, kp, cp, T, H, D, rot, stride,
+                                                           neox);
+}
+
 template <typename KT, typename CT>
 static void launch_rope(const at::Tensor &op, const at::Tensor &np, at::Tensor &key,
                         const at::Tensor &cache, int T, int H, int D, int rot,
                         int64_t stride, bool neox, cudaStream_t s) {
-  const int threads = std::min(1024, std::max(32, ((H * rot / 2) + 31) / 32 * 32));
-  const int blocks = std::min(T, 148 * 16);
   if (op.scalar_type() == at::kLong)
-    rope_delta_kernel<KT, CT, int64_t><<<blocks, threads, 0, s>>>(
-        op.data_ptr<int64_t>(), np.data_ptr<int64_t>(),
-        reinterpret_cast<KT *>(key.data_ptr()),
-        reinterpret_cast<const CT *>(cache.data_ptr()), T, H, D, rot, stride, neox);
+    launch_rope_t<KT, CT, int64_t>(op.data_ptr<int64_t>(), np.data_ptr<int64_t>(), key, cache,
+                                   T, H, D, rot, stride, neox, s);
   else
-    rope_delta_kernel<KT, CT, int32_t><<<blocks, threads, 0, s>>>(
-        op.data_ptr<int32_t>(), np.data_ptr<int32_t>(),
-        reinterpret_cast<KT *>(key.data_ptr()),
-        reinterpret_cast<const CT *>(cache.data_ptr()), T, H, D, rot, stride, neox);
+    launch_rope_t<KT, CT, int32_t>(op.data_ptr<int32_t>(), np.data_ptr<int32_t>(), key, cache,
+                                   T, H, D, rot, stride, neox, s);
 }
 
 void rotary_embedding_k_fused(const at::Tensor &old_positions,

@@ -47,6 +47,10 @@ void encode_fast_new(const at::Tensor &cdf, const at::Tensor &input_sym,
 void decode_fast_prefsum(const at::Tensor &cdf, const at::Tensor &bytestreams,
                          const at::Tensor &lengths, at::Tensor &output);
 // pos_kernels.cu
+void cachegen_quantize(const at::Tensor &x, const at::Tensor &bins, at::Tensor &sym,
+                       at::Tensor &scale, const c10::optional<at::Tensor> &row_dst);
+void cachegen_dequantize(const at::Tensor &sym, const at::Tensor &scale, const at::Tensor &bins,
+                         at::Tensor &y, const c10::optional<at::Tensor> &row_src);
 void rotary_embedding_k_fused(const at::Tensor &old_positions,
                               const at::Tensor &new_positions, at::Tensor &key,
                               int64_t head_size, const at::Tensor &cos_sin_cache,
@@ -144,6 +148,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("output_buffer"), py::arg("output_lengths"),
         py::arg("status") = py::none());
   m.def("decode_fast_prefsum", &decode_fast_prefsum);
+  m.def("cachegen_quantize", &cachegen_quantize, py::arg("x"), py::arg("bins"), py::arg("sym"),
+        py::arg("scale"), py::arg("row_dst") = py::none());
+  m.def("cachegen_dequantize", &cachegen_dequantize, py::arg("sym"), py::arg("scale"),
+        py::arg("bins"), py::arg("y"), py::arg("row_src") = py::none());
   m.def("rotary_embedding_k_fused", &rotary_embedding_k_fused);
 
   m.def("layerwise_prefill_dma_copy", &dma_copy_batch);

@@ -69,19 +69,27 @@ class CacheGenConfig:
 
 def quantize(x: torch.Tensor, bins: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """x [L, T, C] float -> (symbols uint8 [L, T, C], scale fp32 [L, T]).
-    Symmetric: level = round(x / scale) + half, half = bins // 2 - 1."""
-    half = (bins // 2 - 1).to(x.device).view(-1, 1, 1).float()
-    amax = x.float().abs().amax(dim=-1, keepdim=True).clamp_min(1e-8)
-    scale = amax / half
-    q = torch.round(x.float() / scale) + half
-    q = torch.minimum(q.clamp_min(0), 2 * half)
-    return q.to(torch.uint8), scale.squeeze(-1)
+    Symmetric: level = round(x / scale) + half, half = bins // 2 - 1
+    (fused native kernel on CUDA tensors, the same PyTorch expression on CPU)."""
+    return api.cachegen_quantize(x, bins.to(torch.int32))
 
 
 def dequantize(sym: torch.Tensor, scale: torch.Tensor, bins: torch.Tensor,
                dtype: torch.dtype) -> torch.Tensor:
-    half = (bins // 2 - 1).to(sym.device).view(-1, 1, 1).float()
-    return ((sym.float() - half) * scale.unsqueeze(-1)).to(dtype)
+    return api.cachegen_dequantize(sym, scale, bins.to(torch.int32), dtype)
+
+
+def _group_order(row_bins: List[int]) -> Tuple[List[Tuple[int, List[int]]], List[int]]:
+    """Rows grouped by bin count (ascending) and, per source row, its position
+    in the grouped order."""
+    groups = [(b, [r for r, x in enumerate(row_bins) if x == b]) for b in sorted(set(row_bins))]
+    pos = [0] * len(row_bins)
+    i = 0
+    for _, rows in groups:
+        for r in rows:
+            pos[r] = i
+            i += 1
+    return groups, pos
 
 
 def cdf_from_lengths(lengths: torch.Tensor) -> torch.Tensor:
@@ -179,49 +187,60 @@ class CacheGenEncoded:
 
 
 def encode_kv(kv: torch.Tensor, config: CacheGenConfig) -> CacheGenEncoded:
-    """kv: KV_2LTD chunk [2, L, T, C] (device or host)."""
+    """kv: KV_2LTD chunk [2, L, T, C] (device or host).  One quantise launch
+    writes the symbols of rows sharing a bin count next to each other, so
+    every group's CDF and encode run on a contiguous slice."""
     _, L, T, C = kv.shape
     dev = kv.device
-    kb, vb = config.bins("k", dev), config.bins("v", dev)
-    ks, kscale = quantize(kv[0], kb)
-    vs, vscale = quantize(kv[1], vb)
-    sym = torch.cat([ks, vs], dim=0)                       # [2L, T, C]
-    row_bins = torch.cat([kb, vb]).cpu().tolist()
+    kb, vb = config.bins("k"), config.bins("v")
+    row_bins_t = torch.cat([kb, vb]).to(torch.int32)
+    row_bins = row_bins_t.tolist()
+    order, pos = _group_order(row_bins)
+    sym, scale = api.cachegen_quantize(kv.reshape(2 * L, T, C), row_bins_t.to(dev),
+                                       torch.tensor(pos, dtype=torch.int32, device=dev))
     groups = []
-    cap = (T * 12 + 7) // 8 + 1
-    for bins in sorted(set(row_bins)):
-        rows = [r for r, x in enumerate(row_bins) if x == bins]
-        sg = sym[rows].contiguous()
+    cap = ((T * 12 + 7) // 8 + 4) // 4 * 4
+    off = 0
+    for bins, rows in order:
+        sg = sym[off:off + len(rows)]
+        off += len(rows)
         cdf = api.calculate_cdf(sg, bins)
-        out = torch.zeros(len(rows), C, cap, dtype=torch.uint8, device=dev)
-        lens = torch.zeros(len(rows), C, dtype=torch.int32, device=dev)
+        out = torch.empty(len(rows), C, cap, dtype=torch.uint8, device=dev)
+        lens = torch.empty(len(rows), C, dtype=torch.int32, device=dev)
         api.encode_fast_new(cdf, sg, out, lens)
         mask = torch.arange(cap, device=dev).unsqueeze(0) < lens.view(-1, 1)
         streams = out.view(-1, cap)[mask].cpu().numpy().tobytes()
         code_len = (cdf[..., :bins].to(torch.int32) & 0xF).to(torch.uint8)
         groups.append(CacheGenGroup(rows, bins, code_len.cpu(), lens.cpu(), streams))
-    return CacheGenEncoded(L, T, C, kv.dtype, torch.cat([kscale, vscale]).float().cpu(),
-                           kb.cpu(), vb.cpu(), groups)
+    return CacheGenEncoded(L, T, C, kv.dtype, scale.float().cpu(), kb, vb, groups)
 
 
 def decode_kv(enc: CacheGenEncoded, device="cpu", out: Optional[torch.Tensor] = None
               ) -> torch.Tensor:
+    """Decode every group into its slice of the grouped symbol buffer, then one
+    dequantise launch writes the [2, L, T, C] chunk (into ``out`` when given)."""
     L, T, C = enc.num_layers, enc.num_tokens, enc.channels
     dev = torch.device(device)
-    sym = torch.zeros(2 * L, T, C, dtype=torch.uint8, device=dev)
+    sym = torch.empty(2 * L, T, C, dtype=torch.uint8, device=dev)
+    pos = [0] * (2 * L)
+    off = 0
     for g in enc.groups:
         cdf = cdf_from_lengths(g.code_lengths.to(dev))
         stream = torch.frombuffer(bytearray(g.streams), dtype=torch.uint8).to(dev) \
             if g.streams else torch.zeros(1, dtype=torch.uint8, device=dev)
         cum = g.lengths.view(-1).cumsum(0).to(torch.int32).view(len(g.rows), C).to(dev)
-        sg = torch.zeros(len(g.rows), T, C, dtype=torch.uint8, device=dev)
-        api.decode_fast_prefsum(cdf, stream, cum, sg)
-        sym[torch.tensor(g.rows, device=dev)] = sg
-    sc = enc.scales.to(dev)
-    k = dequantize(sym[:L], sc[:L], enc.k_bins, enc.dtype)
-    v = dequantize(sym[L:], sc[L:], enc.v_bins, enc.dtype)
-    res = torch.stack([k, v])
-    if out is not None:
+        api.decode_fast_prefsum(cdf, stream, cum, sym[off:off + len(g.rows)])
+        for i, r in enumerate(g.rows):
+            pos[r] = off + i
+        off += len(g.rows)
+    row_bins = torch.cat([enc.k_bins, enc.v_bins]).to(torch.int32)
+    src = torch.tensor(pos, dtype=torch.int32, device=dev)
+    direct = out is not None and out.is_contiguous() and out.dtype == enc.dtype and \
+        out.device == dev and out.dtype in (torch.float16, torch.bfloat16, torch.float32)
+    y = api.cachegen_dequantize(sym, enc.scales.to(dev), row_bins, enc.dtype, row_src=src,
+                                out=out.view(2 * L, T, C) if direct else None)
+    res = y.view(2, L, T, C)
+    if out is not None and not direct:
         out.copy_(res)
         return out
-    return res
+    return out if direct else res

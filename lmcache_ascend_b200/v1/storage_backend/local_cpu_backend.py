@@ -41,11 +41,19 @@ class LocalCPUBackend(StorageBackendInterface):
         self.store_objects = store_objects and config.local_cpu
         if allocator is None:
             nbytes = int(config.max_local_cpu_size * (1 << 30))
+            numa = config.numa_node
+            if numa == -2:  # auto: the current GPU's node, when the host reports one
+                import torch
+
+                from ...utils.system_detection import resolve_numa_node
+
+                dev = torch.cuda.current_device() if torch.cuda.is_available() else None
+                numa = resolve_numa_node(numa, dev)
             if config.shared_cpu_cache and config.shared_cpu_cache_name:
-                allocator = PinnedMemoryAllocator(nbytes, config.numa_node,
+                allocator = PinnedMemoryAllocator(nbytes, numa,
                                                   shm_name=config.shared_cpu_cache_name)
             else:
-                allocator = PinnedMemoryAllocator(nbytes, config.numa_node)
+                allocator = PinnedMemoryAllocator(nbytes, numa)
         self.allocator = allocator
         self.hot_cache: "OrderedDict[CacheEngineKey, MemoryObj]" = OrderedDict()
         self._lock = threading.RLock()

@@ -154,3 +154,74 @@ def test_gpu_encode_matches_cpu_bitstream():
     a, la = _encode(cdf, sym, cap, "cpu")
     b, lb = _encode(cdf, sym, cap, "cuda")
     assert torch.equal(la, lb) and torch.equal(a, b)
+
+
+def _torch_quantize(x, bins):
+    half = (bins // 2 - 1).view(-1, 1, 1).float()
+    amax = x.float().abs().amax(dim=-1, keepdim=True).clamp_min(1e-8)
+    sc = amax / half
+    q = torch.minimum((torch.round(x.float() / sc) + half).clamp_min(0), 2 * half)
+    return q.to(torch.uint8), sc.squeeze(-1)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("C", [1024, 100])
+def test_gpu_quantize_dequantize_match_torch(dtype, C):
+    from lmcache_ascend_b200.ops import api
+
+    g = torch.Generator().manual_seed(C)
+    R_, T = 6, 77
+    x = (torch.randn(R_, T, C, generator=g) * torch.rand(1, 1, C, generator=g) * 2).to(dtype)
+    bins = torch.tensor([32, 32, 16, 16, 256, 4], dtype=torch.int32)
+    want_q, want_s = _torch_quantize(x, bins)
+    perm = torch.tensor([3, 0, 5, 1, 4, 2], dtype=torch.int32)
+    q, s = api.cachegen_quantize(x.cuda(), bins.cuda(), perm.cuda())
+    assert torch.equal(s.cpu(), want_s)
+    assert torch.equal(q.cpu()[perm.long()], want_q)
+    y = api.cachegen_dequantize(q, s, bins.cuda(), dtype, row_src=perm.cuda())
+    half = (bins // 2 - 1).view(-1, 1, 1).float()
+    want_y = ((want_q.float() - half) * want_s.unsqueeze(-1)).to(dtype)
+    assert torch.equal(y.cpu(), want_y)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bins", [16, 32, 256])
+def test_gpu_codec_odd_shapes_and_misaligned_streams(bins):
+    # T not a multiple of the 64-token tile, C not a multiple of 16 or 128,
+    # cap not a multiple of 4, stream buffer starting 1 byte past an allocation
+    g = torch.Generator().manual_seed(bins + 1)
+    L, T, C = 2, 203, 150
+    x = torch.randn(L, T, C, generator=g) * (bins / 7) + bins / 2
+    sym = x.clamp(0, bins - 1).round().to(torch.uint8)
+    cdf = ops.native().calculate_cdf(sym.cuda(), bins).cpu()
+    assert torch.equal(cdf, R.calculate_cdf_ref(sym, bins))
+    cap = T * 12 // 8 + 3
+    a, la = _encode(cdf, sym, cap, "cpu")
+    b, lb = _encode(cdf, sym, cap, "cuda")
+    assert torch.equal(la, lb) and torch.equal(a, b)
+    streams = torch.cat([a[l, c, :la[l, c]] for l in range(L) for c in range(C)])
+    cum = la.view(-1).cumsum(0).to(torch.int32).view(L, C)
+    buf = torch.zeros(streams.numel() + 1, dtype=torch.uint8, device="cuda")
+    buf[1:] = streams.cuda()
+    out = torch.zeros(L, T, C, dtype=torch.uint8, device="cuda")
+    ops.native().decode_fast_prefsum(cdf.cuda(), buf[1:], cum.cuda(), out)
+    assert torch.equal(out.cpu(), sym)
+
+
+@pytest.mark.gpu
+def test_gpu_cachegen_kv_round_trip_matches_cpu():
+    from lmcache_ascend_b200.v1.cachegen import CacheGenConfig, decode_kv, encode_kv
+
+    g = torch.Generator().manual_seed(3)
+    L, T, C = 6, 256, 256
+    kv = (torch.randn(2, L, T, C, generator=g) *
+          (0.5 + 1.5 * torch.rand(1, 1, 1, C, generator=g))).to(torch.bfloat16)
+    cfg = CacheGenConfig.default(L)
+    e_cpu = encode_kv(kv, cfg)
+    e_gpu = encode_kv(kv.cuda(), cfg)
+    assert e_cpu.to_bytes() == e_gpu.to_bytes()
+    out = torch.empty(2, L, T, C, dtype=torch.bfloat16, device="cuda")
+    y = decode_kv(e_gpu, device="cuda", out=out)
+    assert y.data_ptr() == out.data_ptr()
+    assert torch.equal(y.cpu(), decode_kv(e_cpu))

@@ -86,6 +86,43 @@ def test_direct_multi_chunk(dev):
     assert torch.equal(torch.cat([c.to(dev) for c in chunks], dim=2), ref)
 
 
+@pytest.mark.parametrize("dev", _devs())
+def test_direct_fast_prepared_and_sparse_multi_chunk(dev):
+    kv = make_separate_kv(2, 64, 16, 2, 64, torch.bfloat16, dev, seed=9)
+    lay = PagedKVLayout(kv)
+    T, cs = 256, 128
+    slots = block_slots(T, 16, 64, seed=10, device=dev)
+    pin = dev == "cuda"
+    mk = lambda: [(lambda c: c.pin_memory() if pin else c)(
+        torch.zeros(lay.chunk_shape(cs), dtype=torch.bfloat16)) for _ in range(T // cs)]
+    ref = torch.zeros(lay.chunk_shape(T), dtype=torch.bfloat16, device=dev)
+    lay.gather_ref(ref, slots)
+    a, b = mk(), mk()
+    api.dense_mla_dsa_batched_direct_kv_transfer_fast(a, lay, slots, cs, True)
+    api.dense_mla_dsa_batched_direct_kv_transfer_fast(a, lay, slots, cs, True)  # cached state
+    st = api.DirectTransferState(b, lay, cs)
+    api.dense_mla_dsa_batched_direct_kv_transfer_prepared(st, slots, True)
+    if pin:
+        torch.cuda.synchronize()
+    for got in (a, b):
+        assert torch.equal(torch.cat([c.to(dev) for c in got], dim=2), ref)
+    # sparse multi-chunk: scatter 50 selected tokens of the chunk sequence
+    kv2 = [(torch.zeros_like(x), torch.zeros_like(y)) for x, y in kv]
+    lay2 = PagedKVLayout(kv2)
+    g = torch.Generator().manual_seed(11)
+    sel = torch.randperm(T, generator=g)[:50]
+    dst = random_slots(50, 64 * 16, seed=12, device=dev)
+    api.mla_dsa_sparse_multi_chunk_kv_transfer(a, lay2, dst, sel.to(dev), cs)
+    if pin:
+        torch.cuda.synchronize()
+    for layer in range(2):
+        for plane in range(2):
+            got = kv2[layer][plane].reshape(-1, 128)[dst.long()]
+            assert torch.equal(got.cpu(), ref[plane, layer][sel].cpu())
+    with pytest.raises(NotImplementedError):
+        api.multi_layer_kv_transfer_unilateral()
+
+
 @GPU
 def test_sparse_graph_capture_replay():
     kv = make_separate_kv(1, 64, 16, 4, 64, torch.bfloat16, "cuda", seed=9)

@@ -40,3 +40,28 @@ def test_fused_rope_gpu(head_size, neox, dtype, T):
     torch.cuda.synchronize()
     tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
     assert torch.allclose(kk.float().cpu(), ref, atol=tol * 4, rtol=tol)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("neox", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("rot", [128, 64])
+def test_fused_rope_vector_path_matches_scalar_path(neox, dtype, rot):
+    # the same keys once 16-byte aligned (vector kernel) and once shifted by
+    # one element (scalar kernel): results must be identical
+    T, H, D = 1000, 4, 128
+    cache = R.make_cos_sin_cache(4096, rot, base=10000.0).cuda()
+    k = torch.randn(T, H * D, device="cuda").to(dtype)
+    old = torch.randint(0, 2048, (T,), device="cuda")
+    new = old + torch.randint(0, 2048, (T,), device="cuda")
+    a = k.clone()
+    big = torch.zeros(T, H * D + 1, device="cuda", dtype=dtype)
+    big[:, 1:] = k
+    b = big[:, 1:]
+    ops.native().rotary_embedding_k_fused(old, new, a, D, cache, neox)
+    ops.native().rotary_embedding_k_fused(old, new, b, D, cache, neox)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    ref = R.rope_delta_ref(old.cpu(), new.cpu(), k.cpu(), D, cache.cpu(), neox)
+    tol = 1e-2 if dtype != torch.float32 else 1e-5
+    assert torch.allclose(a.float().cpu(), ref, atol=tol * 4, rtol=tol)
