@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--grid", type=int, default=0)
     ap.add_argument("--tile", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ttft", action="store_true",
+                    help="skip the TTFT-on-prefix-hit measurement (Qwen3-32B, 16k hit)")
+    ap.add_argument("--ttft-requests", type=int, default=8)
     return ap.parse_args()
 
 
@@ -343,6 +346,26 @@ def main():
             if e is not None:
                 e.close()
 
+    # ------------------------------------------------------ TTFT on a hit
+    # Second half of the headline metric: every rank serves a 16k-token
+    # prefix hit of Qwen3-32B (TP1, random init) from its own CPU tier
+    # through the engine API; p50 over requests, max over ranks.
+    ttft = None
+    if not a.no_ttft and a.impl == "ours":
+        for c in (src_cache, dst_cache):
+            if c is not None:
+                c.clear()
+        torch.cuda.empty_cache()
+        barrier()
+        from lmcache_ascend_b200.bench_ttft import run_ttft
+
+        ttft = run_ttft(dev, tokens=a.tokens, requests=a.ttft_requests, warmup=3)
+        p50 = torch.tensor([ttft["p50_ms"]], device=dev)
+        if world > 1:
+            dist.all_reduce(p50, op=dist.ReduceOp.MAX)
+        ttft["p50_ms_max_over_ranks"] = round(float(p50.item()), 3)
+        barrier()
+
     if rank == 0:
         per_pair = value / pairs
         if world == 1:
@@ -360,7 +383,7 @@ def main():
                      "random block tables)",
              "config": cfg, "bytes_per_pair_per_step": bytes_per_pair,
              "per_pair_gbps": round(per_pair, 2), "roofline": roof,
-             "clocks": ck, "e2e": e2e, "gpu_launches": launches})
+             "clocks": ck, "e2e": e2e, "gpu_launches": launches, "ttft": ttft})
     if sender is not None:
         sender.close()
     if world > 1:

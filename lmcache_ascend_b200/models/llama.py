@@ -53,9 +53,9 @@ class LlamaConfig:
 
 
 class RMSNorm(nn.Module):
-    def __init__(self, dim: int, eps: float):
+    def __init__(self, dim: int, eps: float, **fk):
         super().__init__()
-        self.weight = nn.Parameter(torch.ones(dim))
+        self.weight = nn.Parameter(torch.ones(dim, **fk))
         self.eps = eps
 
     def forward(self, x):
@@ -65,21 +65,21 @@ class RMSNorm(nn.Module):
 
 
 class DecoderLayer(nn.Module):
-    def __init__(self, c: LlamaConfig):
+    def __init__(self, c: LlamaConfig, **fk):
         super().__init__()
         self.c = c
         H, KH, D, E = c.num_heads, c.num_kv_heads, c.head_dim, c.hidden_size
-        self.input_layernorm = RMSNorm(E, c.rms_eps)
-        self.q_proj = nn.Linear(E, H * D, bias=False)
-        self.k_proj = nn.Linear(E, KH * D, bias=False)
-        self.v_proj = nn.Linear(E, KH * D, bias=False)
-        self.o_proj = nn.Linear(H * D, E, bias=False)
-        self.q_norm = RMSNorm(D, c.rms_eps) if c.qk_norm else None
-        self.k_norm = RMSNorm(D, c.rms_eps) if c.qk_norm else None
-        self.post_attention_layernorm = RMSNorm(E, c.rms_eps)
-        self.gate_proj = nn.Linear(E, c.intermediate_size, bias=False)
-        self.up_proj = nn.Linear(E, c.intermediate_size, bias=False)
-        self.down_proj = nn.Linear(c.intermediate_size, E, bias=False)
+        self.input_layernorm = RMSNorm(E, c.rms_eps, **fk)
+        self.q_proj = nn.Linear(E, H * D, bias=False, **fk)
+        self.k_proj = nn.Linear(E, KH * D, bias=False, **fk)
+        self.v_proj = nn.Linear(E, KH * D, bias=False, **fk)
+        self.o_proj = nn.Linear(H * D, E, bias=False, **fk)
+        self.q_norm = RMSNorm(D, c.rms_eps, **fk) if c.qk_norm else None
+        self.k_norm = RMSNorm(D, c.rms_eps, **fk) if c.qk_norm else None
+        self.post_attention_layernorm = RMSNorm(E, c.rms_eps, **fk)
+        self.gate_proj = nn.Linear(E, c.intermediate_size, bias=False, **fk)
+        self.up_proj = nn.Linear(E, c.intermediate_size, bias=False, **fk)
+        self.down_proj = nn.Linear(c.intermediate_size, E, bias=False, **fk)
 
     def qkv(self, hidden):
         c = self.c
@@ -98,17 +98,26 @@ class DecoderLayer(nn.Module):
 
 
 class LlamaForBlend(nn.Module):
-    def __init__(self, config: LlamaConfig, device="cpu", dtype=torch.float32, seed: int = 0):
+    def __init__(self, config: LlamaConfig, device="cpu", dtype=torch.float32, seed: int = 0,
+                 lm_head: bool = False):
+        """Parameters are created on ``device`` in ``dtype`` (a 32B model is
+        built on the GPU directly) and drawn from N(0, 0.05^2)."""
         super().__init__()
         torch.manual_seed(seed)
+        if torch.device(device).type == "cuda":
+            torch.cuda.manual_seed(seed)
+        fk = {"device": device, "dtype": dtype}
         self.config = config
-        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
-        self.layers = nn.ModuleList([DecoderLayer(config) for _ in range(config.num_layers)])
-        self.norm = RMSNorm(config.hidden_size, config.rms_eps)
-        for p in self.parameters():
-            if p.dim() == 2:
-                nn.init.normal_(p, std=0.05)
-        self.to(device=device, dtype=dtype)
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size, **fk)
+        self.layers = nn.ModuleList([DecoderLayer(config, **fk)
+                                     for _ in range(config.num_layers)])
+        self.norm = RMSNorm(config.hidden_size, config.rms_eps, **fk)
+        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False, **fk) \
+            if lm_head else None
+        with torch.no_grad():
+            for p in self.parameters():
+                if p.dim() == 2:
+                    p.normal_(0.0, 0.05)
         self.cos_sin_cache = make_cos_sin_cache(config.max_position, config.head_dim,
                                                 config.rope_theta).to(device)
         self.is_neox_style = True
@@ -164,6 +173,37 @@ class LlamaForBlend(nn.Module):
             self.write_kv(kv_caches[l], slot_mapping, k, v)
             h = layer.post(h, self.attend(q, k, v, pos, pos))
         return self.norm(h)
+
+    # ------------------------------------------------ decode on cached KV
+    @torch.no_grad()
+    def decode_step(self, token: torch.Tensor, position: int, kv_caches: List,
+                    ctx_slots: torch.Tensor, new_slot: torch.Tensor,
+                    before_layer=None) -> torch.Tensor:
+        """One token at ``position`` attending to the cached context (paged
+        slots ``ctx_slots`` of positions 0..position-1) and to itself; writes
+        its K/V at ``new_slot`` and returns the greedy next-token id (device
+        int64 [1]).  ``before_layer(l)`` runs before layer l reads its cache
+        (a layerwise KV load hooks in there)."""
+        c = self.config
+        h = self.embed_tokens(token.to(self.device).view(1))
+        pos = torch.full((1,), position, device=self.device, dtype=torch.long)
+        slots = torch.cat([ctx_slots.to(self.device).long(), new_slot.to(self.device).view(1).long()])
+        for l, layer in enumerate(self.layers):
+            if before_layer is not None:
+                before_layer(l)
+            q, k, v = layer.qkv(h)
+            q, k = self.rotary_emb(pos, q, k)
+            self.write_kv(kv_caches[l], new_slot.view(1), k, v)
+            kc, vc = kv_caches[l]
+            K = kc.view(-1, c.num_kv_heads, c.head_dim).index_select(0, slots)
+            V = vc.view(-1, c.num_kv_heads, c.head_dim).index_select(0, slots)
+            o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], K.transpose(0, 1)[None],
+                                               V.transpose(0, 1)[None], enable_gqa=True)
+            h = layer.post(h, o[0].transpose(0, 1).reshape(1, -1))
+        hs = self.norm(h)
+        if self.lm_head is None:
+            return hs
+        return self.lm_head(hs).argmax(dim=-1)
 
     # --------------------------------------------------- layerwise blending
     @torch.no_grad()

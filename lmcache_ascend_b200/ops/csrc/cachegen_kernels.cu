@@ -389,18 +389,21 @@ __global__ void __launch_bounds__(CH) cg_encode_kernel(
 
 // ---------------------------------------------------------------------------
 // decode (prefix-summed lengths): block of 32 threads per (layer, 32-channel
-// tile), thread per stream.  Per-channel table lut[256] of 32-bit entries,
-// indexed by the window's top byte p, stored [p][32 channels] (one bank per
-// lane):
-//   bit 31 clear: one symbol covers every value with top byte p:
+// tile), thread per stream.  Per-channel table lut[256] of 16-bit entries,
+// indexed by the window's top byte p and stored as [p / 2][32 channels]
+// words (one bank per lane):
+//   bit 15 clear: one symbol covers every value with top byte p:
 //                 bits 0-7 symbol, 8-11 code length (<= 8);
-//   bit 31 set:   several symbols start inside p's range (an interval narrower
+//   bit 15 set:   several symbols start inside p's range (an interval narrower
 //                 than 256 is aligned to its width, so it starts and ends
-//                 inside one top-byte range, and its start is a multiple of
-//                 16): bits 0-7 the first of them, bits 8-23 a mask of their
-//                 start nibbles (bits 4-7 of the start).  The symbol is the
+//                 inside one top-byte range and starts at a multiple of 16);
+//                 bits 0-7 index a per-channel pool record holding the first
+//                 of them (bits 0-7) and a mask of their start nibbles (bits
+//                 8-23, nibble = bits 4-7 of the start).  The symbol is the
 //                 first plus the number of starts at or below the window's
 //                 nibble, minus one; its width is the gap to the next start.
+// A multi-symbol range holds at least two symbols, so the pool needs at most
+// bins / 2 records: the table costs 512 + 2 * bins bytes per channel.
 // The window is refilled once per two symbols (codes are at most 12 bits)
 // from a ring of three 16-byte loads, so a load is issued about eight refills
 // before its bits are needed; the same straight-line code runs on every lane.
@@ -430,13 +433,26 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
     const int16_t *__restrict__ cdf, const uint8_t *__restrict__ bytes,
     const int32_t *__restrict__ cum_len, long long total_bytes, uint8_t *out, int L, int T,
     int C, int bins) {
-  __shared__ uint32_t lut[kCgLut * kDecCh];
+  extern __shared__ uint32_t cg_dsmem[];
+  uint32_t *lut = cg_dsmem;                     // [kCgLut / 2][kDecCh]
+  uint32_t *pool = cg_dsmem + (kCgLut / 2) * kDecCh;  // [max(1, bins / 2)][kDecCh]
   const int l = blockIdx.y;
   const int c0 = blockIdx.x * kDecCh;
   const int tid = threadIdx.x;
-  if (c0 + tid >= C) return;  // no block-wide barrier below: every thread owns its column
+  if (c0 + tid >= C) return;  // no block-wide barrier below: every thread owns its columns
+  const int pool_cap = max(1, bins / 2);
+  auto lget = [&](int p) {
+    const uint32_t w = lut[(p >> 1) * kDecCh + tid];
+    return (p & 1) ? (w >> 16) : (w & 0xFFFFu);
+  };
+  auto lset = [&](int p, unsigned v) {
+    uint32_t &w = lut[(p >> 1) * kDecCh + tid];
+    w = (p & 1) ? ((w & 0xFFFFu) | (v << 16)) : ((w & 0xFFFF0000u) | v);
+  };
   const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
-  for (int p = 0; p < kCgLut; ++p) lut[p * kDecCh + tid] = 8u << 8;  // safe default
+  const uint32_t dflt = (8u << 8) | ((8u << 8) << 16);  // safe default: symbol 0, 8 bits
+  for (int p = 0; p < kCgLut / 2; ++p) lut[p * kDecCh + tid] = dflt;
+  int used = 0;
   for (int s = 0; s < bins; ++s) {
     const unsigned e = static_cast<unsigned short>(__ldg(cd + s));
     const unsigned ln = e & 0xFu;
@@ -444,11 +460,18 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
     if (ln <= 8) {
       const unsigned en = min(65536u, st + (1u << (16 - ln)));
       for (unsigned p = st >> 8; p < (en >> 8); ++p)
-        lut[p * kDecCh + tid] = (ln << 8) | static_cast<unsigned>(s);
+        lset(static_cast<int>(p), (ln << 8) | static_cast<unsigned>(s));
     } else {
-      uint32_t &w = lut[(st >> 8) * kDecCh + tid];
+      const int p = static_cast<int>(st >> 8);
       const uint32_t bit = 1u << (8 + ((st >> 4) & 0xFu));
-      w = (w & 0x80000000u) ? (w | bit) : (0x80000000u | bit | static_cast<unsigned>(s));
+      const unsigned cur = lget(p);
+      if (cur & 0x8000u) {
+        pool[(cur & 0xFFu) * kDecCh + tid] |= bit;
+      } else if (used < pool_cap) {
+        pool[used * kDecCh + tid] = bit | static_cast<unsigned>(s);
+        lset(p, 0x8000u | static_cast<unsigned>(used));
+        ++used;
+      }
     }
   }
   const int c = c0 + tid;
@@ -482,12 +505,15 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
   const uint32_t *my = lut + tid;
   auto decode1 = [&]() -> unsigned {
     const unsigned v = static_cast<unsigned>(win >> 48);
-    const uint32_t e = my[(v >> 8) * kDecCh];
+    const unsigned p = v >> 8;
+    const uint32_t w = my[(p >> 1) * kDecCh];
+    const unsigned h = (p & 1) ? (w >> 16) : (w & 0xFFFFu);
     unsigned sym, ln;
-    if (!(e & 0x80000000u)) {
-      sym = e & 0xFFu;
-      ln = (e >> 8) & 0xFu;
+    if (!(h & 0x8000u)) {
+      sym = h & 0xFFu;
+      ln = (h >> 8) & 0xFu;
     } else {
+      const uint32_t e = pool[(h & 0xFFu) * kDecCh + tid];
       const unsigned nib = (v >> 4) & 0xFu;
       const unsigned m = (e >> 8) & 0xFFFFu;
       const unsigned below = (m & ((2u << nib) - 1u)) | 1u;  // bit 0: the first symbol
@@ -557,12 +583,11 @@ __device__ __forceinline__ float cg_rint_div(float x, float s, float r) {
   return rintf(a);
 }
 
-template <typename T>
+template <typename T, int kKeep>  // kKeep: vectors per lane kept in registers between passes
 __global__ void __launch_bounds__(256) cg_quantize_kernel(
     const T *__restrict__ x, const int32_t *__restrict__ bins, const int32_t *__restrict__ row_dst,
     uint8_t *__restrict__ sym, float *__restrict__ scale, int R, int Tn, int C, bool vec) {
   constexpr int kV = 16 / sizeof(T);  // elements per 16-byte vector
-  constexpr int kKeep = 8;            // vectors per lane kept in registers between passes
   const int lane = threadIdx.x & 31;
   const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const int nvec = C / kV;
@@ -786,7 +811,9 @@ void decode_fast_prefsum(const at::Tensor &cdf, const at::Tensor &bytestreams,
   const c10::cuda::CUDAGuard guard(c.device());
   if (L == 0 || C == 0 || T == 0) return;
   dim3 grid((C + kDecCh - 1) / kDecCh, L);
-  cg_decode_kernel<<<grid, kDecCh, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
+  const size_t smem = (kCgLut / 2 + std::max(1, bins / 2)) * kDecCh * 4;
+  cg_smem_attr(reinterpret_cast<const void *>(cg_decode_kernel), smem);
+  cg_decode_kernel<<<grid, kDecCh, smem, at::cuda::getCurrentCUDAStream().stream()>>>(
       c.data_ptr<int16_t>(), reinterpret_cast<const uint8_t *>(b.data_ptr()),
       len.data_ptr<int32_t>(), static_cast<long long>(b.numel()),
       reinterpret_cast<uint8_t *>(output.data_ptr()), L, T, C, bins);
@@ -829,19 +856,28 @@ void cachegen_quantize(const at::Tensor &x, const at::Tensor &bins, at::Tensor &
   const int kV = 16 / static_cast<int>(x.element_size());
   const bool vec = C % kV == 0 && cg_aligned(x.data_ptr(), 16) && cg_aligned(sym.data_ptr(), 8);
   auto *sp = reinterpret_cast<uint8_t *>(sym.data_ptr());
+  // hold the row in registers with as few as cover it (occupancy)
+  const bool four = C / kV <= 32 * 4;
+  auto go = [&](auto tag, auto keep) {
+    using T = decltype(tag);
+    constexpr int K = decltype(keep)::value;
+    cg_quantize_kernel<T, K><<<grid, 256, 0, stream>>>(
+        reinterpret_cast<const T *>(x.data_ptr()), bins.data_ptr<int32_t>(), rd, sp,
+        scale.data_ptr<float>(), R, Tn, C, vec);
+  };
+  auto by_keep = [&](auto tag) {
+    if (four)
+      go(tag, std::integral_constant<int, 4>());
+    else
+      go(tag, std::integral_constant<int, 8>());
+  };
   if (x.scalar_type() == at::kBFloat16) {
-    cg_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        reinterpret_cast<const __nv_bfloat16 *>(x.data_ptr()), bins.data_ptr<int32_t>(), rd, sp,
-        scale.data_ptr<float>(), R, Tn, C, vec);
+    by_keep(__nv_bfloat16());
   } else if (x.scalar_type() == at::kHalf) {
-    cg_quantize_kernel<__half><<<grid, 256, 0, stream>>>(
-        reinterpret_cast<const __half *>(x.data_ptr()), bins.data_ptr<int32_t>(), rd, sp,
-        scale.data_ptr<float>(), R, Tn, C, vec);
+    by_keep(__half());
   } else {
     TORCH_CHECK(x.scalar_type() == at::kFloat, "quantize: bf16, fp16 or fp32 input");
-    cg_quantize_kernel<float><<<grid, 256, 0, stream>>>(
-        x.data_ptr<float>(), bins.data_ptr<int32_t>(), rd, sp, scale.data_ptr<float>(), R, Tn,
-        C, vec);
+    by_keep(float());
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -31,13 +31,25 @@ void dma_copy_batch(const at::Tensor &dsts, const at::Tensor &srcs,
   const int64_t *dp = d.data_ptr<int64_t>(), *sp = s.data_ptr<int64_t>(),
                 *zp = z.data_ptr<int64_t>();
   cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-  for (int64_t i = 0; i < n; ++i) {
-    if (zp[i] <= 0) continue;
-    cudaError_t e = cudaMemcpyAsync(reinterpret_cast<void *>(dp[i]),
-                                    reinterpret_cast<const void *>(sp[i]),
-                                    static_cast<size_t>(zp[i]), cudaMemcpyDefault, st);
+  // entries that continue the previous one on both sides merge into one copy
+  // (per-layer chunk objects allocated back to back land in adjacent staging
+  // slots: a layer of a long prompt becomes one large DMA)
+  int64_t i = 0;
+  while (i < n) {
+    if (zp[i] <= 0) {
+      ++i;
+      continue;
+    }
+    const int64_t d0 = dp[i], s0 = sp[i];
+    int64_t len = zp[i];
+    int64_t j = i + 1;
+    while (j < n && zp[j] > 0 && dp[j] == d0 + len && sp[j] == s0 + len) len += zp[j++];
+    cudaError_t e = cudaMemcpyAsync(reinterpret_cast<void *>(d0),
+                                    reinterpret_cast<const void *>(s0),
+                                    static_cast<size_t>(len), cudaMemcpyDefault, st);
     TORCH_CHECK(e == cudaSuccess, "cudaMemcpyAsync failed at entry ", i, ": ",
                 cudaGetErrorString(e));
+    i = j;
   }
 }
 

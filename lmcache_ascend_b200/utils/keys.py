@@ -83,6 +83,10 @@ def get_hash_function(name: str) -> Callable[..., int]:
         raise ValueError(f"unknown hash function {name!r}; have {sorted(HASH_FUNCTIONS)}")
 
 
+_KEY_FIELDS = ("fmt", "model_name", "world_size", "worker_id", "chunk_hash", "dtype", "group",
+               "tags")
+
+
 @dataclass(frozen=True, order=True)
 class CacheEngineKey:
     fmt: str
@@ -93,6 +97,30 @@ class CacheEngineKey:
     dtype: str = "bfloat16"
     group: int = 0  # KV layer group (0 regular/latent, 1 DSA indexer)
     tags: Tuple[Tuple[str, str], ...] = field(default=(), compare=True)
+
+    # Keys are hashed on every dict access of every tier; the hash of the
+    # immutable fields is computed once (a 16k-token layerwise request touches
+    # thousands of keys).
+    def __hash__(self) -> int:
+        h = self.__dict__.get("_h")
+        if h is None:
+            h = hash(self._fields())
+            object.__setattr__(self, "_h", h)
+        return h
+
+    def _fields(self) -> tuple:
+        return (self.fmt, self.model_name, self.world_size, self.worker_id, self.chunk_hash,
+                self.dtype, self.group, self.tags)
+
+    # str hashes differ between processes: never ship the cached value
+    def __getstate__(self) -> dict:
+        d = dict(self.__dict__)
+        d.pop("_h", None)
+        return d
+
+    def __setstate__(self, d: dict) -> None:
+        for k, v in d.items():
+            object.__setattr__(self, k, v)
 
     def to_string(self) -> str:
         s = (f"{self.fmt}@{self.model_name}@{self.world_size}@{self.worker_id}"
@@ -123,10 +151,23 @@ class CacheEngineKey:
                               self.chunk_hash, self.dtype, self.group, self.tags)
 
     def split_layers(self, num_layers: int) -> List["LayerCacheEngineKey"]:
-        return [LayerCacheEngineKey(self.fmt, self.model_name, self.world_size,
-                                    self.worker_id, self.chunk_hash, self.dtype,
-                                    self.group, self.tags, layer_id=i)
-                for i in range(num_layers)]
+        # bypasses the frozen-dataclass __init__ (one object.__setattr__ per
+        # field): a layerwise request builds thousands of these
+        base = {f: self.__dict__[f] for f in _KEY_FIELDS}
+        out = []
+        for i in range(num_layers):
+            k = object.__new__(LayerCacheEngineKey)
+            d = k.__dict__
+            d.update(base)
+            d["layer_id"] = i
+            out.append(k)
+        return out
+
+    def layer_key(self, layer_id: int) -> "LayerCacheEngineKey":
+        k = object.__new__(LayerCacheEngineKey)
+        k.__dict__.update({f: self.__dict__[f] for f in _KEY_FIELDS})
+        k.__dict__["layer_id"] = layer_id
+        return k
 
     def __str__(self) -> str:  # pragma: no cover - debugging aid
         return self.to_string()
@@ -135,6 +176,13 @@ class CacheEngineKey:
 @dataclass(frozen=True, order=True)
 class LayerCacheEngineKey(CacheEngineKey):
     layer_id: int = 0
+
+    def __hash__(self) -> int:
+        h = self.__dict__.get("_h")
+        if h is None:
+            h = hash(self._fields() + (self.layer_id,))
+            object.__setattr__(self, "_h", h)
+        return h
 
     def to_string(self) -> str:
         return super().to_string() + f"@L{self.layer_id}"

@@ -344,7 +344,7 @@ class LMCacheEngine:
         which is written together with the others once the store finished."""
         if self.config.use_layerwise and getattr(self.gpu_connector, "layout", None) is not None:
             L = self.gpu_connector.layout.num_layers
-            return key.split_layers(L)[L - 1]
+            return key.layer_key(L - 1)
         return key
 
     def lookup_unpin(self, lookup_id: Any) -> None:
@@ -434,14 +434,16 @@ class LMCacheEngine:
         chunks = self._chunks(tokens, mask)
         per_layer: List[List[MemoryObj]] = []
         hit = 0
-        for s, e, k in chunks:
-            lkeys = k.split_layers(L)
-            objs = [self.storage_manager.get(lk) for lk in lkeys]
-            if any(o is None for o in objs):
+        # every layer key of every chunk in one batched get (chunk-major)
+        all_keys = [lk for _, _, k in chunks for lk in k.split_layers(L)]
+        got = self.storage_manager.batched_get(all_keys) if all_keys else []
+        for ci in range(len(chunks)):
+            objs = got[ci * L:(ci + 1) * L]
+            if hit < ci or any(o is None for o in objs):  # the hit prefix ended
                 for o in objs:
                     if o is not None:
                         o.ref_count_down()
-                break
+                continue
             if not per_layer:
                 per_layer = [[] for _ in range(L)]
             for layer, o in enumerate(objs):

@@ -117,7 +117,8 @@ class VLLMPagedMemGPUConnector(GPUConnectorInterface):
                      chunk_layer_begin: int = 0, mode: Optional[int] = None,
                      chunk_ntok: Optional[int] = None, tok_off: int = 0,
                      status=None, chunk_idx=None, chunk_idx_limit: int = 0,
-                     num_tokens_dev=None, layout: Optional[PagedKVLayout] = None) -> None:
+                     num_tokens_dev=None, layout: Optional[PagedKVLayout] = None,
+                     chunk_layout=None) -> None:
         from ... import ops
 
         lay = layout or self.layout
@@ -126,7 +127,8 @@ class VLLMPagedMemGPUConnector(GPUConnectorInterface):
             d = 2 if chunk.dim() == 4 else 0
             chunk_ntok = chunk.shape[d]
         ops.native().kv_transfer(
-            lay.native(), chunk, chunk_ptrs, lay.chunk_native(), chunk_ntok or 0, tok_off,
+            lay.native(), chunk, chunk_ptrs, chunk_layout or lay.chunk_native(), chunk_ntok or 0,
+            tok_off,
             chunk_tokens, chunk_on_device, slots, layer_begin, chunk_layer_begin, nl,
             to_chunk, self._mode() if mode is None else mode,
             status, chunk_idx, chunk_idx_limit, num_tokens_dev)
@@ -327,7 +329,30 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
             self._ll = ops.native().ChunkLayout(*params)
         return self._ll
 
-    def _xfer_layer(self, objs, starts, ends, slots, layer: int, to_chunk: bool) -> None:
+    def _layer_tables(self, objs_per_layer, starts, ends, stream):
+        """Device pointer tables [L, chunks] of every layer's chunk objects,
+        uploaded with one copy on ``stream`` (the stream that reads them), when
+        the chunks tile the token range (all full except the last): each layer
+        then moves in one launch."""
+        if self.device.type != "cuda" or not objs_per_layer or not objs_per_layer[0]:
+            return None
+        if not self._contiguous_batch(objs_per_layer[0], starts, ends):
+            return None
+        ptrs = torch.tensor([[o.tensor.data_ptr() for o in row] for row in objs_per_layer],
+                            dtype=torch.int64).pin_memory()
+        with torch.cuda.stream(stream):
+            return ptrs.to(self.device, non_blocking=True)
+
+    def _xfer_layer(self, objs, starts, ends, slots, layer: int, to_chunk: bool,
+                    table=None) -> None:
+        if table is not None:
+            on_dev = objs[0].raw_data.is_cuda
+            self._native_xfer(None, slots[starts[0]:ends[-1]], to_chunk, chunk_ptrs=table[layer],
+                              chunk_tokens=self.config.chunk_size, chunk_on_device=on_dev,
+                              layer_begin=layer, num_layers=1, chunk_layer_begin=0,
+                              mode=None if on_dev else _MODE["simt"],
+                              layout=None, chunk_layout=self._layer_layout_native())
+            return
         if self.device.type != "cuda":
             for obj, s, e in zip(objs, starts, ends):
                 if to_chunk:
@@ -351,27 +376,90 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
         """Generator: yield once, then gather layer l at each resume."""
         objs_per_layer: List[List[MemoryObj]] = memory_objs  # [L][chunks]
         slots = slot_mapping if self.device.type != "cuda" else self._slots(slot_mapping)
+        table = self._layer_tables(objs_per_layer, starts, ends, self.store_stream)
         yield
         for layer in range(self.layout.num_layers):
             if self.device.type == "cuda":
                 self.store_stream.wait_stream(torch.cuda.current_stream(self.device))
                 with torch.cuda.stream(self.store_stream):
-                    self._xfer_layer(objs_per_layer[layer], starts, ends, slots, layer, True)
+                    self._xfer_layer(objs_per_layer[layer], starts, ends, slots, layer, True,
+                                     table)
             else:
                 self._xfer_layer(objs_per_layer[layer], starts, ends, slots, layer, True)
             yield
         if self.device.type == "cuda" and sync:
             self.store_stream.synchronize()
 
+    def _staged_plan(self, objs_per_layer, starts, ends):
+        """Copy-engine plan for host chunk objects: each layer's objects are
+        copied whole (one cudaMemcpyAsync each, from pinned memory) into the
+        slots of one of two device staging banks, then scattered from the bank
+        by one TMA launch through a pointer table of its slots."""
+        if (self.device.type != "cuda" or self.config.cpu_transfer_mode != "copy_engine"
+                or not objs_per_layer or not objs_per_layer[0]
+                or objs_per_layer[0][0].raw_data.is_cuda
+                or not self._contiguous_batch(objs_per_layer[0], starts, ends)):
+            return None
+        row0 = objs_per_layer[0]
+        n = len(row0)
+        slot = (max(o.get_size() for o in row0) + 255) // 256 * 256
+        need = n * slot
+        banks = getattr(self, "_lw_banks", None)
+        if banks is None or banks[0].numel() < need:
+            banks = [torch.empty(need, dtype=torch.uint8, device=self.device) for _ in range(2)]
+            self._lw_banks = banks
+            self._lw_free = [None, None]
+        dst = [torch.tensor([b.data_ptr() + i * slot for i in range(n)], dtype=torch.int64)
+               for b in banks]
+        with torch.cuda.stream(self.load_stream):
+            dev_tables = [d.pin_memory().to(self.device, non_blocking=True) for d in dst]
+        srcs = torch.tensor([[o.data_ptr() for o in row] for row in objs_per_layer],
+                            dtype=torch.int64)
+        sizes = torch.tensor([o.get_size() for o in row0], dtype=torch.int64)
+        return dst, dev_tables, srcs, sizes
+
+    def _staged_load_layer(self, plan, layer, starts, ends, slots) -> None:
+        from ... import ops
+
+        dst, dev_tables, srcs, sizes = plan
+        b = layer & 1
+        if self._lw_free[b] is not None:  # the bank's previous scatter must be done
+            self.copy_stream.wait_event(self._lw_free[b])
+        with torch.cuda.stream(self.copy_stream):
+            ops.native().layerwise_prefill_dma_copy(dst[b], srcs[layer], sizes)
+            copied = torch.cuda.Event()
+            copied.record(self.copy_stream)
+        self.load_stream.wait_event(copied)
+        with torch.cuda.stream(self.load_stream):
+            self._native_xfer(None, slots[starts[0]:ends[-1]], False, chunk_ptrs=dev_tables[b],
+                              chunk_tokens=self.config.chunk_size, chunk_on_device=True,
+                              layer_begin=layer, num_layers=1, chunk_layer_begin=0,
+                              chunk_layout=self._layer_layout_native())
+            free = torch.cuda.Event()
+            free.record(self.load_stream)
+        self._lw_free[b] = free
+
     def batched_to_gpu(self, memory_objs=None, starts=None, ends=None, slot_mapping=None,
                        sync=True, **kwargs) -> Generator[None, List[List[MemoryObj]], None]:
         """Generator: first ``send`` the per-layer objects, then one layer per resume."""
         objs_per_layer = yield
         slots = slot_mapping if self.device.type != "cuda" else self._slots(slot_mapping)
+        plan = self._staged_plan(objs_per_layer, starts, ends)
+        if plan is not None:
+            for layer in range(self.layout.num_layers):
+                self._staged_load_layer(plan, layer, starts, ends, slots)
+                torch.cuda.current_stream(self.device).wait_stream(self.load_stream)
+                yield
+            if sync:
+                self.load_stream.synchronize()
+            yield
+            return
+        table = self._layer_tables(objs_per_layer, starts, ends, self.load_stream)
         for layer in range(self.layout.num_layers):
             if self.device.type == "cuda":
                 with torch.cuda.stream(self.load_stream):
-                    self._xfer_layer(objs_per_layer[layer], starts, ends, slots, layer, False)
+                    self._xfer_layer(objs_per_layer[layer], starts, ends, slots, layer, False,
+                                     table)
                 torch.cuda.current_stream(self.device).wait_stream(self.load_stream)
             else:
                 self._xfer_layer(objs_per_layer[layer], starts, ends, slots, layer, False)

@@ -102,6 +102,20 @@ class LocalCPUBackend(StorageBackendInterface):
             obj.ref_count_up()  # caller owns one reference
             return obj
 
+    def batched_get_blocking(self, keys: Sequence[CacheEngineKey]) -> List[Optional[MemoryObj]]:
+        """One lock acquisition for the whole batch (a layerwise 16k-token
+        request asks for thousands of per-layer chunks)."""
+        out: List[Optional[MemoryObj]] = []
+        with self._lock:
+            hc = self.hot_cache
+            for key in keys:
+                obj = hc.get(key)
+                if obj is not None:
+                    hc.move_to_end(key)
+                    obj.ref_count_up()
+                out.append(obj)
+        return out
+
     def pin(self, key: CacheEngineKey) -> bool:
         with self._lock:
             obj = self.hot_cache.get(key)

@@ -207,3 +207,24 @@ def test_head_major_cache_round_trip():
     assert bool(eng.retrieve(tokens, slot_mapping=slots2).all())
     assert torch.equal(_rows(conn.layout, slots2), exp)
     eng.close()
+
+
+def test_key_hash_cache_is_not_pickled():
+    import pickle
+    import subprocess
+    import sys
+
+    from lmcache_ascend_b200.utils.keys import CacheEngineKey
+
+    k = CacheEngineKey("vllm", "model-x", 2, 1, 0xABCDEF, "bfloat16", 0, (("tag", "v"),))
+    hash(k)  # fills the cache in this process
+    blob = pickle.dumps(k)
+    assert "_h" not in pickle.loads(blob).__dict__
+    # another process (another str-hash salt) finds the key by equality
+    code = ("import pickle,sys; from lmcache_ascend_b200.utils.keys import CacheEngineKey as K;"
+            "k=pickle.loads(sys.stdin.buffer.read());"
+            "d={K('vllm','model-x',2,1,0xABCDEF,'bfloat16',0,(('tag','v'),)):1};"
+            "print(d.get(k))")
+    out = subprocess.run([sys.executable, "-c", code], input=blob, capture_output=True,
+                         env={**__import__("os").environ, "PYTHONHASHSEED": "123"})
+    assert out.stdout.strip() == b"1", out.stderr
