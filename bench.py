@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--no-ttft", action="store_true",
                     help="skip the TTFT-on-prefix-hit measurement (Qwen3-32B, 16k hit)")
     ap.add_argument("--ttft-requests", type=int, default=8)
+    ap.add_argument("--no-fp8", action="store_true",
+                    help="skip the block-scaled fp8 push measurement")
     return ap.parse_args()
 
 
@@ -263,6 +265,60 @@ def main():
     ms = float(t.item())
     value = bytes_per_pair * pairs / (ms / 1e3) / 1e9
 
+    # ------------------------------------------------- fp8 push (lossy)
+    # The same push with block-scaled fp8 on the wire: the prefiller's kernel
+    # quantises (128-element groups, fp32 scales) into the decoder's staging,
+    # the decoder dequantises into its bf16 cache after the layer flags.
+    # Reported as bf16-equivalent GB/s per pair, receiver dequant included.
+    fp8 = None
+    if not a.no_fp8 and a.impl == "ours":
+        recv8 = PushReceiver(PagedKVLayout(dst_cache), fp8_staging_tokens=T) if role_d else None
+        send8 = PushSender(PagedKVLayout(src_cache), engine="push") if role_p else None
+        if world == 1:
+            send8.connect([recv8.desc])
+        else:
+            d8 = [None] * world
+            dist.all_gather_object(d8, recv8.desc.to_dict() if recv8 else None, group=gloo)
+            if role_p:
+                send8.connect([ReceiverDesc.from_dict(d8[rank + world // 2])])
+            dist.barrier(group=gloo)
+        tg8 = ([recv8.expect(T, tile_tokens=a.tile) for _ in range(a.warmup + a.steps)]
+               if recv8 is not None else [None] * (a.warmup + a.steps))
+
+        def step8(i):
+            if send8 is not None:
+                send8.push(src_slots, dst_slots, tile_tokens=a.tile, grid=a.grid, quant="fp8")
+            if recv8 is not None:
+                recv8.wait(tg8[i], timeout_s=5.0)
+                recv8.dequantize(dst_slots)
+
+        for i in range(a.warmup):
+            step8(i)
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for i in range(a.steps):
+            step8(a.warmup + i)
+        f1.record()
+        torch.cuda.synchronize()
+        fms = torch.tensor([f0.elapsed_time(f1) / a.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(fms, op=dist.ReduceOp.MAX)
+        fms = float(fms.item())
+        barrier()
+        for o in (send8, recv8):
+            if o is not None:
+                o.check()
+        wire = T * L * 2 * (H * D + (H * D // 128) * 4)
+        fp8 = {"bf16_equiv_gbps_per_pair": round(bytes_per_pair / (fms / 1e3) / 1e9, 2),
+               "wire_gbps_per_pair": round(wire / (fms / 1e3) / 1e9, 2),
+               "ms_per_step": round(fms, 4), "wire_bytes_per_pair": wire,
+               "bf16_bytes_per_pair": bytes_per_pair, "group": 128,
+               "note": "lossy (e4m3, one fp32 scale per 128 elements); decoder dequant "
+                       "included"}
+        if send8 is not None:
+            send8.close()
+
     # ------------------------------------------------------------ e2e arm
     # Same transfer through the engine's public API: the prefiller calls
     # LMCacheEngine.store_direct_prefill (PD backend handshake + fused push),
@@ -383,7 +439,8 @@ def main():
                      "random block tables)",
              "config": cfg, "bytes_per_pair_per_step": bytes_per_pair,
              "per_pair_gbps": round(per_pair, 2), "roofline": roof,
-             "clocks": ck, "e2e": e2e, "gpu_launches": launches, "ttft": ttft})
+             "clocks": ck, "e2e": e2e, "gpu_launches": launches, "ttft": ttft,
+             "push_fp8": fp8})
     if sender is not None:
         sender.close()
     if world > 1:

@@ -25,6 +25,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
@@ -167,6 +170,193 @@ __global__ void __launch_bounds__(kPushWarps * 32)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Block-scaled fp8 push.  The prefiller reads bf16 paged rows, quantises
+// every group of G consecutive elements (G = 128: one head of head_dim 128)
+// to e4m3 with scale = amax / 448, and stores the fp8 bytes plus the fp32
+// scales into a staging area in the decoder's HBM (through peer addresses),
+// halving the bytes that cross NVLink.  Staging is laid out by push token
+// order: q[(layer * planes + plane) * T + t][row_elems], scales
+// [(layer * planes + plane) * T + t][row_elems / G].  The per-layer flags are
+// released exactly as in pd_push_kernel; the decoder then runs
+// pd_dequant_scatter_kernel from its staging into its bf16 paged cache.
+// A 16-lane half-warp owns one group: lane i holds elements 8i .. 8i+7.
+// ---------------------------------------------------------------------------
+struct PushQJob {
+  PagedDesc src;
+  const void *src_slots;
+  int32_t slot_is_i64;
+  int32_t num_tokens;     // tokens in this push (staging rows per layer plane)
+  int32_t layer_begin;
+  int32_t num_layers;
+  int32_t tile_tokens;
+  int32_t group;          // elements per scale group (multiple of 128 / 16 lanes)
+  uint8_t *q;             // peer staging, fp8
+  float *scales;          // peer staging, fp32
+  unsigned *flags;
+  DeviceStatus *status;
+};
+
+__device__ __forceinline__ float bf16x2_lo(uint32_t w) {
+  return __uint_as_float(w << 16);
+}
+__device__ __forceinline__ float bf16x2_hi(uint32_t w) {
+  return __uint_as_float(w & 0xFFFF0000u);
+}
+
+constexpr int kQVec = 4;  // groups (half-warp items) per thread in flight
+
+template <int SPG>  // 128-element segments per scale group (group = 128 * SPG)
+__global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j) {
+  const int np = j.src.num_planes;
+  const int tiles = (j.num_tokens + j.tile_tokens - 1) / j.tile_tokens;
+  const int units_per_layer = np * tiles;
+  const int total = units_per_layer * j.num_layers;
+  const int tid = threadIdx.x;
+  const int half = tid >> 4;       // half-warp index in the CTA
+  const int hl = tid & 15;         // lane within the half-warp
+  constexpr int kHalves = kPushWarps * 2;
+  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    const int li = u / units_per_layer;
+    const int rem = u - li * units_per_layer;
+    const int p = rem / tiles;
+    const int tile = rem - p * tiles;
+    const int layer = j.layer_begin + li;
+    const PlaneDesc spl = j.src.plane[p];
+    const int row_elems = spl.row_bytes >> 1;
+    const int gpr = row_elems / j.group;       // groups per row
+    constexpr int spg = SPG;
+    const int t0 = tile * j.tile_tokens;
+    const int n = min(j.num_tokens - t0, j.tile_tokens);
+    const char *sbase = reinterpret_cast<const char *>(j.src.ptrs[layer * np + p]);
+    const int64_t rowq0 = (static_cast<int64_t>(li + j.layer_begin) * np + p) * j.num_tokens;
+    const int items = n * gpr;                 // (token, group) pairs of this unit
+    for (int base = 0; base < items; base += kHalves * kQVec) {
+      uint4 v[kQVec][SPG];
+      int ti_[kQVec], gi_[kQVec];
+      bool ok[kQVec];
+#pragma unroll
+      for (int k = 0; k < kQVec; ++k) {
+        const int it = base + k * kHalves + half;
+        ok[k] = false;
+        ti_[k] = gi_[k] = 0;
+        if (it < items) {
+          const int ti = it / gpr;
+          const int gi = it - ti * gpr;
+          ti_[k] = ti;
+          gi_[k] = gi;
+          const int64_t ss = push_slot(j.src_slots, j.slot_is_i64, t0 + ti);
+          if (ss >= 0 && ss < j.src.num_slots) {
+            ok[k] = true;
+            const unsigned ro = row_off(j.src, spl, static_cast<unsigned>(ss));
+#pragma unroll
+            for (int sgi = 0; sgi < SPG; ++sgi) {
+              const unsigned vb = static_cast<unsigned>(gi * j.group + sgi * 128 + hl * 8) * 2u;
+              const int4 x = ld_nc_v4(sbase + ro + seg_off(spl, vb));
+              v[k][sgi] = make_uint4(static_cast<unsigned>(x.x), static_cast<unsigned>(x.y),
+                                     static_cast<unsigned>(x.z), static_cast<unsigned>(x.w));
+            }
+          } else if (ss >= j.src.num_slots && hl == 0 && gi == 0) {
+            report_status(j.status, kStatusBadSlot, t0 + ti, ss, j.src.num_slots);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kQVec; ++k) {
+        float amax = 0.f;
+#pragma unroll
+        for (int sgi = 0; sgi < SPG; ++sgi) {
+          if (ok[k]) {
+            const uint32_t w[4] = {v[k][sgi].x, v[k][sgi].y, v[k][sgi].z, v[k][sgi].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              amax = fmaxf(amax, fmaxf(fabsf(bf16x2_lo(w[e])), fabsf(bf16x2_hi(w[e]))));
+          }
+        }
+#pragma unroll
+        for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (!ok[k]) continue;
+        const float inv = amax > 0.f ? __fdiv_rn(448.f, amax) : 0.f;
+        const int64_t row = rowq0 + t0 + ti_[k];
+        uint8_t *qrow = j.q + row * row_elems + static_cast<int64_t>(gi_[k]) * j.group;
+#pragma unroll
+        for (int sgi = 0; sgi < SPG; ++sgi) {
+          {
+            const uint32_t w[4] = {v[k][sgi].x, v[k][sgi].y, v[k][sgi].z, v[k][sgi].w};
+            uint32_t packed[2];
+#pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+              const __nv_fp8x2_storage_t a = __nv_cvt_float2_to_fp8x2(
+                  make_float2(bf16x2_lo(w[e]) * inv, bf16x2_hi(w[e]) * inv), __NV_SATFINITE,
+                  __NV_E4M3);
+              const __nv_fp8x2_storage_t b = __nv_cvt_float2_to_fp8x2(
+                  make_float2(bf16x2_lo(w[e + 1]) * inv, bf16x2_hi(w[e + 1]) * inv),
+                  __NV_SATFINITE, __NV_E4M3);
+              packed[e >> 1] = static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+            }
+            *reinterpret_cast<uint2 *>(qrow + sgi * 128 + hl * 8) = make_uint2(packed[0], packed[1]);
+          }
+        }
+        if (hl == 0) j.scales[row * gpr + gi_[k]] = __fdiv_rn(amax, 448.f);
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && j.flags) {
+      fence_acq_rel_sys();
+      red_release_sys_add(j.flags + layer, 1u);
+    }
+  }
+}
+
+// Decoder side: staging (fp8 + scales, push order) -> bf16 paged cache at
+// dst_slots[t].  Thread per 8 elements (one 16-byte store).
+__global__ void __launch_bounds__(256) pd_dequant_scatter_kernel(
+    PagedDesc dst, const uint8_t *__restrict__ q, const float *__restrict__ scales,
+    const void *dst_slots, int slot_is_i64, int num_tokens, int layer_begin, int num_layers,
+    int group, DeviceStatus *status) {
+  const int np = dst.num_planes;
+  const long long nth = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (int p = 0; p < np; ++p) {
+    const PlaneDesc pl = plane_of(dst, p);
+    const int row_elems = pl.row_bytes >> 1;
+    const int vpr = row_elems >> 3;
+    const int gpr = row_elems / group;
+    const long long total = static_cast<long long>(num_layers) * num_tokens * vpr;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += nth) {
+      const int vi = static_cast<int>(i % vpr);
+      const long long lt = i / vpr;
+      const int t = static_cast<int>(lt % num_tokens);
+      const int li = static_cast<int>(lt / num_tokens);
+      const int layer = layer_begin + li;
+      const int64_t ds = push_slot(dst_slots, slot_is_i64, t);
+      if (ds < 0) continue;
+      if (ds >= dst.num_slots) {
+        if (vi == 0) report_status(status, kStatusBadSlot, t, ds, dst.num_slots);
+        continue;
+      }
+      const int64_t row = (static_cast<int64_t>(layer) * np + p) * num_tokens + t;
+      const uint2 w = *reinterpret_cast<const uint2 *>(q + row * row_elems + vi * 8);
+      const float sc = scales[row * gpr + (vi * 8) / group];
+      const uint32_t ww[2] = {w.x, w.y};
+      uint32_t out[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+              static_cast<__nv_fp8x2_storage_t>((ww[e] >> (16 * h)) & 0xFFFFu), __NV_E4M3);
+          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
+          const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+          out[e * 2 + h] = *reinterpret_cast<const uint32_t *>(&b);
+        }
+      }
+      char *pa = paged_addr(dst, layer, p, ds) + seg_off(pl, static_cast<unsigned>(vi * 16));
+      *reinterpret_cast<uint4 *>(pa) = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+  }
+}
+
 // Decoder side: one thread per layer waits (bounded) until
 // flags[layer] - targets[i] >= 0.  Writes kStatusFlagTimeout on expiry.
 __global__ void pd_wait_flags_kernel(const unsigned *flags,
@@ -287,6 +477,96 @@ void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets,
       reinterpret_cast<const unsigned *>(flags_ptr),
       reinterpret_cast<const unsigned *>(targets.data_ptr()),
       static_cast<int>(layer_begin), n, budget, st);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t fp8_staging_bytes(const PagedLayout &layout, int64_t num_tokens, int64_t num_layers,
+                          int64_t group, bool scales) {
+  int64_t q = 0, sc = 0;
+  for (int p = 0; p < layout.desc().num_planes; ++p) {
+    const int64_t re = layout.desc().plane[p].row_bytes / 2;
+    q += re;
+    sc += re / group;
+  }
+  return scales ? num_layers * num_tokens * sc * 4 : num_layers * num_tokens * q;
+}
+
+void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
+                 const at::Tensor &src_slots, int64_t layer_begin, int64_t num_layers,
+                 int64_t flag_ptr, int64_t tile_tokens, int64_t grid, int64_t group,
+                 const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(src_slots.is_cuda() && src_slots.is_contiguous() &&
+                  (src_slots.scalar_type() == at::kInt || src_slots.scalar_type() == at::kLong),
+              "src_slots: contiguous device int32/int64");
+  TORCH_CHECK(group == 128 || group == 256 || group == 512,
+              "fp8 push: group of 128, 256 or 512 elements");
+  TORCH_CHECK(layer_begin >= 0 && layer_begin + num_layers <= src.desc().num_layers,
+              "layer range out of the cache");
+  for (int p = 0; p < src.desc().num_planes; ++p) {
+    const auto &pl = src.desc().plane[p];
+    TORCH_CHECK((pl.row_bytes / 2) % group == 0, "fp8 push: row elements must be a multiple "
+                "of the group (bf16 rows)");
+    TORCH_CHECK(pl.row_bytes == src.desc().plane[0].row_bytes,
+                "fp8 push: every plane must have the same row size");
+    TORCH_CHECK(pl.seg_bytes == 0 || pl.seg_bytes % 256 == 0,
+                "fp8 push: head-major segments must hold whole 128-element pieces");
+  }
+  TORCH_CHECK(q_ptr % 16 == 0 && scale_ptr % 4 == 0, "fp8 push: staging alignment");
+  if (src_slots.numel() == 0 || num_layers == 0) return;
+  const c10::cuda::CUDAGuard guard(src_slots.device());
+  PushQJob j;
+  std::memset(&j, 0, sizeof(j));
+  j.src = src.desc();
+  j.src_slots = src_slots.data_ptr();
+  j.slot_is_i64 = src_slots.scalar_type() == at::kLong;
+  j.num_tokens = static_cast<int32_t>(src_slots.numel());
+  j.layer_begin = static_cast<int32_t>(layer_begin);
+  j.num_layers = static_cast<int32_t>(num_layers);
+  j.tile_tokens = static_cast<int32_t>(tile_tokens > 0 ? tile_tokens : 128);
+  j.group = static_cast<int32_t>(group);
+  j.q = reinterpret_cast<uint8_t *>(q_ptr);
+  j.scales = reinterpret_cast<float *>(scale_ptr);
+  j.flags = reinterpret_cast<unsigned *>(flag_ptr);
+  if (status.has_value()) j.status = reinterpret_cast<DeviceStatus *>(status->data_ptr());
+  const int dev = src_slots.device().index();
+  const long long units =
+      push_units_per_layer(j.num_tokens, j.src.num_planes, j.tile_tokens) * num_layers;
+  int g = grid > 0 ? static_cast<int>(grid) : env_int2("LMC_PUSH_GRID", num_sms(dev) * 16);
+  g = static_cast<int>(std::max(1LL, std::min<long long>(units, g)));
+  auto stream = at::cuda::getCurrentCUDAStream(dev).stream();
+  if (group == 128)
+    pd_push_fp8_kernel<1><<<g, kPushWarps * 32, 0, stream>>>(j);
+  else if (group == 256)
+    pd_push_fp8_kernel<2><<<g, kPushWarps * 32, 0, stream>>>(j);
+  else
+    pd_push_fp8_kernel<4><<<g, kPushWarps * 32, 0, stream>>>(j);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void pd_dequant_scatter(const PagedLayout &dst, int64_t q_ptr, int64_t scale_ptr,
+                        const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
+                        int64_t group, const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(dst_slots.is_cuda() && dst_slots.is_contiguous() &&
+                  (dst_slots.scalar_type() == at::kInt || dst_slots.scalar_type() == at::kLong),
+              "dst_slots: contiguous device int32/int64");
+  for (int p = 0; p < dst.desc().num_planes; ++p) {
+    const auto &pl = dst.desc().plane[p];
+    TORCH_CHECK(pl.row_bytes == dst.desc().plane[0].row_bytes && pl.row_bytes % 16 == 0 &&
+                    (pl.row_bytes / 2) % group == 0 && pl.block_stride % 16 == 0 &&
+                    pl.slot_stride % 16 == 0 && (pl.seg_bytes == 0 || pl.seg_bytes % 16 == 0),
+                "dequant scatter: equal, 16-byte aligned bf16 rows");
+  }
+  if (dst_slots.numel() == 0 || num_layers == 0) return;
+  const c10::cuda::CUDAGuard guard(dst_slots.device());
+  const int dev = dst_slots.device().index();
+  DeviceStatus *st = status.has_value() ? reinterpret_cast<DeviceStatus *>(status->data_ptr())
+                                        : nullptr;
+  pd_dequant_scatter_kernel<<<num_sms(dev) * 8, 256, 0,
+                              at::cuda::getCurrentCUDAStream(dev).stream()>>>(
+      dst.desc(), reinterpret_cast<const uint8_t *>(q_ptr),
+      reinterpret_cast<const float *>(scale_ptr), dst_slots.data_ptr(),
+      dst_slots.scalar_type() == at::kLong, static_cast<int>(dst_slots.numel()),
+      static_cast<int>(layer_begin), static_cast<int>(num_layers), static_cast<int>(group), st);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -37,6 +37,15 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst, const at::Tensor &s
              const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
              int64_t replicas, const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
              int64_t grid, const c10::optional<at::Tensor> &status);
+int64_t fp8_staging_bytes(const PagedLayout &layout, int64_t num_tokens, int64_t num_layers,
+                          int64_t group, bool scales);
+void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
+                 const at::Tensor &src_slots, int64_t layer_begin, int64_t num_layers,
+                 int64_t flag_ptr, int64_t tile_tokens, int64_t grid, int64_t group,
+                 const c10::optional<at::Tensor> &status);
+void pd_dequant_scatter(const PagedLayout &dst, int64_t q_ptr, int64_t scale_ptr,
+                        const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
+                        int64_t group, const c10::optional<at::Tensor> &status);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
@@ -140,6 +149,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("replicas") = 1, py::arg("flag_ptrs") = std::vector<int64_t>{},
         py::arg("tile_tokens") = 128, py::arg("grid") = 0,
         py::arg("status") = py::none());
+  m.def("fp8_staging_bytes", &fp8_staging_bytes);
+  m.def("pd_push_fp8", &pd_push_fp8, py::arg("src"), py::arg("q_ptr"), py::arg("scale_ptr"),
+        py::arg("src_slots"), py::arg("layer_begin"), py::arg("num_layers"),
+        py::arg("flag_ptr"), py::arg("tile_tokens") = 128, py::arg("grid") = 0,
+        py::arg("group") = 128, py::arg("status") = py::none());
+  m.def("pd_dequant_scatter", &pd_dequant_scatter, py::arg("dst"), py::arg("q_ptr"),
+        py::arg("scale_ptr"), py::arg("dst_slots"), py::arg("layer_begin"),
+        py::arg("num_layers"), py::arg("group") = 128, py::arg("status") = py::none());
   m.def("pd_wait_flags", &pd_wait_flags, py::arg("flags_ptr"), py::arg("targets"),
         py::arg("layer_begin"), py::arg("timeout_s"), py::arg("status") = py::none());
 

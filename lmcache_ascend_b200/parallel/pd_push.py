@@ -13,6 +13,13 @@ The exchange of descriptors is left to the caller (torch.distributed object
 collectives in the benchmark, the PD backend's ZMQ handshake in serving).
 Fan-out to several receivers (TP-replicated MLA latent) is one launch with
 ``replicas`` destination tables; the rows are read once.
+
+Optional block-scaled fp8 transfer (``quant="fp8"``): the same kernel pass
+quantises each group of 128 bf16 elements to e4m3 with one fp32 scale and
+stores them into a staging area in the receiver's HBM, so about half the
+bytes cross NVLink; the receiver dequantises into its bf16 paged cache after
+the layer flags (``PushReceiver.dequantize``).  Lossy: the relative error of
+an element is at most 2^-4 of its group's maximum.
 """
 
 from __future__ import annotations
@@ -40,6 +47,10 @@ class ReceiverDesc:
     device: int
     seg_bytes: List[int] = field(default_factory=list)   # head-major rows (0: contiguous)
     seg_stride: List[int] = field(default_factory=list)
+    fp8_q: Optional[dict] = None        # IpcDesc dict of the fp8 staging rows
+    fp8_scales: Optional[dict] = None   # IpcDesc dict of the staging scales
+    fp8_tokens: int = 0                 # staging capacity in tokens per push
+    fp8_group: int = 128
 
     def to_dict(self) -> dict:
         return self.__dict__.copy()
@@ -50,7 +61,8 @@ class ReceiverDesc:
 
 
 class PushReceiver:
-    def __init__(self, layout: PagedKVLayout, max_layers: Optional[int] = None):
+    def __init__(self, layout: PagedKVLayout, max_layers: Optional[int] = None,
+                 fp8_staging_tokens: int = 0, fp8_group: int = 128):
         self.layout = layout
         self.device = layout.device
         dev = self.device.index or 0
@@ -75,6 +87,20 @@ class PushReceiver:
             flags=export_local(self._flags_buf.data_ptr(), dev).to_dict(), device=dev,
             seg_bytes=[p.seg_elems * es if p.segmented else 0 for p in layout.planes],
             seg_stride=[p.seg_stride * es if p.segmented else 0 for p in layout.planes])
+        self.fp8_tokens, self.fp8_group = fp8_staging_tokens, fp8_group
+        if fp8_staging_tokens > 0:
+            mod = ops.native()
+            nat = layout.native()
+            qb = mod.fp8_staging_bytes(nat, fp8_staging_tokens, layout.num_layers, fp8_group,
+                                       False)
+            sb = mod.fp8_staging_bytes(nat, fp8_staging_tokens, layout.num_layers, fp8_group,
+                                       True)
+            self._q_buf = mod.device_buffer(qb, dev)
+            self._s_buf = mod.device_buffer(sb, dev)
+            self.desc.fp8_q = export_local(self._q_buf.data_ptr(), dev).to_dict()
+            self.desc.fp8_scales = export_local(self._s_buf.data_ptr(), dev).to_dict()
+            self.desc.fp8_tokens = fp8_staging_tokens
+            self.desc.fp8_group = fp8_group
 
     def expect(self, num_tokens: int, layer_begin: int = 0,
                num_layers: Optional[int] = None, tile_tokens: int = 128) -> torch.Tensor:
@@ -94,6 +120,19 @@ class PushReceiver:
         """Enqueue a bounded wait on the current stream (no host sync)."""
         ops.native().pd_wait_flags(self._flags_buf.data_ptr(), targets, layer_begin,
                                    timeout_s, self.status.tensor)
+
+    def dequantize(self, dst_slots: torch.Tensor, layer_begin: int = 0,
+                   num_layers: Optional[int] = None) -> None:
+        """After ``wait``: fp8 staging of the last push -> bf16 paged cache at
+        ``dst_slots`` (enqueued on the current stream)."""
+        if self.fp8_tokens <= 0:
+            raise RuntimeError("receiver was built without fp8 staging")
+        if dst_slots.numel() > self.fp8_tokens:
+            raise ValueError("push larger than the fp8 staging area")
+        nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
+        ops.native().pd_dequant_scatter(self.layout.native(), self._q_buf.data_ptr(),
+                                        self._s_buf.data_ptr(), dst_slots, layer_begin, nl,
+                                        self.fp8_group, self.status.tensor)
 
     def check(self) -> None:
         self.status.check("pd push receiver")
@@ -139,6 +178,11 @@ class PushSender:
         self._dst.set_bases_aligned(all(p % 16 == 0 for p in ptrs))
         self._flag_ptrs = [self.peers.resolve(IpcDesc.from_dict(r.flags)) for r in receivers]
         self.replicas = len(receivers)
+        self._fp8 = None
+        if r0.fp8_q is not None and len(receivers) == 1:
+            self._fp8 = (self.peers.resolve(IpcDesc.from_dict(r0.fp8_q)),
+                         self.peers.resolve(IpcDesc.from_dict(r0.fp8_scales)),
+                         r0.fp8_tokens, r0.fp8_group)
         import os
 
         self._local = (self.engine == "auto" and len(receivers) == 1
@@ -146,11 +190,26 @@ class PushSender:
                        and r0.device == (self.device.index or 0))
 
     def push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, layer_begin: int = 0,
-             num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0) -> None:
-        """Enqueue the push of ``num_layers`` layers on the current stream."""
+             num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0,
+             quant: str = "none") -> None:
+        """Enqueue the push of ``num_layers`` layers on the current stream.
+        ``quant="fp8"`` sends block-scaled fp8 to the receiver's staging (the
+        receiver applies ``dst_slots`` in ``PushReceiver.dequantize``)."""
         if self._dst is None:
             raise RuntimeError("PushSender.connect() first")
         nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
+        if quant == "fp8":
+            if self._fp8 is None:
+                raise RuntimeError("fp8 push needs one receiver built with fp8 staging")
+            q_ptr, s_ptr, cap, group = self._fp8
+            if src_slots.numel() > cap:
+                raise ValueError("push larger than the receiver's fp8 staging area")
+            ops.native().pd_push_fp8(self.layout.native(), q_ptr, s_ptr, src_slots,
+                                     layer_begin, nl, self._flag_ptrs[0], tile_tokens, grid,
+                                     group, self.status.tensor)
+            return
+        if quant != "none":
+            raise ValueError("quant must be 'none' or 'fp8'")
         if self._local:
             units = ops.native().push_units_per_layer(src_slots.numel(), self.layout.num_planes,
                                                       tile_tokens)

@@ -111,3 +111,45 @@ def test_wait_times_out_with_status():
     # the context is still usable
     x = torch.ones(4, device=DEV) * 2
     assert float(x.sum()) == 8.0
+
+
+def _fp8_ref(rows: torch.Tensor, group: int) -> torch.Tensor:
+    """PyTorch reference of the block-scaled fp8 round trip of bf16 rows."""
+    x = rows.float().view(rows.shape[0], -1, group)
+    amax = x.abs().amax(dim=-1, keepdim=True)
+    # IEEE fp32 quotients (PyTorch divides by a scalar through its reciprocal):
+    # a float64 quotient rounded once to fp32 is the correctly rounded one
+    inv = torch.where(amax > 0, (448.0 / amax.double()).float(), torch.zeros_like(amax))
+    scale = (amax.double() / 448.0).float()
+    q = (x * inv).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return (q.float() * scale).to(torch.bfloat16).view_as(rows)
+
+
+@pytest.mark.parametrize("group", [128, 256])
+@pytest.mark.parametrize("tile", [64, 128])
+def test_fp8_push_matches_reference_and_halves_bytes(group, tile):
+    L, NB, BS, H, D = 4, 32, 128, 2, 128
+    src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=11)
+    dst = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=12)
+    src[1][0][3] = 0  # an all-zero block: scale 0
+    T = 900
+    ss = block_slots(T, BS, NB, seed=13, device=DEV, dtype=torch.int32)
+    ds = random_slots(T, NB * BS, seed=14, device=DEV, dtype=torch.int32)
+    recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=1024, fp8_group=group)
+    send = PushSender(PagedKVLayout(src), engine="push")
+    send.connect([recv.desc])
+    tg = recv.expect(T, tile_tokens=tile)
+    send.push(ss, ds, tile_tokens=tile, quant="fp8")
+    recv.wait(tg, timeout_s=2.0)
+    recv.dequantize(ds)
+    torch.cuda.synchronize()
+    send.check()
+    recv.check()
+    for a, b in zip(_rows(src, ss), _rows(dst, ds)):
+        assert torch.equal(b, _fp8_ref(a, group))
+        # bounded error: at most 2^-4 of the group's amax per element
+        err = (b.float() - a.float()).view(T, -1, group).abs()
+        bound = a.float().view(T, -1, group).abs().amax(-1, keepdim=True) * (2 ** -4) + 1e-2
+        assert bool((err <= bound).all())
+    wire = recv._q_buf.numel() + recv._s_buf.numel()
+    assert wire < 0.56 * 1024 * L * 2 * H * D * 2  # about half the bf16 bytes
