@@ -288,9 +288,11 @@ def main():
         def step8(i):
             if send8 is not None:
                 send8.push(src_slots, dst_slots, tile_tokens=a.tile, grid=a.grid, quant="fp8")
-            if recv8 is not None:
-                recv8.wait(tg8[i], timeout_s=5.0)
-                recv8.dequantize(dst_slots)
+            if recv8 is not None:  # dequantise each 8-layer group as soon as it landed
+                for l0 in range(0, L, 8):
+                    n8 = min(8, L - l0)
+                    recv8.wait(tg8[i][l0:l0 + n8], layer_begin=l0, timeout_s=5.0)
+                    recv8.dequantize(dst_slots, layer_begin=l0, num_layers=n8)
 
         for i in range(a.warmup):
             step8(i)

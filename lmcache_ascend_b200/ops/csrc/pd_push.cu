@@ -180,7 +180,6 @@ __global__ void __launch_bounds__(kPushWarps * 32)
 // [(layer * planes + plane) * T + t][row_elems / G].  The per-layer flags are
 // released exactly as in pd_push_kernel; the decoder then runs
 // pd_dequant_scatter_kernel from its staging into its bf16 paged cache.
-// A 16-lane half-warp owns one group: lane i holds elements 8i .. 8i+7.
 // ---------------------------------------------------------------------------
 struct PushQJob {
   PagedDesc src;
@@ -206,6 +205,8 @@ __device__ __forceinline__ float bf16x2_hi(uint32_t w) {
 
 constexpr int kQVec = 4;  // groups (half-warp items) per thread in flight
 
+// An 8-lane quarter-warp owns one 128-element segment of a group: lane i
+// holds elements 16i .. 16i+15 (two 16-byte loads, one 16-byte fp8 store).
 template <int SPG>  // 128-element segments per scale group (group = 128 * SPG)
 __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j) {
   const int np = j.src.num_planes;
@@ -213,9 +214,9 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
   const int units_per_layer = np * tiles;
   const int total = units_per_layer * j.num_layers;
   const int tid = threadIdx.x;
-  const int half = tid >> 4;       // half-warp index in the CTA
-  const int hl = tid & 15;         // lane within the half-warp
-  constexpr int kHalves = kPushWarps * 2;
+  const int quarter = tid >> 3;    // quarter-warp index in the CTA
+  const int ql = tid & 7;          // lane within the quarter-warp
+  constexpr int kQuarters = kPushWarps * 4;
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
     const int li = u / units_per_layer;
     const int rem = u - li * units_per_layer;
@@ -225,19 +226,18 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
     const PlaneDesc spl = j.src.plane[p];
     const int row_elems = spl.row_bytes >> 1;
     const int gpr = row_elems / j.group;       // groups per row
-    constexpr int spg = SPG;
     const int t0 = tile * j.tile_tokens;
     const int n = min(j.num_tokens - t0, j.tile_tokens);
     const char *sbase = reinterpret_cast<const char *>(j.src.ptrs[layer * np + p]);
-    const int64_t rowq0 = (static_cast<int64_t>(li + j.layer_begin) * np + p) * j.num_tokens;
+    const int64_t rowq0 = (static_cast<int64_t>(layer) * np + p) * j.num_tokens;
     const int items = n * gpr;                 // (token, group) pairs of this unit
-    for (int base = 0; base < items; base += kHalves * kQVec) {
-      uint4 v[kQVec][SPG];
+    for (int base = 0; base < items; base += kQuarters * kQVec) {
+      uint4 v[kQVec][SPG][2];
       int ti_[kQVec], gi_[kQVec];
       bool ok[kQVec];
 #pragma unroll
       for (int k = 0; k < kQVec; ++k) {
-        const int it = base + k * kHalves + half;
+        const int it = base + k * kQuarters + quarter;
         ok[k] = false;
         ti_[k] = gi_[k] = 0;
         if (it < items) {
@@ -251,12 +251,16 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
             const unsigned ro = row_off(j.src, spl, static_cast<unsigned>(ss));
 #pragma unroll
             for (int sgi = 0; sgi < SPG; ++sgi) {
-              const unsigned vb = static_cast<unsigned>(gi * j.group + sgi * 128 + hl * 8) * 2u;
-              const int4 x = ld_nc_v4(sbase + ro + seg_off(spl, vb));
-              v[k][sgi] = make_uint4(static_cast<unsigned>(x.x), static_cast<unsigned>(x.y),
-                                     static_cast<unsigned>(x.z), static_cast<unsigned>(x.w));
+#pragma unroll
+              for (int hv = 0; hv < 2; ++hv) {
+                const unsigned vb =
+                    static_cast<unsigned>(gi * j.group + sgi * 128 + ql * 16 + hv * 8) * 2u;
+                const int4 x = ld_nc_v4(sbase + ro + seg_off(spl, vb));
+                v[k][sgi][hv] = make_uint4(static_cast<unsigned>(x.x), static_cast<unsigned>(x.y),
+                                           static_cast<unsigned>(x.z), static_cast<unsigned>(x.w));
+              }
             }
-          } else if (ss >= j.src.num_slots && hl == 0 && gi == 0) {
+          } else if (ss >= j.src.num_slots && ql == 0 && gi == 0) {
             report_status(j.status, kStatusBadSlot, t0 + ti, ss, j.src.num_slots);
           }
         }
@@ -264,26 +268,32 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
 #pragma unroll
       for (int k = 0; k < kQVec; ++k) {
         float amax = 0.f;
+        if (ok[k]) {
 #pragma unroll
-        for (int sgi = 0; sgi < SPG; ++sgi) {
-          if (ok[k]) {
-            const uint32_t w[4] = {v[k][sgi].x, v[k][sgi].y, v[k][sgi].z, v[k][sgi].w};
+          for (int sgi = 0; sgi < SPG; ++sgi) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              amax = fmaxf(amax, fmaxf(fabsf(bf16x2_lo(w[e])), fabsf(bf16x2_hi(w[e]))));
+            for (int hv = 0; hv < 2; ++hv) {
+              const uint32_t w[4] = {v[k][sgi][hv].x, v[k][sgi][hv].y, v[k][sgi][hv].z,
+                                     v[k][sgi][hv].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                amax = fmaxf(amax, fmaxf(fabsf(bf16x2_lo(w[e])), fabsf(bf16x2_hi(w[e]))));
+            }
           }
         }
 #pragma unroll
-        for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        for (int o = 4; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (!ok[k]) continue;
         const float inv = amax > 0.f ? __fdiv_rn(448.f, amax) : 0.f;
         const int64_t row = rowq0 + t0 + ti_[k];
         uint8_t *qrow = j.q + row * row_elems + static_cast<int64_t>(gi_[k]) * j.group;
 #pragma unroll
         for (int sgi = 0; sgi < SPG; ++sgi) {
-          {
-            const uint32_t w[4] = {v[k][sgi].x, v[k][sgi].y, v[k][sgi].z, v[k][sgi].w};
-            uint32_t packed[2];
+          uint32_t packed[4];
+#pragma unroll
+          for (int hv = 0; hv < 2; ++hv) {
+            const uint32_t w[4] = {v[k][sgi][hv].x, v[k][sgi][hv].y, v[k][sgi][hv].z,
+                                   v[k][sgi][hv].w};
 #pragma unroll
             for (int e = 0; e < 4; e += 2) {
               const __nv_fp8x2_storage_t a = __nv_cvt_float2_to_fp8x2(
@@ -292,12 +302,14 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
               const __nv_fp8x2_storage_t b = __nv_cvt_float2_to_fp8x2(
                   make_float2(bf16x2_lo(w[e + 1]) * inv, bf16x2_hi(w[e + 1]) * inv),
                   __NV_SATFINITE, __NV_E4M3);
-              packed[e >> 1] = static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+              packed[hv * 2 + (e >> 1)] =
+                  static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
             }
-            *reinterpret_cast<uint2 *>(qrow + sgi * 128 + hl * 8) = make_uint2(packed[0], packed[1]);
           }
+          *reinterpret_cast<uint4 *>(qrow + sgi * 128 + ql * 16) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
-        if (hl == 0) j.scales[row * gpr + gi_[k]] = __fdiv_rn(amax, 448.f);
+        if (ql == 0) j.scales[row * gpr + gi_[k]] = __fdiv_rn(amax, 448.f);
       }
     }
     __syncthreads();
