@@ -46,6 +46,10 @@ void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
 void pd_dequant_scatter(const PagedLayout &dst, int64_t q_ptr, int64_t scale_ptr,
                         const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
                         int64_t group, const c10::optional<at::Tensor> &status);
+void pd_push_multimem(const PagedLayout &src, int64_t mc_rows, int64_t mc_flags,
+                      const at::Tensor &src_slots, int64_t layer_begin, int64_t num_layers,
+                      int64_t tile_tokens, int64_t grid,
+                      const c10::optional<at::Tensor> &status);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
@@ -150,6 +154,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("tile_tokens") = 128, py::arg("grid") = 0,
         py::arg("status") = py::none());
   m.def("fp8_staging_bytes", &fp8_staging_bytes);
+  m.def("pd_push_multimem", &pd_push_multimem, py::arg("src"), py::arg("mc_rows"),
+        py::arg("mc_flags"), py::arg("src_slots"), py::arg("layer_begin"),
+        py::arg("num_layers"), py::arg("tile_tokens") = 128, py::arg("grid") = 0,
+        py::arg("status") = py::none());
   m.def("pd_push_fp8", &pd_push_fp8, py::arg("src"), py::arg("q_ptr"), py::arg("scale_ptr"),
         py::arg("src_slots"), py::arg("layer_begin"), py::arg("num_layers"),
         py::arg("flag_ptr"), py::arg("tile_tokens") = 128, py::arg("grid") = 0,

@@ -1,0 +1,83 @@
+"""PD push fan-out through NVSwitch multicast (NVLS).
+
+One prefiller sends the same KV to several decoders (a TP-replicated MLA
+latent cache, or a decoder group larger than the prefill group) while its
+NVLink egress carries the bytes once: the group's members share a symmetric
+staging buffer bound to an NVLink multicast object
+(``torch.distributed._symmetric_memory``), the prefiller's kernel stores every
+vector once with ``multimem.st`` and bumps per-layer flags with
+``multimem.red.release``, and each decoder waits on its own copy of the flags
+(bounded) and scatters the staging rows into its paged cache locally.
+
+Construction is collective over ``group`` (every member passes the same
+shapes).  ``has_multicast`` is False where the system has no NVLS; callers
+then use ``PushSender`` fan-out (one peer store per decoder).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..v1.kv_format import PagedKVLayout
+
+
+class MulticastFanout:
+    def __init__(self, group, num_layers: int, num_planes: int, row_bytes: int,
+                 max_tokens: int, device: torch.device):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.num_layers, self.num_planes = num_layers, num_planes
+        self.row_bytes, self.max_tokens = row_bytes, max_tokens
+        self.device = torch.device(device)
+        rows = num_layers * num_planes * max_tokens * row_bytes
+        self.flags_off = (rows + 255) // 256 * 256
+        self.buf = symm_mem.empty(self.flags_off + 4 * max(num_layers, 1), dtype=torch.uint8,
+                                  device=self.device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, group)
+        self.has_multicast = bool(self.handle.has_multicast_support())
+        self.mc = int(self.handle.multicast_ptr) if self.has_multicast else 0
+        torch.cuda.synchronize(self.device)
+        self.handle.barrier()  # zeroed flags visible to every member before any push
+        self.expected = [0] * num_layers
+        self.status = ops.DeviceStatus(self.device)
+        # row ((layer * planes + p) * T + t): plane p starts p * rb * T in,
+        # layer l at l * planes * rb * T, token t at t * rb
+        rb, npl = row_bytes, num_planes
+        self._chunk_layout = ops.native().ChunkLayout([rb] * npl, npl * rb, [rb] * npl,
+                                                      [0] * npl)
+
+    # ------------------------------------------------------------ sender
+    def push(self, layout: PagedKVLayout, src_slots: torch.Tensor, tile_tokens: int = 128,
+             grid: int = 0) -> None:
+        if not self.has_multicast:
+            raise RuntimeError("NVLink multicast is not available on this system")
+        if src_slots.numel() > self.max_tokens:
+            raise ValueError("push larger than the multicast staging area")
+        ops.native().pd_push_multimem(layout.native(), self.mc, self.mc + self.flags_off,
+                                      src_slots, 0, self.num_layers, tile_tokens, grid,
+                                      self.status.tensor)
+
+    # ---------------------------------------------------------- receiver
+    def expect(self, num_tokens: int, tile_tokens: int = 128) -> torch.Tensor:
+        units = ops.native().push_units_per_layer(num_tokens, self.num_planes, tile_tokens)
+        tg = []
+        for l in range(self.num_layers):
+            self.expected[l] = (self.expected[l] + units) & 0xFFFFFFFF
+            tg.append(self.expected[l] - (1 << 32) if self.expected[l] >= (1 << 31)
+                      else self.expected[l])
+        return torch.tensor(tg, dtype=torch.int32).to(self.device, non_blocking=True)
+
+    def wait(self, targets: torch.Tensor, timeout_s: float = 10.0) -> None:
+        ops.native().pd_wait_flags(self.buf.data_ptr() + self.flags_off, targets, 0,
+                                   timeout_s, self.status.tensor)
+
+    def scatter(self, layout: PagedKVLayout, dst_slots: torch.Tensor, num_tokens: int) -> None:
+        """Local staging rows of the last push -> this member's paged cache."""
+        ops.native().kv_transfer(layout.native(), self.buf, None, self._chunk_layout,
+                                 num_tokens, 0, 0, True, dst_slots, 0, 0, self.num_layers,
+                                 False, 0, self.status.tensor, None, 0, None)
+
+    def check(self) -> None:
+        self.status.check("multicast fan-out")
