@@ -125,6 +125,45 @@ def bench_offload(small: bool):
         for o in objs:
             o.ref_count_down()
         alloc.close()
+    # layerwise: per-layer chunk objects, one transfer per layer (the engine's
+    # store_layer / retrieve_layer path)
+    from .v1.gpu_connector import VLLMPagedMemLayerwiseGPUConnector
+
+    L = len(kv)
+    for mode in ("copy_engine", "zero_copy"):
+        cfg = LMCacheEngineConfig.from_defaults(chunk_size=cs, cpu_transfer_mode=mode,
+                                                use_layerwise=True)
+        conn = VLLMPagedMemLayerwiseGPUConnector(cfg, kvcaches=kv)
+        starts = list(range(0, T, cs))
+        ends = [min(s + cs, T) for s in starts]
+        per_layer_bytes = sum(conn.get_shape(e - s).numel() * 2 for s, e in zip(starts, ends))
+        alloc = PinnedMemoryAllocator(L * per_layer_bytes + (4 << 20))
+        objs = [[alloc.allocate(conn.get_shape(e - s), torch.bfloat16, MemoryFormat.KV_2LTD)
+                 for s, e in zip(starts, ends)] for _ in range(L)]
+        moved = L * per_layer_bytes
+
+        def store():
+            g = conn.batched_from_gpu(objs, starts, ends, slot_mapping=slots)
+            for _ in g:
+                pass
+
+        def load():
+            g = conn.batched_to_gpu(None, starts, ends, slot_mapping=slots)
+            next(g)
+            g.send(objs)
+            for _ in g:
+                pass
+
+        ms = _time(store, 5, 2)
+        _emit(f"offload_layerwise_store_{mode}", ms, moved, traffic_bytes=moved, tokens=T,
+              layers=L, note="one transfer per layer; bound: host link")
+        ms = _time(load, 5, 2)
+        _emit(f"offload_layerwise_load_{mode}", ms, moved, traffic_bytes=moved, tokens=T,
+              layers=L, note="one transfer per layer; bound: host link")
+        for row in objs:
+            for o in row:
+                o.ref_count_down()
+        alloc.close()
 
 
 def bench_cachegen(small: bool):

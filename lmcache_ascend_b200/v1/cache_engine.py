@@ -386,6 +386,7 @@ class LMCacheEngine:
         for layer in range(L):
             yield
             next(gen, None)
+        next(gen, None)  # finish the generator: every layer's bytes are in the objects
         q = self.layerwise_put_queue
         req_id = kwargs.get("req_id", "")
         for layer in range(L):

@@ -376,6 +376,17 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
         """Generator: yield once, then gather layer l at each resume."""
         objs_per_layer: List[List[MemoryObj]] = memory_objs  # [L][chunks]
         slots = slot_mapping if self.device.type != "cuda" else self._slots(slot_mapping)
+        plan = self._staged_plan(objs_per_layer, starts, ends, store=True)
+        if plan is not None:
+            yield
+            for layer in range(self.layout.num_layers):
+                self.store_stream.wait_stream(torch.cuda.current_stream(self.device))
+                self._staged_store_layer(plan, layer, starts, ends, slots)
+                yield
+            self.store_stream.wait_stream(self.copy_stream)
+            if sync:
+                self.store_stream.synchronize()
+            return
         table = self._layer_tables(objs_per_layer, starts, ends, self.store_stream)
         yield
         for layer in range(self.layout.num_layers):
@@ -390,11 +401,14 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
         if self.device.type == "cuda" and sync:
             self.store_stream.synchronize()
 
-    def _staged_plan(self, objs_per_layer, starts, ends):
-        """Copy-engine plan for host chunk objects: each layer's objects are
-        copied whole (one cudaMemcpyAsync each, from pinned memory) into the
-        slots of one of two device staging banks, then scattered from the bank
-        by one TMA launch through a pointer table of its slots."""
+    def _staged_plan(self, objs_per_layer, starts, ends, store: bool = False):
+        """Copy-engine plan for host chunk objects.  Loads: each layer's objects
+        are copied whole (one coalesced cudaMemcpyAsync batch from pinned
+        memory) into the slots of one of two device staging banks, then
+        scattered from the bank by one TMA launch through a pointer table of
+        its slots.  Stores (``store``): the mirror image, TMA gather into a
+        bank then one coalesced device-to-host batch; loads and stores use
+        separate banks."""
         if (self.device.type != "cuda" or self.config.cpu_transfer_mode != "copy_engine"
                 or not objs_per_layer or not objs_per_layer[0]
                 or objs_per_layer[0][0].raw_data.is_cuda
@@ -404,19 +418,41 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
         n = len(row0)
         slot = (max(o.get_size() for o in row0) + 255) // 256 * 256
         need = n * slot
-        banks = getattr(self, "_lw_banks", None)
+        attr = "_lws" if store else "_lw"
+        banks = getattr(self, attr + "_banks", None)
         if banks is None or banks[0].numel() < need:
             banks = [torch.empty(need, dtype=torch.uint8, device=self.device) for _ in range(2)]
-            self._lw_banks = banks
-            self._lw_free = [None, None]
+            setattr(self, attr + "_banks", banks)
+            setattr(self, attr + "_free", [None, None])
         dst = [torch.tensor([b.data_ptr() + i * slot for i in range(n)], dtype=torch.int64)
                for b in banks]
-        with torch.cuda.stream(self.load_stream):
+        with torch.cuda.stream(self.store_stream if store else self.load_stream):
             dev_tables = [d.pin_memory().to(self.device, non_blocking=True) for d in dst]
         srcs = torch.tensor([[o.data_ptr() for o in row] for row in objs_per_layer],
                             dtype=torch.int64)
         sizes = torch.tensor([o.get_size() for o in row0], dtype=torch.int64)
         return dst, dev_tables, srcs, sizes
+
+    def _staged_store_layer(self, plan, layer, starts, ends, slots) -> None:
+        from ... import ops
+
+        bank_ptrs, dev_tables, host_ptrs, sizes = plan
+        b = layer & 1
+        if self._lws_free[b] is not None:  # the bank's previous copy-out must be done
+            self.store_stream.wait_event(self._lws_free[b])
+        with torch.cuda.stream(self.store_stream):
+            self._native_xfer(None, slots[starts[0]:ends[-1]], True, chunk_ptrs=dev_tables[b],
+                              chunk_tokens=self.config.chunk_size, chunk_on_device=True,
+                              layer_begin=layer, num_layers=1, chunk_layer_begin=0,
+                              chunk_layout=self._layer_layout_native())
+            gathered = torch.cuda.Event()
+            gathered.record(self.store_stream)
+        self.copy_stream.wait_event(gathered)
+        with torch.cuda.stream(self.copy_stream):
+            ops.native().layerwise_prefill_dma_copy(host_ptrs[layer], bank_ptrs[b], sizes)
+            free = torch.cuda.Event()
+            free.record(self.copy_stream)
+        self._lws_free[b] = free
 
     def _staged_load_layer(self, plan, layer, starts, ends, slots) -> None:
         from ... import ops
