@@ -135,8 +135,13 @@ class LMCacheConnectorV1Impl:
 
     def __init__(self, role: str, config: LMCacheEngineConfig, model_name: str,
                  block_size: int, world_size: int = 1, rank: int = 0, use_mla: bool = False,
-                 dp_rank: int = 0, engine=None, kv_dtype=None):
+                 dp_rank: int = 0, engine=None, kv_dtype=None, kv_role: str = "kv_both"):
+        if kv_role not in ("kv_both", "kv_producer", "kv_consumer"):
+            raise ValueError(f"unknown kv_role {kv_role!r}")
         self.role = role
+        # vLLM's KVTransferConfig.kv_role: a consumer (disaggregated decoder)
+        # only loads; producers and kv_both instances also save
+        self.kv_role = kv_role
         self.config = config
         self.block_size = block_size
         self.chunk_size = config.chunk_size
@@ -309,7 +314,7 @@ class LMCacheConnectorV1Impl:
             next(g, None)
 
     def save_kv_layer(self, layer_name: str, kv_layer=None, attn_metadata=None, **kw) -> None:
-        if self._meta is None or not self.config.use_layerwise:
+        if self._meta is None or not self.config.use_layerwise or self.kv_role == "kv_consumer":
             return
         eng = self._ensure_engine()
         if layer_name == self._layer_names[0]:
@@ -326,7 +331,7 @@ class LMCacheConnectorV1Impl:
             next(g, None)
 
     def wait_for_save(self) -> None:
-        if self._meta is None:
+        if self._meta is None or self.kv_role == "kv_consumer":
             return
         eng = self._ensure_engine()
         if self.config.use_layerwise:

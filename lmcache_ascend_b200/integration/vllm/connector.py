@@ -53,7 +53,8 @@ class LMCacheB200ConnectorV1(KVConnectorBase_V1):
         self._impl = LMCacheConnectorV1Impl(
             r, cfg, model_name=str(mc.model), block_size=vllm_config.cache_config.block_size,
             world_size=pc.tensor_parallel_size, rank=tp_rank, use_mla=bool(mc.use_mla),
-            dp_rank=getattr(pc, "data_parallel_rank", 0) or 0, kv_dtype=None)
+            dp_rank=getattr(pc, "data_parallel_rank", 0) or 0, kv_dtype=None,
+            kv_role=getattr(kvt, "kv_role", None) or "kv_both")
 
     # ---------------------------------------------------------- worker
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]):

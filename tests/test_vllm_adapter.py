@@ -138,3 +138,28 @@ def test_lookup_over_ipc():
     client.close()
     worker.shutdown()
     worker.engine.close()
+
+
+def test_kv_consumer_loads_but_never_saves():
+    import pytest
+
+    cfg = LMCacheEngineConfig.from_defaults(chunk_size=256, max_local_cpu_size=0.05)
+    worker = LMCacheConnectorV1Impl("worker", cfg, "m", BS, kv_role="kv_consumer")
+    kv = _kv()
+    worker.register_kv_caches(kv)
+    sched = LMCacheConnectorV1Impl("scheduler", cfg, "m", BS, engine=worker.engine,
+                                   kv_role="kv_consumer")
+    prompt = list(range(3000, 3600))
+    req = SimpleNamespace(request_id="C", prompt_token_ids=prompt)
+    sched.get_num_new_matched_tokens(req, 0)
+    sched.update_state_after_alloc(req, None, 0)
+    new = SimpleNamespace(req_id="C", prompt_token_ids=prompt, block_ids=(list(range(38)),),
+                          num_computed_tokens=0)
+    meta = sched.build_connector_meta(_sched_out([new], scheduled={"C": 600}))
+    _fill(kv, _slots(list(range(38)), 600), seed=3)
+    _step(worker, meta)
+    assert worker.engine.lookup(torch.tensor(prompt)) == 0  # nothing was stored
+    with pytest.raises(ValueError):
+        LMCacheConnectorV1Impl("worker", cfg, "m", BS, kv_role="kv_sideways")
+    worker.shutdown()
+    worker.engine.close()
