@@ -74,6 +74,64 @@ class _StoreRequest:
     error: Optional[BaseException] = None
 
 
+class _LazyLayers:
+    """Per-layer chunk objects of a layerwise retrieve, fetched from the tiers
+    when the connector first asks for a layer, so the CPU-tier lookups of
+    later layers overlap the transfers of earlier ones.  A chunk missing in a
+    later layer (evicted despite the lookup pin) borrows the same chunk's
+    object of the previous layer (same shape) and ends the usable prefix
+    there: the caller recomputes, and overwrites, those tokens."""
+
+    def __init__(self, storage_manager, chunk_layer_keys, num_layers: int):
+        self.sm = storage_manager
+        self.keys = chunk_layer_keys  # [chunk][layer]
+        self.L = num_layers
+        self.rows: Dict[int, List[MemoryObj]] = {}
+        self.owned: List[MemoryObj] = []
+        self.complete = len(chunk_layer_keys)
+
+    def prefix_of_layer0(self) -> int:
+        got = self.sm.batched_get([ks[0] for ks in self.keys])
+        n = 0
+        while n < len(got) and got[n] is not None:
+            n += 1
+        for o in got[n:]:
+            if o is not None:
+                o.ref_count_down()
+        self.keys = self.keys[:n]
+        self.complete = n
+        self.rows[0] = list(got[:n])
+        self.owned.extend(got[:n])
+        return n
+
+    def __len__(self) -> int:
+        return self.L
+
+    def __getitem__(self, layer: int) -> List[MemoryObj]:
+        row = self.rows.get(layer)
+        if row is None:
+            got = self.sm.batched_get([ks[layer] for ks in self.keys])
+            prev = self[layer - 1]
+            row = []
+            for c, o in enumerate(got):
+                if o is None:
+                    self.complete = min(self.complete, c)
+                    row.append(prev[c])
+                else:
+                    self.owned.append(o)
+                    row.append(o)
+            self.rows[layer] = row
+        return row
+
+    def __iter__(self):
+        return (self[l] for l in range(self.L))
+
+    def release(self) -> None:
+        for o in self.owned:
+            o.ref_count_down()
+        self.owned = []
+
+
 class LMCacheEngine:
     def __init__(self, config: LMCacheEngineConfig, metadata: LMCacheEngineMetadata,
                  gpu_connector: GPUConnectorInterface,
@@ -433,40 +491,33 @@ class LMCacheEngine:
         n = len(tokens)
         ret = torch.zeros(n, dtype=torch.bool)
         chunks = self._chunks(tokens, mask)
-        per_layer: List[List[MemoryObj]] = []
+        sm = self.storage_manager
+        # the hit: chunks whose last layer is stored (store_layer puts layers
+        # in order, so the last layer present means every layer is)
         hit = 0
-        # every layer key of every chunk in one batched get (chunk-major)
-        all_keys = [lk for _, _, k in chunks for lk in k.split_layers(L)]
-        got = self.storage_manager.batched_get(all_keys) if all_keys else []
-        for ci in range(len(chunks)):
-            objs = got[ci * L:(ci + 1) * L]
-            if hit < ci or any(o is None for o in objs):  # the hit prefix ended
-                for o in objs:
-                    if o is not None:
-                        o.ref_count_down()
-                continue
-            if not per_layer:
-                per_layer = [[] for _ in range(L)]
-            for layer, o in enumerate(objs):
-                per_layer[layer].append(o)
+        for _, _, k in chunks:
+            if sm.contains(k.layer_key(L - 1)) is None:
+                break
             hit += 1
         chunks = chunks[:hit]
+        layers = _LazyLayers(sm, [k.split_layers(L) for _, _, k in chunks], L)
+        if hit:
+            hit = layers.prefix_of_layer0()  # layer 0 now; later layers on demand
+            chunks = chunks[:hit]
         starts = [s for s, _, _ in chunks]
         ends = [e for _, e, _ in chunks]
         yield None
         if hit:
             gen = conn.batched_to_gpu(None, starts, ends, slot_mapping=kwargs["slot_mapping"])
             next(gen)
-            gen.send(per_layer)
+            gen.send(layers)
             for layer in range(1, L):
                 yield None
                 next(gen)
             yield None
             next(gen, None)
-            for row in per_layer:
-                for o in row:
-                    o.ref_count_down()
-            for s, e in zip(starts, ends):
+            layers.release()
+            for s, e in zip(starts[:layers.complete], ends[:layers.complete]):
                 ret[s:e] = True
         else:
             for _ in range(L):

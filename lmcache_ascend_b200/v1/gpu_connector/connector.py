@@ -428,15 +428,16 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
                for b in banks]
         with torch.cuda.stream(self.store_stream if store else self.load_stream):
             dev_tables = [d.pin_memory().to(self.device, non_blocking=True) for d in dst]
-        srcs = torch.tensor([[o.data_ptr() for o in row] for row in objs_per_layer],
-                            dtype=torch.int64)
         sizes = torch.tensor([o.get_size() for o in row0], dtype=torch.int64)
-        return dst, dev_tables, srcs, sizes
+        # host addresses are read per layer, when that layer moves: the rows of
+        # later layers may still be being fetched from the CPU tier
+        return dst, dev_tables, objs_per_layer, sizes
 
     def _staged_store_layer(self, plan, layer, starts, ends, slots) -> None:
         from ... import ops
 
-        bank_ptrs, dev_tables, host_ptrs, sizes = plan
+        bank_ptrs, dev_tables, objs, sizes = plan
+        host = torch.tensor([o.data_ptr() for o in objs[layer]], dtype=torch.int64)
         b = layer & 1
         if self._lws_free[b] is not None:  # the bank's previous copy-out must be done
             self.store_stream.wait_event(self._lws_free[b])
@@ -449,7 +450,7 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
             gathered.record(self.store_stream)
         self.copy_stream.wait_event(gathered)
         with torch.cuda.stream(self.copy_stream):
-            ops.native().layerwise_prefill_dma_copy(host_ptrs[layer], bank_ptrs[b], sizes)
+            ops.native().layerwise_prefill_dma_copy(host, bank_ptrs[b], sizes)
             free = torch.cuda.Event()
             free.record(self.copy_stream)
         self._lws_free[b] = free
@@ -457,12 +458,13 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
     def _staged_load_layer(self, plan, layer, starts, ends, slots) -> None:
         from ... import ops
 
-        dst, dev_tables, srcs, sizes = plan
+        dst, dev_tables, objs, sizes = plan
+        srcs_l = torch.tensor([o.data_ptr() for o in objs[layer]], dtype=torch.int64)
         b = layer & 1
         if self._lw_free[b] is not None:  # the bank's previous scatter must be done
             self.copy_stream.wait_event(self._lw_free[b])
         with torch.cuda.stream(self.copy_stream):
-            ops.native().layerwise_prefill_dma_copy(dst[b], srcs[layer], sizes)
+            ops.native().layerwise_prefill_dma_copy(dst[b], srcs_l, sizes)
             copied = torch.cuda.Event()
             copied.record(self.copy_stream)
         self.load_stream.wait_event(copied)

@@ -228,3 +228,27 @@ def test_key_hash_cache_is_not_pickled():
     out = subprocess.run([sys.executable, "-c", code], input=blob, capture_output=True,
                          env={**__import__("os").environ, "PYTHONHASHSEED": "123"})
     assert out.stdout.strip() == b"1", out.stderr
+
+
+def test_layerwise_retrieve_survives_a_chunk_evicted_between_layers():
+    L = 4
+    kv = make_separate_kv(L, 32, 16, 2, 16, torch.float32, "cpu")
+    eng, conn = _engine(kv, chunk=64, layerwise=True)
+    tokens = torch.arange(192)
+    slots = random_slots(192, 512, seed=9)
+    exp = _rows(conn.layout, slots)
+    for _ in eng.store_layer(tokens, slot_mapping=slots):
+        pass
+    cpu = eng.storage_manager.backends["LocalCPUBackend"]
+    conn.register_kv_caches(zeros_like_kv(kv))
+    slots2 = random_slots(192, 512, seed=10)
+    gen = eng.retrieve_layer(tokens, slot_mapping=slots2)
+    next(gen)  # lookup done: all 3 chunks hit
+    keys = [k for _, _, k in eng._chunks(tokens)]
+    cpu.remove(keys[1].layer_key(2))  # chunk 1 of layer 2 goes away mid-retrieve
+    ret = list(gen)[-1]
+    assert int(ret.sum()) == 64 and bool(ret[:64].all())  # usable prefix: chunk 0
+    got = _rows(conn.layout, slots2)  # [L, T, E]
+    assert torch.equal(got[:, :64], exp[:, :64])
+    assert cpu.allocator.num_active == len(cpu.keys())  # no leaked references
+    eng.close()
