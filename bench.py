@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--ttft-requests", type=int, default=8)
     ap.add_argument("--no-fp8", action="store_true",
                     help="skip the block-scaled fp8 push measurement")
+    ap.add_argument("--fp8-tile", type=int, default=512,
+                    help="tokens per fp8 push unit (one flag release per unit)")
     return ap.parse_args()
 
 
@@ -282,12 +284,13 @@ def main():
             if role_p:
                 send8.connect([ReceiverDesc.from_dict(d8[rank + world // 2])])
             dist.barrier(group=gloo)
-        tg8 = ([recv8.expect(T, tile_tokens=a.tile) for _ in range(a.warmup + a.steps)]
+        tg8 = ([recv8.expect(T, tile_tokens=a.fp8_tile) for _ in range(a.warmup + a.steps)]
                if recv8 is not None else [None] * (a.warmup + a.steps))
 
         def step8(i):
             if send8 is not None:
-                send8.push(src_slots, dst_slots, tile_tokens=a.tile, grid=a.grid, quant="fp8")
+                send8.push(src_slots, dst_slots, tile_tokens=a.fp8_tile, grid=a.grid,
+                           quant="fp8")
             if recv8 is not None:  # dequantise each 8-layer group as soon as it landed
                 for l0 in range(0, L, 8):
                     n8 = min(8, L - l0)

@@ -296,6 +296,19 @@ def bench_push(small: bool):
         _emit("push_loopback_" + ("tma_copy" if engine == "auto" else "push_kernel"), ms,
               moved, tokens=T, layers=L)
         send.check()
+    # fp8 push kernel alone (into the receiver's staging; local stores here)
+    recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=T)
+    send = PushSender(PagedKVLayout(src), engine="push")
+    send.connect([recv.desc])
+    wire = T * L * 2 * (H * D + (H * D // 128) * 4)
+    for tile in (128, 512):
+        ms = _time(lambda: send.push(ss, ds, quant="fp8", tile_tokens=tile))
+        _emit(f"push_loopback_fp8_kernel_tile{tile}", ms, moved, traffic_bytes=moved + wire,
+              tokens=T, layers=L, wire_bytes=wire)
+    ms = _time(lambda: recv.dequantize(ds))
+    _emit("push_fp8_dequantize", ms, moved, traffic_bytes=moved + wire, tokens=T, layers=L)
+    send.check()
+    recv.check()
 
 
 CASES = {"gather": bench_gather_scatter, "offload": bench_offload, "cachegen": bench_cachegen,

@@ -429,6 +429,10 @@ __device__ __forceinline__ uint32_t cg_word(const uint4 &v, int j) {
   return cg_bswap(w);
 }
 
+// kWide (bins > 64): the table holds 32-bit entries and keeps a multi-symbol
+// range's first symbol and nibble mask in the entry itself (no pool lookup):
+// 1 KB per channel, worth it when long codes are common.
+template <bool kWide>
 __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
     const int16_t *__restrict__ cdf, const uint8_t *__restrict__ bytes,
     const int32_t *__restrict__ cum_len, long long total_bytes, uint8_t *out, int L, int T,
@@ -450,10 +454,28 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
     w = (p & 1) ? ((w & 0xFFFFu) | (v << 16)) : ((w & 0xFFFF0000u) | v);
   };
   const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
+  if constexpr (kWide) {
+    for (int p = 0; p < kCgLut; ++p) lut[p * kDecCh + tid] = 8u << 8;  // symbol 0, 8 bits
+    for (int s = 0; s < bins; ++s) {
+      const unsigned e = static_cast<unsigned short>(__ldg(cd + s));
+      const unsigned ln = e & 0xFu;
+      const unsigned st = e & 0xFFF0u;
+      if (ln <= 8) {
+        const unsigned en = min(65536u, st + (1u << (16 - ln)));
+        for (unsigned p = st >> 8; p < (en >> 8); ++p)
+          lut[p * kDecCh + tid] = (ln << 8) | static_cast<unsigned>(s);
+      } else {
+        uint32_t &w = lut[(st >> 8) * kDecCh + tid];
+        const uint32_t bit = 1u << (8 + ((st >> 4) & 0xFu));
+        w = (w & 0x80000000u) ? (w | bit) : (0x80000000u | bit | static_cast<unsigned>(s));
+      }
+    }
+  }
   const uint32_t dflt = (8u << 8) | ((8u << 8) << 16);  // safe default: symbol 0, 8 bits
-  for (int p = 0; p < kCgLut / 2; ++p) lut[p * kDecCh + tid] = dflt;
+  if constexpr (!kWide)
+    for (int p = 0; p < kCgLut / 2; ++p) lut[p * kDecCh + tid] = dflt;
   int used = 0;
-  for (int s = 0; s < bins; ++s) {
+  for (int s = 0; s < (kWide ? 0 : bins); ++s) {
     const unsigned e = static_cast<unsigned short>(__ldg(cd + s));
     const unsigned ln = e & 0xFu;
     const unsigned st = e & 0xFFF0u;
@@ -506,14 +528,23 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
   auto decode1 = [&]() -> unsigned {
     const unsigned v = static_cast<unsigned>(win >> 48);
     const unsigned p = v >> 8;
-    const uint32_t w = my[(p >> 1) * kDecCh];
-    const unsigned h = (p & 1) ? (w >> 16) : (w & 0xFFFFu);
     unsigned sym, ln;
-    if (!(h & 0x8000u)) {
+    uint32_t e = 0;
+    bool single;
+    if constexpr (kWide) {
+      e = my[p * kDecCh];
+      single = !(e & 0x80000000u);
+      sym = e & 0xFFu;
+      ln = (e >> 8) & 0xFu;
+    } else {
+      const uint32_t w = my[(p >> 1) * kDecCh];
+      const unsigned h = (p & 1) ? (w >> 16) : (w & 0xFFFFu);
+      single = !(h & 0x8000u);
       sym = h & 0xFFu;
       ln = (h >> 8) & 0xFu;
-    } else {
-      const uint32_t e = pool[(h & 0xFFu) * kDecCh + tid];
+      if (!single) e = pool[(h & 0xFFu) * kDecCh + tid];
+    }
+    if (!single) {
       const unsigned nib = (v >> 4) & 0xFu;
       const unsigned m = (e >> 8) & 0xFFFFu;
       const unsigned below = (m & ((2u << nib) - 1u)) | 1u;  // bit 0: the first symbol
@@ -811,12 +842,21 @@ void decode_fast_prefsum(const at::Tensor &cdf, const at::Tensor &bytestreams,
   const c10::cuda::CUDAGuard guard(c.device());
   if (L == 0 || C == 0 || T == 0) return;
   dim3 grid((C + kDecCh - 1) / kDecCh, L);
-  const size_t smem = (kCgLut / 2 + std::max(1, bins / 2)) * kDecCh * 4;
-  cg_smem_attr(reinterpret_cast<const void *>(cg_decode_kernel), smem);
-  cg_decode_kernel<<<grid, kDecCh, smem, at::cuda::getCurrentCUDAStream().stream()>>>(
-      c.data_ptr<int16_t>(), reinterpret_cast<const uint8_t *>(b.data_ptr()),
-      len.data_ptr<int32_t>(), static_cast<long long>(b.numel()),
-      reinterpret_cast<uint8_t *>(output.data_ptr()), L, T, C, bins);
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  const auto *bp = reinterpret_cast<const uint8_t *>(b.data_ptr());
+  auto *op8 = reinterpret_cast<uint8_t *>(output.data_ptr());
+  const long long nbytes = static_cast<long long>(b.numel());
+  if (bins > 64) {
+    const size_t smem = static_cast<size_t>(kCgLut) * kDecCh * 4;
+    cg_smem_attr(reinterpret_cast<const void *>(cg_decode_kernel<true>), smem);
+    cg_decode_kernel<true><<<grid, kDecCh, smem, stream>>>(
+        c.data_ptr<int16_t>(), bp, len.data_ptr<int32_t>(), nbytes, op8, L, T, C, bins);
+  } else {
+    const size_t smem = (kCgLut / 2 + std::max(1, bins / 2)) * kDecCh * 4;
+    cg_smem_attr(reinterpret_cast<const void *>(cg_decode_kernel<false>), smem);
+    cg_decode_kernel<false><<<grid, kDecCh, smem, stream>>>(
+        c.data_ptr<int16_t>(), bp, len.data_ptr<int32_t>(), nbytes, op8, L, T, C, bins);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -320,51 +320,97 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
   }
 }
 
-// Decoder side: staging (fp8 + scales, push order) -> bf16 paged cache at
-// dst_slots[t].  Thread per 8 elements (one 16-byte store).
-__global__ void __launch_bounds__(256) pd_dequant_scatter_kernel(
+// Decoder side of the fp8 push: staging (fp8 rows + per-group scales) ->
+// bf16 paged rows at dst_slots.  Same shape as the quantising push kernel run
+// backwards: a CTA takes (layer, plane, tile of tokens) units, so the index
+// math is per unit; an 8-lane quarter-warp owns one token's 128-element
+// segments (lane i: elements 16i .. 16i+15, one 16-byte fp8 load and two
+// 16-byte bf16 stores), and each lane keeps kDqSegs segments of loads in
+// flight.  SPR: 128-element segments per row (upper bound; `spr` is exact).
+constexpr int kDqWarps = 8;
+constexpr int kDqSegs = 8;
+constexpr int kDqTile = 256;
+
+template <int SPR>
+__global__ void __launch_bounds__(kDqWarps * 32) pd_dequant_scatter_kernel(
     PagedDesc dst, const uint8_t *__restrict__ q, const float *__restrict__ scales,
     const void *dst_slots, int slot_is_i64, int num_tokens, int layer_begin, int num_layers,
     int group, DeviceStatus *status) {
+  constexpr int kTok = SPR >= kDqSegs ? 1 : kDqSegs / SPR;  // tokens per quarter in flight
+  constexpr int kQuarters = kDqWarps * 4;
   const int np = dst.num_planes;
-  const long long nth = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (int p = 0; p < np; ++p) {
+  const int row_elems = dst.plane[0].row_bytes >> 1;  // every plane has the same rows
+  const int spr = row_elems >> 7;
+  const int gpr = row_elems / group;
+  const int tiles = (num_tokens + kDqTile - 1) / kDqTile;
+  const int units_per_layer = np * tiles;
+  const int total = units_per_layer * num_layers;
+  const int quarter = threadIdx.x >> 3;
+  const int ql = threadIdx.x & 7;
+  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    const int li = u / units_per_layer;
+    const int rem = u - li * units_per_layer;
+    const int p = rem / tiles;
+    const int tile = rem - p * tiles;
+    const int layer = layer_begin + li;
     const PlaneDesc pl = plane_of(dst, p);
-    const int row_elems = pl.row_bytes >> 1;
-    const int vpr = row_elems >> 3;
-    const int gpr = row_elems / group;
-    const long long total = static_cast<long long>(num_layers) * num_tokens * vpr;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += nth) {
-      const int vi = static_cast<int>(i % vpr);
-      const long long lt = i / vpr;
-      const int t = static_cast<int>(lt % num_tokens);
-      const int li = static_cast<int>(lt / num_tokens);
-      const int layer = layer_begin + li;
-      const int64_t ds = push_slot(dst_slots, slot_is_i64, t);
-      if (ds < 0) continue;
-      if (ds >= dst.num_slots) {
-        if (vi == 0) report_status(status, kStatusBadSlot, t, ds, dst.num_slots);
-        continue;
-      }
-      const int64_t row = (static_cast<int64_t>(layer) * np + p) * num_tokens + t;
-      const uint2 w = *reinterpret_cast<const uint2 *>(q + row * row_elems + vi * 8);
-      const float sc = scales[row * gpr + (vi * 8) / group];
-      const uint32_t ww[2] = {w.x, w.y};
-      uint32_t out[4];
+    char *dbase = reinterpret_cast<char *>(dst.ptrs[layer * np + p]);
+    const int t0 = tile * kDqTile;
+    const int n = min(num_tokens - t0, kDqTile);
+    const int64_t row0 = (static_cast<int64_t>(layer) * np + p) * num_tokens + t0;
+    for (int base = 0; base < n; base += kQuarters * kTok) {
+      uint4 w[kTok][SPR];
+      float sc[kTok][SPR];
+      int64_t ds[kTok];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
+      for (int k = 0; k < kTok; ++k) {
+        const int ti = base + k * kQuarters + quarter;
+        ds[k] = -1;
+        if (ti < n) {
+          ds[k] = push_slot(dst_slots, slot_is_i64, t0 + ti);
+          const int64_t row = row0 + ti;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
-              static_cast<__nv_fp8x2_storage_t>((ww[e] >> (16 * h)) & 0xFFFFu), __NV_E4M3);
-          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
-          const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * sc, f.y * sc);
-          out[e * 2 + h] = *reinterpret_cast<const uint32_t *>(&b);
+          for (int s = 0; s < SPR; ++s) {
+            if (s < spr) {
+              w[k][s] = __ldg(reinterpret_cast<const uint4 *>(q + row * row_elems + s * 128 +
+                                                              ql * 16));
+              sc[k][s] = __ldg(scales + row * gpr + (s * 128) / group);
+            }
+          }
         }
       }
-      char *pa = paged_addr(dst, layer, p, ds) + seg_off(pl, static_cast<unsigned>(vi * 16));
-      *reinterpret_cast<uint4 *>(pa) = make_uint4(out[0], out[1], out[2], out[3]);
+#pragma unroll
+      for (int k = 0; k < kTok; ++k) {
+        if (ds[k] < 0) continue;
+        if (ds[k] >= dst.num_slots) {
+          if (ql == 0) report_status(status, kStatusBadSlot, t0 + base + k * kQuarters + quarter,
+                                     ds[k], dst.num_slots);
+          continue;
+        }
+        char *prow = dbase + row_off(dst, pl, static_cast<unsigned>(ds[k]));
+#pragma unroll
+        for (int s = 0; s < SPR; ++s) {
+          if (s >= spr) continue;
+          const uint32_t ww[4] = {w[k][s].x, w[k][s].y, w[k][s].z, w[k][s].w};
+          uint32_t out[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+                  static_cast<__nv_fp8x2_storage_t>((ww[e] >> (16 * h)) & 0xFFFFu), __NV_E4M3);
+              const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
+              const __nv_bfloat162 bv = __floats2bfloat162_rn(f.x * sc[k][s], f.y * sc[k][s]);
+              out[e * 2 + h] = *reinterpret_cast<const uint32_t *>(&bv);
+            }
+          }
+          const unsigned vb = static_cast<unsigned>(s * 128 + ql * 16) * 2u;
+          *reinterpret_cast<uint4 *>(prow + seg_off(pl, vb)) =
+              make_uint4(out[0], out[1], out[2], out[3]);
+          *reinterpret_cast<uint4 *>(prow + seg_off(pl, vb + 16)) =
+              make_uint4(out[4], out[5], out[6], out[7]);
+        }
+      }
     }
   }
 }
@@ -573,12 +619,39 @@ void pd_dequant_scatter(const PagedLayout &dst, int64_t q_ptr, int64_t scale_ptr
   const int dev = dst_slots.device().index();
   DeviceStatus *st = status.has_value() ? reinterpret_cast<DeviceStatus *>(status->data_ptr())
                                         : nullptr;
-  pd_dequant_scatter_kernel<<<num_sms(dev) * 8, 256, 0,
-                              at::cuda::getCurrentCUDAStream(dev).stream()>>>(
-      dst.desc(), reinterpret_cast<const uint8_t *>(q_ptr),
-      reinterpret_cast<const float *>(scale_ptr), dst_slots.data_ptr(),
-      dst_slots.scalar_type() == at::kLong, static_cast<int>(dst_slots.numel()),
-      static_cast<int>(layer_begin), static_cast<int>(num_layers), static_cast<int>(group), st);
+  TORCH_CHECK(num_layers * dst.desc().num_planes * dst_slots.numel() < (1LL << 31),
+              "dequant scatter: too many rows for one launch");
+  const int rb = dst.desc().plane[0].row_bytes;
+  TORCH_CHECK(rb % 256 == 0 && rb <= 8 * 256,
+              "dequant scatter: rows of 128 .. 1024 bf16 elements, in 128-element pieces");
+  for (int p = 0; p < dst.desc().num_planes; ++p) {
+    const int64_t nblk = (dst.desc().num_slots + dst.desc().block_size - 1) / dst.desc().block_size;
+    TORCH_CHECK(nblk * dst.desc().plane[p].block_stride < (1LL << 32) - 1,
+                "dequant scatter: each layer plane must span less than 4 GiB");
+  }
+  const auto stream = at::cuda::getCurrentCUDAStream(dev).stream();
+  const auto *qp = reinterpret_cast<const uint8_t *>(q_ptr);
+  const auto *sp = reinterpret_cast<const float *>(scale_ptr);
+  const int is64 = dst_slots.scalar_type() == at::kLong;
+  const int n = static_cast<int>(dst_slots.numel());
+  const long long units = static_cast<long long>(dst.desc().num_planes) *
+                          ((n + kDqTile - 1) / kDqTile) * num_layers;
+  const int g = static_cast<int>(std::max(1LL, std::min<long long>(units, num_sms(dev) * 8)));
+  auto go = [&](auto spr) {
+    constexpr int V = decltype(spr)::value;
+    pd_dequant_scatter_kernel<V><<<g, kDqWarps * 32, 0, stream>>>(
+        dst.desc(), qp, sp, dst_slots.data_ptr(), is64, n, static_cast<int>(layer_begin),
+        static_cast<int>(num_layers), static_cast<int>(group), st);
+  };
+  const int spr = rb / 256;
+  if (spr <= 1)
+    go(std::integral_constant<int, 1>());
+  else if (spr <= 2)
+    go(std::integral_constant<int, 2>());
+  else if (spr <= 4)
+    go(std::integral_constant<int, 4>());
+  else
+    go(std::integral_constant<int, 8>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
