@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--ttft-requests", type=int, default=8)
     ap.add_argument("--no-fp8", action="store_true",
                     help="skip the block-scaled fp8 push measurement")
+    ap.add_argument("--multicast", action="store_true",
+                    help="also time the NVLS fan-out (rank 0 -> every other rank), N > 1")
     ap.add_argument("--fp8-tile", type=int, default=512,
                     help="tokens per fp8 push unit (one flag release per unit)")
     return ap.parse_args()
@@ -324,6 +326,50 @@ def main():
         if send8 is not None:
             send8.close()
 
+    # ------------------------------------------------ NVLS fan-out (opt-in)
+    # Rank 0 writes the whole cache once through the multicast address of a
+    # symmetric staging buffer; NVSwitch delivers it to every rank; the
+    # decoders scatter it into their paged caches.  Steps are separated by a
+    # host barrier (one staging buffer), each timed on its own: receivers
+    # measure wait + scatter from before the push starts, rank 0 the push.
+    mcast = None
+    if a.multicast and world > 1 and a.impl == "ours":
+        from lmcache_ascend_b200.parallel.pd_multicast import MulticastFanout
+
+        fan = MulticastFanout(dist.group.WORLD, L, 2, H * D * 2, T, dev)
+        if fan.has_multicast:
+            src_l = PagedKVLayout(src_cache) if rank == 0 else None
+            dst_l = PagedKVLayout(dst_cache) if dst_cache is not None else None
+            per = []
+            for i in range(a.warmup + a.steps):
+                tg = fan.expect(T, tile_tokens=a.tile)
+                barrier()
+                m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                m0.record()
+                if rank == 0:
+                    fan.push(src_l, src_slots, tile_tokens=a.tile)
+                fan.wait(tg, timeout_s=5.0)
+                if dst_l is not None:
+                    fan.scatter(dst_l, dst_slots, T)
+                m1.record()
+                torch.cuda.synchronize()
+                if i >= a.warmup:
+                    per.append(m0.elapsed_time(m1))
+            fan.check()
+            mms = torch.tensor([sum(per) / len(per)], device=dev)
+            dist.all_reduce(mms, op=dist.ReduceOp.MAX)
+            mms = float(mms.item())
+            receivers = world - 1
+            mcast = {"ms_per_step": round(mms, 4), "receivers": receivers,
+                     "egress_gbps": round(bytes_per_pair / (mms / 1e3) / 1e9, 2),
+                     "delivered_gbps": round(bytes_per_pair * receivers / (mms / 1e3) / 1e9, 2),
+                     "note": "rank 0 -> all ranks through one multicast store per vector; "
+                             "decoder scatter included; host barrier between steps"}
+        else:
+            mcast = {"unavailable": "no NVLink multicast on this system"}
+        barrier()
+        del fan
+
     # ------------------------------------------------------------ e2e arm
     # Same transfer through the engine's public API: the prefiller calls
     # LMCacheEngine.store_direct_prefill (PD backend handshake + fused push),
@@ -447,7 +493,7 @@ def main():
              "config": cfg, "bytes_per_pair_per_step": bytes_per_pair,
              "per_pair_gbps": round(per_pair, 2), "roofline": roof,
              "clocks": ck, "e2e": e2e, "gpu_launches": launches, "ttft": ttft,
-             "push_fp8": fp8})
+             "push_fp8": fp8, **({"multicast": mcast} if mcast is not None else {})})
     if sender is not None:
         sender.close()
     if world > 1:

@@ -36,10 +36,16 @@ class MulticastFanout:
                                   device=self.device)
         self.buf.zero_()
         self.handle = symm_mem.rendezvous(self.buf, group)
-        self.has_multicast = bool(self.handle.has_multicast_support())
-        self.mc = int(self.handle.multicast_ptr) if self.has_multicast else 0
+        from torch._C._autograd import DeviceType
+
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.has_multicast = bool(
+            symm_mem._SymmetricMemory.has_multicast_support(DeviceType.CUDA, idx))
+        self.mc = self._multicast_addr() if self.has_multicast else 0
+        self.has_multicast = self.mc != 0
         torch.cuda.synchronize(self.device)
-        self.handle.barrier()  # zeroed flags visible to every member before any push
+        # zeroed flags visible to every member before any push (bounded wait)
+        self.handle.barrier(0, 30000)
         self.expected = [0] * num_layers
         self.status = ops.DeviceStatus(self.device)
         # row ((layer * planes + p) * T + t): plane p starts p * rb * T in,
@@ -47,6 +53,22 @@ class MulticastFanout:
         rb, npl = row_bytes, num_planes
         self._chunk_layout = ops.native().ChunkLayout([rb] * npl, npl * rb, [rb] * npl,
                                                       [0] * npl)
+
+    def _multicast_addr(self) -> int:
+        """Multicast address of ``self.buf``'s first byte, or 0 when the
+        tensor cannot be located inside the handle's allocation (multicast is
+        then left off rather than storing at an unverified address)."""
+        mc = int(self.handle.multicast_ptr)
+        if mc == 0:
+            return 0
+        base = int(self.handle.buffer_ptrs[self.handle.rank])
+        off = int(getattr(self.handle, "offset", 0) or 0)
+        data = self.buf.data_ptr()
+        if data == base + off:
+            return mc + off
+        if data == base and off == 0:
+            return mc
+        return 0
 
     # ------------------------------------------------------------ sender
     def push(self, layout: PagedKVLayout, src_slots: torch.Tensor, tile_tokens: int = 128,
