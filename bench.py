@@ -329,7 +329,8 @@ def main():
     # ------------------------------------------------ NVLS fan-out (opt-in)
     # Rank 0 writes the whole cache once through the multicast address of a
     # symmetric staging buffer; NVSwitch delivers it to every rank; the
-    # decoders scatter it into their paged caches.  Steps are separated by a
+    # decoders scatter each 8-layer group into their paged caches as soon as
+    # its flags complete.  Steps are separated by a
     # host barrier (one staging buffer), each timed on its own: receivers
     # measure wait + scatter from before the push starts, rank 0 the push.
     mcast = None
@@ -348,9 +349,11 @@ def main():
                 m0.record()
                 if rank == 0:
                     fan.push(src_l, src_slots, tile_tokens=a.tile)
-                fan.wait(tg, timeout_s=5.0)
-                if dst_l is not None:
-                    fan.scatter(dst_l, dst_slots, T)
+                for l0 in range(0, L, 8):  # scatter each 8-layer group as it lands
+                    n8 = min(8, L - l0)
+                    fan.wait(tg[l0:l0 + n8], timeout_s=5.0, layer_begin=l0)
+                    if dst_l is not None:
+                        fan.scatter(dst_l, dst_slots, T, layer_begin=l0, num_layers=n8)
                 m1.record()
                 torch.cuda.synchronize()
                 if i >= a.warmup:

@@ -16,6 +16,8 @@ then use ``PushSender`` fan-out (one peer store per decoder).
 
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 
 from .. import ops
@@ -91,14 +93,19 @@ class MulticastFanout:
                       else self.expected[l])
         return torch.tensor(tg, dtype=torch.int32).to(self.device, non_blocking=True)
 
-    def wait(self, targets: torch.Tensor, timeout_s: float = 10.0) -> None:
-        ops.native().pd_wait_flags(self.buf.data_ptr() + self.flags_off, targets, 0,
+    def wait(self, targets: torch.Tensor, timeout_s: float = 10.0, layer_begin: int = 0) -> None:
+        """Bounded device wait until layers ``layer_begin ..`` (one target
+        each, from ``expect``) have landed in this member's staging."""
+        ops.native().pd_wait_flags(self.buf.data_ptr() + self.flags_off, targets, layer_begin,
                                    timeout_s, self.status.tensor)
 
-    def scatter(self, layout: PagedKVLayout, dst_slots: torch.Tensor, num_tokens: int) -> None:
-        """Local staging rows of the last push -> this member's paged cache."""
+    def scatter(self, layout: PagedKVLayout, dst_slots: torch.Tensor, num_tokens: int,
+                layer_begin: int = 0, num_layers: Optional[int] = None) -> None:
+        """Local staging rows of the last push -> this member's paged cache
+        (layers ``layer_begin .. layer_begin + num_layers``)."""
+        n = self.num_layers - layer_begin if num_layers is None else num_layers
         ops.native().kv_transfer(layout.native(), self.buf, None, self._chunk_layout,
-                                 num_tokens, 0, 0, True, dst_slots, 0, 0, self.num_layers,
+                                 num_tokens, 0, 0, True, dst_slots, layer_begin, layer_begin, n,
                                  False, 0, self.status.tensor, None, 0, None)
 
     def check(self) -> None:

@@ -42,6 +42,11 @@ def _worker(rank, world, port, q):
         if not fan.has_multicast:
             q.put((rank, "no-multicast"))
             return
+        def same():
+            return all(torch.equal(src[l][p].view(NB * BS, -1)[ss.long()],
+                                   dst[l][p].view(NB * BS, -1)[ds.long()])
+                       for l in range(L) for p in range(2))
+
         tg = fan.expect(T)
         if rank == 0:
             fan.push(PagedKVLayout(src), ss)
@@ -49,9 +54,21 @@ def _worker(rank, world, port, q):
         fan.scatter(PagedKVLayout(dst), ds, T)
         torch.cuda.synchronize()
         fan.check()
-        ok = all(torch.equal(src[l][p].view(NB * BS, -1)[ss.long()],
-                             dst[l][p].view(NB * BS, -1)[ds.long()])
-                 for l in range(L) for p in range(2))
+        ok = same()
+        # second push, consumed two layers at a time as each pair lands
+        for l in range(L):
+            for p in range(2):
+                dst[l][p].zero_()
+        dist.barrier()
+        tg = fan.expect(T)
+        if rank == 0:
+            fan.push(PagedKVLayout(src), ss)
+        for l0 in range(0, L, 2):
+            fan.wait(tg[l0:l0 + 2], timeout_s=5.0, layer_begin=l0)
+            fan.scatter(PagedKVLayout(dst), ds, T, layer_begin=l0, num_layers=2)
+        torch.cuda.synchronize()
+        fan.check()
+        ok = ok and same()
         dist.barrier()
         q.put((rank, "ok" if ok else "mismatch"))
     except Exception as e:  # report, do not hang the parent
