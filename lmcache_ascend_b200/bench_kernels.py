@@ -302,7 +302,9 @@ def bench_push(small: bool):
     send.connect([recv.desc])
     wire = T * L * 2 * (H * D + (H * D // 128) * 4)
     for tile in (128, 512):
-        ms = _time(lambda: send.push(ss, ds, quant="fp8", tile_tokens=tile))
+        # the release hands the staging buffer back (no dequant in this case)
+        ms = _time(lambda: (send.push(ss, ds, quant="fp8", tile_tokens=tile),
+                            recv.release_staging()))
         _emit(f"push_loopback_fp8_kernel_tile{tile}", ms, moved, traffic_bytes=moved + wire,
               tokens=T, layers=L, wire_bytes=wire)
     ms = _time(lambda: recv.dequantize(ds))

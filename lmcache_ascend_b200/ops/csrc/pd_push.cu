@@ -429,6 +429,21 @@ __global__ void pd_wait_flags_kernel(const unsigned *flags,
     report_status(status, kStatusFlagTimeout, layer_begin + i, seen, targets[i]);
 }
 
+// One thread: bounded wait until *flag - target >= 0 (local or peer flag).
+__global__ void pd_wait_value_kernel(const unsigned *flag, unsigned target,
+                                     unsigned long long budget_ns, DeviceStatus *status) {
+  unsigned seen = 0;
+  if (!wait_flag_geq(flag, target, budget_ns, &seen))
+    report_status(status, kStatusFlagTimeout, -1, seen, target);
+}
+
+// One thread: *flag += inc with release semantics, after the stream's
+// earlier work (hands a staging buffer back to its writer).
+__global__ void pd_flag_add_kernel(unsigned *flag, unsigned inc) {
+  fence_acq_rel_sys();
+  red_release_sys_add(flag, inc);
+}
+
 // Positive integer from the environment, else `dflt` (0 or unset = default).
 static int env_int2(const char *name, int dflt) {
   const char *v = std::getenv(name);
@@ -652,6 +667,25 @@ void pd_dequant_scatter(const PagedLayout &dst, int64_t q_ptr, int64_t scale_ptr
     go(std::integral_constant<int, 4>());
   else
     go(std::integral_constant<int, 8>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void pd_wait_value(int64_t flag_ptr, int64_t target, double timeout_s,
+                   const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(flag_ptr % 4 == 0, "flag must be 4-byte aligned");
+  DeviceStatus *st = status.has_value() ? reinterpret_cast<DeviceStatus *>(status->data_ptr())
+                                        : nullptr;
+  const unsigned long long budget =
+      static_cast<unsigned long long>(std::max(0.0, timeout_s) * 1e9);
+  pd_wait_value_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
+      reinterpret_cast<const unsigned *>(flag_ptr), static_cast<unsigned>(target), budget, st);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void pd_flag_add(int64_t flag_ptr, int64_t inc) {
+  TORCH_CHECK(flag_ptr % 4 == 0, "flag must be 4-byte aligned");
+  pd_flag_add_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
+      reinterpret_cast<unsigned *>(flag_ptr), static_cast<unsigned>(inc));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

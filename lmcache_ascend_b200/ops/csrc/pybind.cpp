@@ -50,6 +50,9 @@ void pd_push_multimem(const PagedLayout &src, int64_t mc_rows, int64_t mc_flags,
                       const at::Tensor &src_slots, int64_t layer_begin, int64_t num_layers,
                       int64_t tile_tokens, int64_t grid,
                       const c10::optional<at::Tensor> &status);
+void pd_wait_value(int64_t flag_ptr, int64_t target, double timeout_s,
+                   const c10::optional<at::Tensor> &status);
+void pd_flag_add(int64_t flag_ptr, int64_t inc);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
@@ -167,6 +170,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("num_layers"), py::arg("group") = 128, py::arg("status") = py::none());
   m.def("pd_wait_flags", &pd_wait_flags, py::arg("flags_ptr"), py::arg("targets"),
         py::arg("layer_begin"), py::arg("timeout_s"), py::arg("status") = py::none());
+  m.def("pd_wait_value", &pd_wait_value, py::arg("flag_ptr"), py::arg("target"),
+        py::arg("timeout_s"), py::arg("status") = py::none());
+  m.def("pd_flag_add", &pd_flag_add, py::arg("flag_ptr"), py::arg("inc") = 1);
 
   m.def("calculate_cdf", &calculate_cdf);
   m.def("encode_fast_new", &encode_fast_new, py::arg("cdf"), py::arg("input_sym"),

@@ -20,6 +20,15 @@ stores them into a staging area in the receiver's HBM, so about half the
 bytes cross NVLink; the receiver dequantises into its bf16 paged cache after
 the layer flags (``PushReceiver.dequantize``).  Lossy: the relative error of
 an element is at most 2^-4 of its group's maximum.
+
+The staging area holds ``fp8_buffers`` requests (two by default), used in
+turn.  A push whose ``layer_begin`` is 0 starts a new request in the next
+buffer; before it writes into a buffer that an earlier request used, the
+sender's stream waits (bounded, on the device) until the receiver has released
+that request.  The receiver releases a request when it dequantises the last
+layer (or when ``dequantize(..., release=True)``) by adding 1 to a counter in
+its own HBM.  A wait that runs out reports a flag timeout through the sender's
+status, and the staging contents are then not to be trusted.
 """
 
 from __future__ import annotations
@@ -51,6 +60,10 @@ class ReceiverDesc:
     fp8_scales: Optional[dict] = None   # IpcDesc dict of the staging scales
     fp8_tokens: int = 0                 # staging capacity in tokens per push
     fp8_group: int = 128
+    fp8_buffers: int = 1                # requests the staging holds at once
+    fp8_q_stride: int = 0               # bytes between staging buffers (rows)
+    fp8_s_stride: int = 0               # bytes between staging buffers (scales)
+    fp8_release_index: int = -1         # flag word the receiver bumps per released request
 
     def to_dict(self) -> dict:
         return self.__dict__.copy()
@@ -62,12 +75,13 @@ class ReceiverDesc:
 
 class PushReceiver:
     def __init__(self, layout: PagedKVLayout, max_layers: Optional[int] = None,
-                 fp8_staging_tokens: int = 0, fp8_group: int = 128):
+                 fp8_staging_tokens: int = 0, fp8_group: int = 128, fp8_buffers: int = 2):
         self.layout = layout
         self.device = layout.device
         dev = self.device.index or 0
         n = max(layout.num_layers, max_layers or 0)
-        self._flags_buf = ops.native().device_buffer(4 * max(n, 1), dev)
+        self._release_index = max(n, 1)  # one word after the layer flags
+        self._flags_buf = ops.native().device_buffer(4 * (self._release_index + 1), dev)
         self.flags = self._flags_buf.view(torch.int32)
         self.expected = [0] * n  # cumulative flag target per layer
         self.status = ops.DeviceStatus(self.device)
@@ -95,12 +109,20 @@ class PushReceiver:
                                        False)
             sb = mod.fp8_staging_bytes(nat, fp8_staging_tokens, layout.num_layers, fp8_group,
                                        True)
-            self._q_buf = mod.device_buffer(qb, dev)
-            self._s_buf = mod.device_buffer(sb, dev)
+            if fp8_buffers < 1:
+                raise ValueError("fp8_buffers must be >= 1")
+            sb = (sb + 15) // 16 * 16
+            self._fp8_nb, self._fp8_qb, self._fp8_sb = fp8_buffers, qb, sb
+            self._q_buf = mod.device_buffer(qb * fp8_buffers, dev)
+            self._s_buf = mod.device_buffer(sb * fp8_buffers, dev)
+            self._fp8_seq = 0  # next request to dequantise
             self.desc.fp8_q = export_local(self._q_buf.data_ptr(), dev).to_dict()
             self.desc.fp8_scales = export_local(self._s_buf.data_ptr(), dev).to_dict()
             self.desc.fp8_tokens = fp8_staging_tokens
             self.desc.fp8_group = fp8_group
+            self.desc.fp8_buffers = fp8_buffers
+            self.desc.fp8_q_stride, self.desc.fp8_s_stride = qb, sb
+            self.desc.fp8_release_index = self._release_index
 
     def expect(self, num_tokens: int, layer_begin: int = 0,
                num_layers: Optional[int] = None, tile_tokens: int = 128) -> torch.Tensor:
@@ -122,17 +144,31 @@ class PushReceiver:
                                    timeout_s, self.status.tensor)
 
     def dequantize(self, dst_slots: torch.Tensor, layer_begin: int = 0,
-                   num_layers: Optional[int] = None) -> None:
-        """After ``wait``: fp8 staging of the last push -> bf16 paged cache at
-        ``dst_slots`` (enqueued on the current stream)."""
+                   num_layers: Optional[int] = None, release: Optional[bool] = None) -> None:
+        """After ``wait``: fp8 staging of the current request -> bf16 paged
+        cache at ``dst_slots`` (enqueued on the current stream).  ``release``
+        (default: when the range ends at the last layer) hands the request's
+        staging buffer back to the sender after this dequantisation."""
         if self.fp8_tokens <= 0:
             raise RuntimeError("receiver was built without fp8 staging")
         if dst_slots.numel() > self.fp8_tokens:
             raise ValueError("push larger than the fp8 staging area")
         nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
-        ops.native().pd_dequant_scatter(self.layout.native(), self._q_buf.data_ptr(),
-                                        self._s_buf.data_ptr(), dst_slots, layer_begin, nl,
-                                        self.fp8_group, self.status.tensor)
+        b = self._fp8_seq % self._fp8_nb
+        ops.native().pd_dequant_scatter(self.layout.native(),
+                                        self._q_buf.data_ptr() + b * self._fp8_qb,
+                                        self._s_buf.data_ptr() + b * self._fp8_sb, dst_slots,
+                                        layer_begin, nl, self.fp8_group, self.status.tensor)
+        if release is None:
+            release = layer_begin + nl >= self.layout.num_layers
+        if release:
+            self.release_staging()
+
+    def release_staging(self) -> None:
+        """Hand the current request's fp8 staging buffer back to the sender
+        (stream-ordered after the work already enqueued)."""
+        ops.native().pd_flag_add(self._flags_buf.data_ptr() + 4 * self._release_index, 1)
+        self._fp8_seq += 1
 
     def check(self) -> None:
         self.status.check("pd push receiver")
@@ -179,10 +215,14 @@ class PushSender:
         self._flag_ptrs = [self.peers.resolve(IpcDesc.from_dict(r.flags)) for r in receivers]
         self.replicas = len(receivers)
         self._fp8 = None
+        self._fp8_seq, self._fp8_buf = 0, 0
         if r0.fp8_q is not None and len(receivers) == 1:
+            rel = (self._flag_ptrs[0] + 4 * r0.fp8_release_index
+                   if r0.fp8_release_index >= 0 else 0)
             self._fp8 = (self.peers.resolve(IpcDesc.from_dict(r0.fp8_q)),
                          self.peers.resolve(IpcDesc.from_dict(r0.fp8_scales)),
-                         r0.fp8_tokens, r0.fp8_group)
+                         r0.fp8_tokens, r0.fp8_group, max(1, r0.fp8_buffers),
+                         r0.fp8_q_stride, r0.fp8_s_stride, rel)
         import os
 
         self._local = (self.engine == "auto" and len(receivers) == 1
@@ -191,22 +231,33 @@ class PushSender:
 
     def push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, layer_begin: int = 0,
              num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0,
-             quant: str = "none") -> None:
+             quant: str = "none", staging_timeout_s: float = 10.0) -> None:
         """Enqueue the push of ``num_layers`` layers on the current stream.
         ``quant="fp8"`` sends block-scaled fp8 to the receiver's staging (the
-        receiver applies ``dst_slots`` in ``PushReceiver.dequantize``)."""
+        receiver applies ``dst_slots`` in ``PushReceiver.dequantize``); a push
+        from layer 0 starts a new request in the next staging buffer, after a
+        bounded device wait (``staging_timeout_s``) for the receiver to have
+        released that buffer's previous request."""
         if self._dst is None:
             raise RuntimeError("PushSender.connect() first")
         nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
         if quant == "fp8":
             if self._fp8 is None:
                 raise RuntimeError("fp8 push needs one receiver built with fp8 staging")
-            q_ptr, s_ptr, cap, group = self._fp8
+            q_ptr, s_ptr, cap, group, nb, qst, sst, rel = self._fp8
             if src_slots.numel() > cap:
                 raise ValueError("push larger than the receiver's fp8 staging area")
-            ops.native().pd_push_fp8(self.layout.native(), q_ptr, s_ptr, src_slots,
-                                     layer_begin, nl, self._flag_ptrs[0], tile_tokens, grid,
-                                     group, self.status.tensor)
+            if layer_begin == 0 or self._fp8_seq == 0:
+                seq = self._fp8_seq
+                self._fp8_seq += 1
+                self._fp8_buf = seq % nb
+                if seq >= nb and rel:
+                    ops.native().pd_wait_value(rel, seq - nb + 1, staging_timeout_s,
+                                               self.status.tensor)
+            b = self._fp8_buf
+            ops.native().pd_push_fp8(self.layout.native(), q_ptr + b * qst, s_ptr + b * sst,
+                                     src_slots, layer_begin, nl, self._flag_ptrs[0],
+                                     tile_tokens, grid, group, self.status.tensor)
             return
         if quant != "none":
             raise ValueError("quant must be 'none' or 'fp8'")

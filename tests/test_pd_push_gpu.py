@@ -151,5 +151,58 @@ def test_fp8_push_matches_reference_and_halves_bytes(group, tile):
         err = (b.float() - a.float()).view(T, -1, group).abs()
         bound = a.float().view(T, -1, group).abs().amax(-1, keepdim=True) * (2 ** -4) + 1e-2
         assert bool((err <= bound).all())
-    wire = recv._q_buf.numel() + recv._s_buf.numel()
+    wire = recv._fp8_qb + recv._fp8_sb  # one staging buffer = one request's bytes
     assert wire < 0.56 * 1024 * L * 2 * H * D * 2  # about half the bf16 bytes
+
+
+def test_fp8_requests_rotate_through_staging_buffers():
+    """Five fp8 requests in a row through two staging buffers: each is
+    dequantised from the buffer it was written to, and every wait on a
+    released buffer completes (no timeout reported)."""
+    L, NB, BS, H, D = 2, 16, 128, 2, 128
+    dst = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=21)
+    recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=512, fp8_buffers=2)
+    T = 300
+    src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=30)
+    send = PushSender(PagedKVLayout(src), engine="push")
+    send.connect([recv.desc])
+    for i in range(5):
+        g = torch.Generator(device=DEV).manual_seed(70 + i)
+        for layer in src:
+            for plane in layer:
+                plane.copy_(torch.randn(plane.shape, generator=g, device=DEV))
+        ss = block_slots(T, BS, NB, seed=40 + i, device=DEV, dtype=torch.int32)
+        ds = random_slots(T, NB * BS, seed=50 + i, device=DEV, dtype=torch.int32)
+        tg = recv.expect(T)
+        send.push(ss, ds, quant="fp8", staging_timeout_s=2.0)
+        for l0 in range(L):  # one layer at a time; the last one releases
+            recv.wait(tg[l0:l0 + 1], layer_begin=l0, timeout_s=2.0)
+            recv.dequantize(ds, layer_begin=l0, num_layers=1)
+        torch.cuda.synchronize()
+        send.check()
+        recv.check()
+        for a, b in zip(_rows(src, ss), _rows(dst, ds)):
+            assert torch.equal(b, _fp8_ref(a, 128))
+    send.close()
+    assert recv._fp8_seq == 5 and send._fp8_seq == 5
+
+
+def test_fp8_staging_not_released_reports_timeout():
+    """The receiver never dequantises: the sender's third request finds no
+    free staging buffer and its bounded wait reports a flag timeout."""
+    L, NB, BS, H, D = 2, 16, 128, 2, 128
+    src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=61)
+    dst = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=62)
+    recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=256, fp8_buffers=2)
+    send = PushSender(PagedKVLayout(src), engine="push")
+    send.connect([recv.desc])
+    ss = block_slots(200, BS, NB, seed=63, device=DEV, dtype=torch.int32)
+    send.push(ss, ss, quant="fp8", staging_timeout_s=0.2)
+    send.push(ss, ss, quant="fp8", staging_timeout_s=0.2)
+    torch.cuda.synchronize()
+    send.check()  # two buffers: no wait yet
+    send.push(ss, ss, quant="fp8", staging_timeout_s=0.2)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError):
+        send.check()
+    send.close()
