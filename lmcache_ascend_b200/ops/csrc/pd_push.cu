@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
 // 16-byte bf16 stores), and each lane keeps kDqSegs segments of loads in
 // flight.  SPR: 128-element segments per row (upper bound; `spr` is exact).
 constexpr int kDqWarps = 8;
-constexpr int kDqSegs = 8;
+constexpr int kDqSegs = 4;
 constexpr int kDqTile = 256;
 
 template <int SPR>
