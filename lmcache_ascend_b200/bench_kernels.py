@@ -288,17 +288,17 @@ def bench_push(small: bool):
     ss = (torch.randperm(nb, generator=g)[: T // BS][t // BS] * BS + t % BS).int().cuda()
     ds = (torch.randperm(nb, generator=g)[: T // BS][t // BS] * BS + t % BS).int().cuda()
     moved = T * L * 2 * H * D * 2
-    for engine in ("auto", "push"):
+    for engine in ("bulk", "simt"):
         recv = PushReceiver(PagedKVLayout(dst))
         send = PushSender(PagedKVLayout(src), engine=engine)
         send.connect([recv.desc])
         ms = _time(lambda: send.push(ss, ds))
-        _emit("push_loopback_" + ("tma_copy" if engine == "auto" else "push_kernel"), ms,
-              moved, tokens=T, layers=L)
+        _emit(f"push_loopback_{engine}_kernel", ms, moved, traffic_bytes=2 * moved,
+              tokens=T, layers=L)
         send.check()
     # fp8 push kernel alone (into the receiver's staging; local stores here)
     recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=T)
-    send = PushSender(PagedKVLayout(src), engine="push")
+    send = PushSender(PagedKVLayout(src))
     send.connect([recv.desc])
     wire = T * L * 2 * (H * D + (H * D // 128) * 4)
     for tile in (128, 512):

@@ -86,6 +86,11 @@ class LMCacheEngineConfig:
     pd_backpressure_reserve: float = 0.05
     pd_push_layerwise: bool = True
     pd_flag_timeout_s: float = 10.0
+    # direct paged push: the decoder grants a push only into the slots it
+    # reserved for the request (False: any in-range slots of a live, current
+    # registration); the prefiller asks for the grant for at most this long
+    pd_direct_require_reservation: bool = True
+    pd_reserve_timeout_s: float = 5.0
     # --- P2P cross-instance ---------------------------------------------------
     enable_p2p: bool = False
     p2p_host: Optional[str] = None

@@ -17,6 +17,24 @@ worker role
   layer); ``save_kv_layer`` / ``wait_for_save`` store (layer by layer or at
   the end of the step).
 
+disaggregated prefill, direct paged push (``enable_pd`` with the NVLink
+channel; the reference drives the same from ``save_kv_layer`` with
+per-layer source-ready events, vllm_v1_adapter.py:668-752, and submits after
+a preflight, :803-818)
+  The router gives the prefill and the decode instance the same
+  ``kv_transfer_params = {"lmcache_direct_push": True, "pd_req_id": ID}``.
+  Decoder (``kv_consumer``): the scheduler reports the prompt (minus the
+  token vLLM computes itself) as an asynchronous external hit, vLLM
+  allocates blocks, and the worker reserves exactly those slots for ID.
+  Prefiller (``kv_producer``): at the first ``save_kv_layer`` of a step the
+  worker asks the decoder for the grant (its slots come back in it; a dead
+  decoder, a stale registration or a refusal raises before anything is
+  launched), then launches layer l's push on a side stream behind layer
+  l's KV write, so it overlaps layers l+1.. of the forward.  vLLM keeps the
+  prefiller's blocks until ``get_finished`` reports the push done; the
+  decoder's ``get_finished`` reports the request received once every
+  layer's flag arrived (bounded device wait).
+
 This module only uses attribute access on vLLM's objects, so the logic can be
 exercised with light stand-ins in tests; ``connector.py`` binds it to
 ``KVConnectorBase_V1``.
@@ -25,6 +43,7 @@ exercised with light stand-ins in tests; ``connector.py`` binds it to
 from __future__ import annotations
 
 import os
+import time
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
@@ -58,6 +77,7 @@ class RequestTracker:
     allocated_block_ids: List[int]
     num_saved_tokens: int = 0
     disagg_spec: Optional[dict] = None
+    num_pushed_tokens: int = 0  # prompt tokens handed to the direct push so far
 
     def update(self, new_token_ids: Sequence[int], new_block_ids: Optional[Sequence[int]]):
         self.token_ids.extend(new_token_ids)
@@ -74,6 +94,8 @@ class ReqMeta:
     load_spec: Optional[LoadSpec] = None
     is_last_prefill: bool = False
     disagg_spec: Optional[dict] = None
+    # direct paged push: {"mode": "send"|"recv", "pd_req_id": ID, ...}
+    direct: Optional[dict] = None
 
     @staticmethod
     def build(tracker: RequestTracker, block_size: int, chunk_size: int,
@@ -112,6 +134,32 @@ class LMCacheConnectorMetadata:
         self.requests.append(r)
 
 
+def direct_push_id(request) -> Optional[str]:
+    """The disaggregated request id shared by prefiller and decoder, when the
+    router asked for a direct paged push of this request."""
+    params = getattr(request, "kv_transfer_params", None) or {}
+    if params.get("lmcache_direct_push") and params.get("pd_req_id"):
+        return str(params["pd_req_id"])
+    return None
+
+
+def block_ids_of(blocks) -> List[int]:
+    """Block ids of vLLM's ``KVCacheBlocks`` (first group) or a plain list."""
+    if blocks is None:
+        return []
+    get = getattr(blocks, "get_block_ids", None)
+    if callable(get):
+        ids = get()
+        return list(ids[0]) if ids and isinstance(ids[0], (list, tuple)) else list(ids)
+    return list(blocks)
+
+
+def slots_of(block_ids: Sequence[int], block_size: int, begin: int, end: int) -> torch.Tensor:
+    blocks = torch.tensor(list(block_ids), dtype=torch.long)
+    t = torch.arange(begin, end)
+    return blocks[t // block_size] * block_size + t % block_size
+
+
 def config_from_extra(extra: Optional[Dict[str, Any]]) -> LMCacheEngineConfig:
     """Engine config from LMCACHE_CONFIG_FILE / LMCACHE_* env, overridden by
     ``kv_connector_extra_config`` keys prefixed with ``lmcache.``
@@ -121,6 +169,12 @@ def config_from_extra(extra: Optional[Dict[str, Any]]) -> LMCacheEngineConfig:
     if over:
         cfg.update(over)
     return cfg
+
+
+class _DoneEvent:
+    @staticmethod
+    def query() -> bool:
+        return True
 
 
 class LMCacheConnectorV1Impl:
@@ -164,12 +218,35 @@ class LMCacheConnectorV1Impl:
         self._layer_load_gens: List = []
         self._layer_store_gens: List = []
         self._layer_idx = 0
+        # direct paged push state
+        self._direct_recv: Dict[str, dict] = {}     # scheduler: decoder requests awaiting blocks
+        self._direct_senders: set = set()           # scheduler: prefiller requests that push
+        self._push_handles: Dict[str, Any] = {}     # worker: vLLM req id -> DirectPrefillPush
+        self._step_handles: List[Tuple[str, Any]] = []
+        self._sending: Dict[str, Any] = {}          # worker: pushes whose blocks vLLM holds
+        self._receiving: Dict[str, dict] = {}       # worker: reserved decoder requests
+        self._recv_stream = None
+        self.load_error_block_ids: set = set()
+        self._pushed: Dict[str, int] = {}   # worker: reserved tokens pushed per request
+        self._push_failed: set = set()
+        self._finished_pushers: set = set()  # finished in vLLM, blocks held for the push
+        self._layer_index: Dict[str, int] = {}
 
     # ============================================================ scheduler
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int) -> Tuple[int, bool]:
         tokens = list(request.prompt_token_ids or [])
         if not tokens:
             return 0, False
+        pid = direct_push_id(request)
+        if pid is not None and self.kv_role == "kv_consumer":
+            # the prefiller pushes the prompt's KV: an asynchronous external hit
+            # of every prompt token vLLM does not compute itself
+            need = len(tokens) - 1 - num_computed_tokens
+            if need <= 0:
+                return 0, False
+            self._direct_recv[request.request_id] = {"pd_req_id": pid,
+                                                     "first": num_computed_tokens, "n": need}
+            return need, True
         hit = self._lookup.lookup(tokens, lookup_id=request.request_id)
         # vLLM must compute at least the last prompt token itself, so report
         # one token less; the load still covers every cached chunk (a chunk
@@ -182,6 +259,14 @@ class LMCacheConnectorV1Impl:
         return need, False
 
     def update_state_after_alloc(self, request, blocks, num_external_tokens: int) -> None:
+        rec = self._direct_recv.get(request.request_id)
+        if rec is not None:
+            if num_external_tokens == 0:
+                self._direct_recv.pop(request.request_id, None)
+            else:
+                rec["n"] = num_external_tokens
+                rec["blocks"] = block_ids_of(blocks)
+            return
         spec = self._load_specs.get(request.request_id)
         if spec is None:
             return
@@ -190,16 +275,49 @@ class LMCacheConnectorV1Impl:
             return
         spec.can_load = True
 
+    def _direct_send_meta(self, tr: RequestTracker, done: int) -> Optional[ReqMeta]:
+        """Prefiller: the tokens computed by this step go to the decoder."""
+        done = min(done, tr.prompt_len)
+        if done <= tr.num_pushed_tokens:
+            return None
+        slots = slots_of(tr.allocated_block_ids, self.block_size, 0, done)
+        r = ReqMeta(tr.req_id, torch.tensor(tr.token_ids[:done], dtype=torch.long), slots,
+                    is_last_prefill=done >= tr.prompt_len)
+        r.direct = {"mode": "send", "pd_req_id": tr.disagg_spec["pd_req_id"],
+                    "token_begin": tr.num_pushed_tokens}
+        tr.num_pushed_tokens = done
+        return r
+
     def build_connector_meta(self, scheduler_output) -> LMCacheConnectorMetadata:
         meta = LMCacheConnectorMetadata()
         for req_id in getattr(scheduler_output, "finished_req_ids", ()) or ():
             self._trackers.pop(req_id, None)
             self._load_specs.pop(req_id, None)
+            self._direct_recv.pop(req_id, None)
+        # decoder: requests whose blocks were just allocated for the push
+        for req_id, rec in list(self._direct_recv.items()):
+            if "blocks" not in rec:
+                continue
+            self._direct_recv.pop(req_id)
+            slots = slots_of(rec["blocks"], self.block_size, rec["first"],
+                             rec["first"] + rec["n"])
+            r = ReqMeta(req_id, torch.empty(0, dtype=torch.long), slots)
+            r.direct = {"mode": "recv", "pd_req_id": rec["pd_req_id"], "first": rec["first"]}
+            meta.add_request(r)
         for new in scheduler_output.scheduled_new_reqs:
             tokens = list(new.prompt_token_ids or [])
             blocks = list(new.block_ids[0]) if new.block_ids else []
             tr = RequestTracker(new.req_id, len(tokens), tokens, blocks)
             self._trackers[new.req_id] = tr
+            pid = direct_push_id(new) if self.kv_role == "kv_producer" else None
+            if pid is not None and self.engine_supports_direct():
+                tr.disagg_spec = {"pd_req_id": pid}
+                self._direct_senders.add(new.req_id)
+                done = new.num_computed_tokens + scheduler_output.num_scheduled_tokens[new.req_id]
+                r = self._direct_send_meta(tr, done)
+                if r is not None:
+                    meta.add_request(r)
+                continue
             spec = self._load_specs.pop(new.req_id, None)
             done = new.num_computed_tokens + scheduler_output.num_scheduled_tokens[new.req_id]
             if spec is not None and spec.can_load:
@@ -218,6 +336,11 @@ class LMCacheConnectorV1Impl:
             tr.update(cached.new_token_ids[i] if cached.new_token_ids else [],
                       list(new_blocks[0]) if new_blocks else None)
             done = cached.num_computed_tokens[i] + scheduler_output.num_scheduled_tokens[req_id]
+            if tr.disagg_spec is not None:  # chunked prefill of a direct push
+                r = self._direct_send_meta(tr, done)
+                if r is not None:
+                    meta.add_request(r)
+                continue
             if tr.num_saved_tokens >= tr.prompt_len:
                 continue  # decode phase: nothing to store
             r = ReqMeta.build(tr, self.block_size, self.chunk_size, None, done,
@@ -226,10 +349,18 @@ class LMCacheConnectorV1Impl:
                 meta.add_request(r)
         return meta
 
+    def engine_supports_direct(self) -> bool:
+        return bool(self.config.enable_pd and self.config.pd_role == "sender")
+
     def request_finished(self, request, block_ids) -> Tuple[bool, Optional[dict]]:
         self._trackers.pop(request.request_id, None)
+        self._direct_recv.pop(request.request_id, None)
         if self._lookup is not None:
             self._lookup.unpin(request.request_id)
+        if request.request_id in self._direct_senders:
+            # keep the blocks until the worker reports the push done
+            self._direct_senders.discard(request.request_id)
+            return True, None
         return False, None
 
     # =============================================================== worker
@@ -255,6 +386,7 @@ class LMCacheConnectorV1Impl:
             return 0
 
         self._layer_names = sorted(kv_caches, key=layer_index)
+        self._layer_index = {n: i for i, n in enumerate(self._layer_names)}
         caches = [kv_caches[n] for n in self._layer_names]
         from ...v1.kv_layer_groups import KVLayerGroupsManager
 
@@ -291,6 +423,15 @@ class LMCacheConnectorV1Impl:
         self._layer_load_gens = []
         self._layer_idx = 0
         for r in self._meta.requests:
+            if r.direct is not None and r.direct["mode"] == "recv":
+                # decoder: these freshly allocated blocks take the prefiller's push
+                eng.reserve_direct_prefill(r.direct["pd_req_id"], r.slot_mapping,
+                                           first_token=r.direct["first"])
+                self._receiving[r.req_id] = {
+                    "pd_req_id": r.direct["pd_req_id"], "event": None,
+                    "slots": r.slot_mapping, "deadline": time.monotonic()
+                    + self.config.pd_reserve_timeout_s + self.config.pd_flag_timeout_s}
+                continue
             spec = r.load_spec
             if spec is None or not spec.can_load:
                 continue
@@ -313,8 +454,39 @@ class LMCacheConnectorV1Impl:
         for g in self._layer_load_gens:
             next(g, None)
 
+    def _begin_direct_pushes(self, eng) -> None:
+        """Prefiller, first layer of a step: one grant per pushing request
+        (nothing is launched for a request whose grant failed)."""
+        self._step_handles = []
+        for r in self._meta.requests:
+            if r.direct is None or r.direct["mode"] != "send":
+                continue
+            try:
+                h = eng.begin_direct_prefill(r.direct["pd_req_id"], slot_mapping=r.slot_mapping,
+                                             token_begin=self._pushed_of(r))
+            except Exception as e:  # refused / dead decoder: no launch, request not pushed
+                logger.warning("direct push of %s not granted: %s", r.req_id, e)
+                self._push_failed.add(r.req_id)
+                continue
+            self._pushed[r.req_id] = self._pushed_of(r) + h.num_tokens
+            self._step_handles.append((r.req_id, h))
+
+    def _pushed_of(self, r: ReqMeta) -> int:
+        return self._pushed.get(r.req_id, 0)
+
     def save_kv_layer(self, layer_name: str, kv_layer=None, attn_metadata=None, **kw) -> None:
-        if self._meta is None or not self.config.use_layerwise or self.kv_role == "kv_consumer":
+        if self._meta is None or self.kv_role == "kv_consumer":
+            return
+        if any(r.direct is not None for r in self._meta.requests):
+            eng = self._ensure_engine()
+            idx = self._layer_index.get(layer_name, 0)
+            if idx == 0:
+                self._begin_direct_pushes(eng)
+            # this layer's KV write is enqueued on the current stream: the push
+            # of layer idx waits for it on the handle's side stream
+            for _, h in self._step_handles:
+                h.push_layer(idx)
+        if not self.config.use_layerwise:
             return
         eng = self._ensure_engine()
         if layer_name == self._layer_names[0]:
@@ -333,6 +505,10 @@ class LMCacheConnectorV1Impl:
     def wait_for_save(self) -> None:
         if self._meta is None or self.kv_role == "kv_consumer":
             return
+        for req_id, h in self._step_handles:
+            h.finish()  # the blocks stay with vLLM until get_finished reports it
+            self._sending.setdefault(req_id, []).append(h)
+        self._step_handles = []
         eng = self._ensure_engine()
         if self.config.use_layerwise:
             for g in self._layer_store_gens:
@@ -347,11 +523,86 @@ class LMCacheConnectorV1Impl:
             eng.store(r.token_ids, self._mask(n, r.save_spec.skip_leading_tokens),
                       slot_mapping=r.slot_mapping, req_id=r.req_id)
 
+    def _poll_receiving(self) -> set:
+        """Decoder: requests whose pushed KV has fully arrived.  Once every
+        reserved token is granted, a bounded flag wait is enqueued on a side
+        stream; its event completing means every layer landed.  A request
+        never granted before its deadline is cancelled, and its blocks are
+        reported as load errors."""
+        done = set()
+        eng = self.engine
+        for req_id, st in list(self._receiving.items()):
+            pid = st["pd_req_id"]
+            if st["event"] is None:
+                if eng.direct_prefill_granted(pid):
+                    if not st["slots"].is_cuda and not torch.cuda.is_available():
+                        eng.wait_direct_prefill(pid)  # host-resident caches: no device wait
+                        st["event"] = _DoneEvent()
+                    else:
+                        if self._recv_stream is None:
+                            self._recv_stream = torch.cuda.Stream()
+                        with torch.cuda.stream(self._recv_stream):
+                            eng.wait_direct_prefill(pid)
+                            ev = torch.cuda.Event()
+                            ev.record()
+                        st["event"] = ev
+                elif time.monotonic() > st["deadline"]:
+                    logger.error("direct push of %s (%s) never granted; failing its load",
+                                 req_id, pid)
+                    eng.cancel_direct_prefill(pid)
+                    self.load_error_block_ids.update(
+                        (st["slots"] // self.block_size).unique().tolist())
+                    self._receiving.pop(req_id)
+                    done.add(req_id)
+                    continue
+            if st["event"] is not None and st["event"].query():
+                pd = eng.storage_manager.backends.get("PDBackend")
+                try:
+                    pd.push_receiver.check()
+                except RuntimeError as e:
+                    logger.error("direct push of %s failed on the device: %s", req_id, e)
+                    self.load_error_block_ids.update(
+                        (st["slots"] // self.block_size).unique().tolist())
+                self._receiving.pop(req_id)
+                done.add(req_id)
+        return done
+
+    def _poll_sending(self) -> set:
+        """Prefiller: finished requests whose pushes have all run (vLLM may
+        free their blocks now)."""
+        done = set()
+        for req_id in list(self._finished_pushers):
+            hs = self._sending.get(req_id, [])
+            if all(h.done() for h in hs):
+                self._sending.pop(req_id, None)
+                self._pushed.pop(req_id, None)
+                self._push_failed.discard(req_id)
+                self._finished_pushers.discard(req_id)
+                done.add(req_id)
+        return done
+
     def get_finished(self, finished_req_ids) -> Tuple[Optional[set], Optional[set]]:
+        sending = set()
         if self.engine is not None and self.config.store_async:
-            done = set(self.engine.get_finished_stores())
-            return (done or None), None
-        return None, None
+            sending |= set(self.engine.get_finished_stores())
+        for req_id in finished_req_ids or ():
+            if req_id in self._sending or req_id in self._push_failed or req_id in self._pushed:
+                self._finished_pushers.add(req_id)
+        sending |= self._poll_sending()
+        recving = self._poll_receiving() if self._receiving else set()
+        return (sending or None), (recving or None)
+
+    def join_pushes_on_current_stream(self) -> None:
+        """Make the current stream wait for every direct push this worker has
+        finished enqueuing (for timing a step end to end)."""
+        for hs in self._sending.values():
+            for h in hs:
+                if h._done_event is not None:
+                    torch.cuda.current_stream().wait_event(h._done_event)
+
+    def get_block_ids_with_load_errors(self) -> set:
+        out, self.load_error_block_ids = self.load_error_block_ids, set()
+        return out
 
     def shutdown(self) -> None:
         if self._lookup_server is not None:

@@ -84,6 +84,9 @@ class LMCacheB200ConnectorV1(KVConnectorBase_V1):
     def get_finished(self, finished_req_ids: set[str]):
         return self._impl.get_finished(finished_req_ids)
 
+    def get_block_ids_with_load_errors(self) -> set[int]:
+        return self._impl.get_block_ids_with_load_errors()
+
     # ------------------------------------------------------- scheduler
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int):
         return self._impl.get_num_new_matched_tokens(request, num_computed_tokens)

@@ -307,13 +307,6 @@ int num_sms(int device) {
   return cached[device];
 }
 
-// Positive integer from the environment, else `dflt` (0 or unset = default).
-static int env_int(const char *name, int dflt) {
-  const char *v = std::getenv(name);
-  const int x = v ? std::atoi(v) : 0;
-  return x > 0 ? x : dflt;
-}
-
 PagedLayout::PagedLayout(at::Tensor ptrs, std::vector<int64_t> block_stride,
                          std::vector<int64_t> slot_stride,
                          std::vector<int64_t> row_bytes, int64_t block_size,
@@ -388,9 +381,11 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
   bool use_tma = (mode == 1) || (mode == 0 && chunk_on_device && aligned);
   if (mode == 1) TORCH_CHECK(aligned, "TMA mode needs 16-byte aligned rows");
   if (use_tma) {
-    const int stage_bytes = env_int("LMC_TMA_STAGE_BYTES", 8192);
-    const int stages = std::max(2, env_int("LMC_TMA_STAGES", 2));
-    const int warps = std::min(8, std::max(1, env_int("LMC_TMA_WARPS", 2)));
+    // 2 warps x 2 stages x 8 KiB per CTA: several CTAs per SM, each warp an
+    // independent load/store pipeline (measured best on B200 for 0.5-2 KiB rows)
+    constexpr int stage_bytes = 8192;
+    constexpr int stages = 2;
+    constexpr int warps = 2;
     int max_rb = 0;
     for (int p = 0; p < j.paged.num_planes; ++p)
       max_rb = std::max(max_rb, static_cast<int>(j.paged.plane[p].row_bytes));
@@ -414,7 +409,7 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
     }
     units *= j.num_layers;
     const int per_sm = std::max(1, static_cast<int>((228 * 1024) / (smem + 1024)));
-    const int grid_cap = env_int("LMC_TMA_GRID", num_sms(device) * per_sm);
+    const int grid_cap = num_sms(device) * per_sm;
     const long long ctas = (units + warps - 1) / warps;
     const int grid = static_cast<int>(std::max(1LL, std::min<long long>(ctas, grid_cap)));
     const unsigned long long budget_ns = 2000000000ull;  // 2 s
@@ -430,8 +425,7 @@ void launch_copy(const CopyJob &j, bool chunk_on_device, bool aligned,
     }
     const long long rows = static_cast<long long>(j.num_layers) * nsel * j.num_tokens;
     const int threads = 256;
-    const long long cap = static_cast<long long>(num_sms(device)) *
-                          env_int("LMC_SIMT_BLOCKS_PER_SM", 8);
+    const long long cap = static_cast<long long>(num_sms(device)) * 8;
     if (small) {  // thread per row
       long long blocks = (rows + threads - 1) / threads;
       blocks = std::max(1LL, std::min(blocks, cap));

@@ -15,9 +15,10 @@
 //  * the staging array holds LMC_NOALLOC_STAGING_BYTES (16 MiB) per device;
 //    every GPU that loads the library reserves it until the process exits.
 //    A transfer whose chunk is larger is rejected with an error, not split;
-//  * the first call on each device looks up the array's device address (a
-//    one-time set-up with that device current); make that first call before
-//    any stream capture;
+//  * every call looks up the array's device address on its device (a symbol
+//    lookup, no allocation), so the entry point stays valid across a device
+//    reset; the first call on a device also loads the library's module there,
+//    so make that first call before any stream capture;
 //  * all calls share the one array: calls that overlap on the GPU (two
 //    streams, two threads) race on it.  Serialise them;
 //  * nothing is allocated: no cudaMalloc, cudaFree or allocating library

@@ -7,7 +7,6 @@
 #include <cstdio>
 #include <cstring>
 #include <exception>
-#include <mutex>
 
 #include "kv_copy.cuh"
 #include "mem_kernels.h"
@@ -22,19 +21,16 @@ namespace {
 static __device__ __align__(256) unsigned char lmc_noalloc_staging[LMC_NOALLOC_STAGING_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-void *g_staging_addr[kMaxDevices] = {nullptr};
 
-// Once per device, with that device current: look up the array's address.
-cudaError_t staging_address(int device, void **out) {
-  std::lock_guard<std::mutex> lk(g_setup_mu);
-  if (g_staging_addr[device] == nullptr) {
-    void *p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, lmc_noalloc_staging);
-    if (e != cudaSuccess) return e;
-    g_staging_addr[device] = p;
-  }
-  *out = g_staging_addr[device];
+// With the target device current: the array's device address on that device.
+// Looked up on every call (a symbol lookup, no allocation), so a device reset
+// or a re-created primary context never leaves a stale address behind.  The
+// first lookup on a device loads the library's module there.
+cudaError_t staging_address(void **out) {
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, lmc_noalloc_staging);
+  if (e != cudaSuccess) return e;
+  *out = p;
   return cudaSuccess;
 }
 
@@ -97,7 +93,7 @@ extern "C" int lmc_staged_kv_transfer_noalloc(
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
   };
   void *stage = nullptr;
-  cudaError_t e = staging_address(device, &stage);
+  cudaError_t e = staging_address(&stage);
   if (e != cudaSuccess) {
     restore();
     return fail(err, err_len, 4, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
@@ -155,7 +151,9 @@ extern "C" int lmc_staged_kv_transfer_noalloc(
       e = cudaMemcpyAsync(stage, host_chunk, chunk_bytes, cudaMemcpyHostToDevice, stream);
       if (e == cudaSuccess) lmc::launch_copy(j, true, false, 2, stream, device);
     }
-    if (e == cudaSuccess) e = cudaGetLastError();
+    // launch_copy checks its own launch (and throws); only the return codes of
+    // this call's memset/memcpy are read here, so errors left by unrelated
+    // work in the process are neither reported nor cleared
     if (e != cudaSuccess)
       code = fail(err, err_len, 5, "CUDA error: %s", cudaGetErrorString(e));
   } catch (const std::exception &ex) {

@@ -171,6 +171,231 @@ __global__ void __launch_bounds__(kPushWarps * 32)
 }
 
 // ---------------------------------------------------------------------------
+// Bulk (TMA) push: the default engine for 16-byte aligned, contiguous rows.
+//
+// Each warp of a CTA is an independent pipeline over the units it owns
+// (unit = (layer, plane, tile of `tile_tokens` tokens), the same units and
+// flag counts as pd_push_kernel).  A unit is cut into pieces of at most 64
+// tokens that fit one shared-memory stage; for each piece the warp's lanes
+// plan runs of tokens contiguous on both sides (plan_runs), load them from
+// this GPU's paged cache with `cp.async.bulk.shared::cta.global` (mbarrier
+// completion; never multicast), and write them to the destination's paged
+// blocks -- local or peer memory -- with `cp.async.bulk.global.shared::cta`,
+// one bulk group per piece.
+//
+// Two waits, decoupled:
+//  * stage reuse: before loading piece k + S - 1 into the stage piece k - 1
+//    used, `cp.async.bulk.wait_group.read 1` (piece k - 1's stores have read
+//    their shared memory; their writes may still be in flight);
+//  * flags: a unit is published once its writes have completed.  A finished
+//    unit waits in a small queue; when its last piece is kLag pieces old,
+//    `cp.async.bulk.wait_group kLag` (writes of every piece <= k - kLag done,
+//    which by then costs nothing) is followed by a proxy fence, a system
+//    fence and red.release.sys.add on the decoder's layer flag.
+// ---------------------------------------------------------------------------
+constexpr int kBulkWarps = 2;
+constexpr int kBulkStages = 2;
+constexpr int kBulkStageBytes = 8192;
+constexpr int kBulkLag = 4;       // pieces between a unit's end and its release
+constexpr int kBulkPending = 4;   // units that may wait for their release
+constexpr int kTmaRingOffset = 128;  // mbarriers (warps * stages * 8 bytes) come first
+static_assert(kBulkWarps * kBulkStages * 8 <= kTmaRingOffset, "mbarrier area too small");
+
+__device__ __forceinline__ unsigned warp_sum_u32(unsigned v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+struct BulkPushJob {
+  CopyJob c;                       // src paged + replica-0 dst paged + slots
+  const int64_t *dst_ptrs;         // [replicas][dst_layers * planes] destination bases
+  int32_t dst_layers;              // layers per replica in dst_ptrs
+  int32_t replicas;
+  int32_t tile_tokens;             // flag unit
+  int32_t stage_bytes;
+  unsigned *flags[kMaxReplicas];   // per replica: layer flag array (or null)
+  unsigned long long budget_ns;    // bound on each mbarrier wait
+};
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_complete() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Position of a warp in its own sequence of pieces.
+struct PieceCursor {
+  int i;      // i-th unit of this warp: unit index = gw + i * nw
+  int piece;  // piece within the unit
+};
+
+__global__ void __launch_bounds__(kBulkWarps * 32)
+    pd_push_bulk_kernel(BulkPushJob j) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int S = kBulkStages;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * S;
+  unsigned char *ring =
+      smem + kTmaRingOffset + static_cast<size_t>(warp) * S * j.stage_bytes;
+  const CopyJob &c = j.c;
+  const int np = c.paged.num_planes;
+  const int tiles = (c.num_tokens + j.tile_tokens - 1) / j.tile_tokens;
+  const int units_per_layer = np * tiles;
+  const int total = units_per_layer * c.num_layers;
+  const int gw = blockIdx.x * kBulkWarps + warp;
+  const int nw = gridDim.x * kBulkWarps;
+  if (gw >= total) return;
+  // tokens per piece of plane p: as many rows as fit one stage, at most 64
+  auto piece_tokens = [&](int p) {
+    const int t = j.stage_bytes / plane_of(c.paged, p).row_bytes;
+    return t > 64 ? 64 : (t < 1 ? 1 : t);
+  };
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  auto valid = [&](const PieceCursor &q) { return gw + q.i * nw < total; };
+  // piece -> (layer index in launch, plane, tokens); `last`: ends its unit
+  auto piece_unit = [&](const PieceCursor &q, bool &last) {
+    const int u = gw + q.i * nw;
+    const int li = u / units_per_layer;
+    const int rem = u - li * units_per_layer;
+    const int p = rem / tiles;
+    const int t0 = (rem - p * tiles) * j.tile_tokens;
+    const int n = min(c.num_tokens - t0, j.tile_tokens);
+    const int per = piece_tokens(p);
+    Unit r;
+    r.layer = li;
+    r.plane = p;
+    r.t0 = t0 + q.piece * per;
+    r.n = min(per, t0 + n - r.t0);
+    last = r.t0 + r.n >= t0 + n;
+    return r;
+  };
+  auto advance = [&](PieceCursor &q, bool last) {
+    if (last) {
+      ++q.i;
+      q.piece = 0;
+    } else {
+      ++q.piece;
+    }
+  };
+
+  auto issue_loads = [&](const PieceCursor &q, int k) {
+    bool last;
+    const Unit u = piece_unit(q, last);
+    const int s = k % S;
+    const LaneRuns r = plan_runs(c, u, lane, c.num_tokens);
+    const unsigned rb = plane_of(c.paged, u.plane).row_bytes;
+    const unsigned bytes = warp_sum_u32((r.len[0] + r.len[1]) * rb);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[s], bytes);
+    __syncwarp();
+    unsigned char *buf = ring + static_cast<size_t>(s) * j.stage_bytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (r.len[h]) bulk_g2s(buf + (h * 32 + lane) * rb, r.src[h], r.len[h] * rb, &bars[s]);
+  };
+
+  // Finished units waiting for their release, oldest first: (absolute layer,
+  // index of the unit's last piece); -1 = empty.  Constant indices only, so
+  // the queue lives in registers.
+  int ql[kBulkPending], qk[kBulkPending];
+#pragma unroll
+  for (int i = 0; i < kBulkPending; ++i) ql[i] = -1, qk[i] = 0;
+  auto publish_front = [&]() {
+    if (lane == 0) {
+      fence_acq_rel_sys();
+      for (int r = 0; r < j.replicas; ++r)
+        if (j.flags[r]) red_release_sys_add(j.flags[r] + ql[0], 1u);
+    }
+#pragma unroll
+    for (int i = 0; i + 1 < kBulkPending; ++i) ql[i] = ql[i + 1], qk[i] = qk[i + 1];
+    ql[kBulkPending - 1] = -1;
+  };
+  // Publish every queued unit whose writes are known complete (last piece
+  // <= kdone); the caller waited for those bulk groups.
+  auto release_upto = [&](int kdone) {
+    if (ql[0] < 0 || qk[0] > kdone) return;
+    // each lane's completed bulk writes (async proxy) before the generic
+    // release lane 0 issues
+    fence_proxy_async_global();
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < kBulkPending; ++i)
+      if (ql[0] >= 0 && qk[0] <= kdone) publish_front();
+  };
+  auto enqueue = [&](int layer, int k) {
+    if (ql[kBulkPending - 1] >= 0) {  // full: drain every outstanding write
+      bulk_wait_complete<0>();
+      release_upto(0x7fffffff);
+    }
+    bool placed = false;
+#pragma unroll
+    for (int i = 0; i < kBulkPending; ++i)
+      if (!placed && ql[i] < 0) ql[i] = layer, qk[i] = k, placed = true;
+  };
+
+  PieceCursor lc{0, 0}, sc{0, 0};
+  int kl = 0;
+  for (; kl < S - 1 && valid(lc); ++kl) {
+    bool last;
+    piece_unit(lc, last);
+    issue_loads(lc, kl);
+    advance(lc, last);
+  }
+  for (int k = 0; valid(sc); ++k) {
+    const int s = k % S;
+    const unsigned parity = (k / S) & 1;
+    if (!mbar_wait_bounded(&bars[s], parity, j.budget_ns)) {
+      if (lane == 0) report_status(c.status, kStatusMbarTimeout, gw, k, 0);
+      break;
+    }
+    bool last;
+    const Unit u = piece_unit(sc, last);
+    const LaneRuns r = plan_runs(c, u, lane, c.num_tokens);
+    const unsigned rb = plane_of(c.paged, u.plane).row_bytes;
+    const unsigned char *buf = ring + static_cast<size_t>(s) * j.stage_bytes;
+    const int layer = c.layer_begin + u.layer;
+    const int64_t slot0 = static_cast<int64_t>(layer) * np + u.plane;
+    const char *base0 = reinterpret_cast<const char *>(j.dst_ptrs[slot0]);
+    for (int rep = 0; rep < j.replicas; ++rep) {
+      const char *base = reinterpret_cast<const char *>(
+          j.dst_ptrs[static_cast<int64_t>(rep) * j.dst_layers * np + slot0]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        if (r.len[h])
+          bulk_s2g(const_cast<char *>(base) + (r.dst[h] - base0),
+                   buf + (h * 32 + lane) * rb, r.len[h] * rb);
+    }
+    bulk_commit();
+    advance(sc, last);
+    if (last) enqueue(layer, k);
+    if (ql[0] >= 0 && qk[0] <= k - kBulkLag) {
+      bulk_wait_complete<kBulkLag>();  // pieces <= k - kBulkLag written
+      release_upto(k - kBulkLag);
+    }
+    if (valid(lc)) {
+      bulk_wait_read<1>();  // piece k - 1 has read its stage
+      __syncwarp();
+      bool ll;
+      piece_unit(lc, ll);
+      issue_loads(lc, kl);
+      advance(lc, ll);
+      ++kl;
+    }
+  }
+  bulk_wait_complete<0>();
+  release_upto(0x7fffffff);
+}
+
+// ---------------------------------------------------------------------------
 // Block-scaled fp8 push.  The prefiller reads bf16 paged rows, quantises
 // every group of G consecutive elements (G = 128: one head of head_dim 128)
 // to e4m3 with scale = amax / 448, and stores the fp8 bytes plus the fp32
@@ -284,7 +509,12 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
 #pragma unroll
         for (int o = 4; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (!ok[k]) continue;
-        const float inv = amax > 0.f ? __fdiv_rn(448.f, amax) : 0.f;
+        // A group whose largest magnitude is below 448 / FLT_MAX (bf16
+        // subnormals) would get an infinite inverse scale and turn its zeros
+        // into NaN (0 * inf): such a group is sent as zeros with scale 0.
+        float inv = amax > 0.f ? __fdiv_rn(448.f, amax) : 0.f;
+        const bool tiny = !(inv <= 3.402823466e38f);
+        if (tiny) inv = 0.f;
         const int64_t row = rowq0 + t0 + ti_[k];
         uint8_t *qrow = j.q + row * row_elems + static_cast<int64_t>(gi_[k]) * j.group;
 #pragma unroll
@@ -309,7 +539,7 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
           *reinterpret_cast<uint4 *>(qrow + sgi * 128 + ql * 16) =
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
-        if (ql == 0) j.scales[row * gpr + gi_[k]] = __fdiv_rn(amax, 448.f);
+        if (ql == 0) j.scales[row * gpr + gi_[k]] = tiny ? 0.f : __fdiv_rn(amax, 448.f);
       }
     }
     __syncthreads();
@@ -444,13 +674,6 @@ __global__ void pd_flag_add_kernel(unsigned *flag, unsigned inc) {
   red_release_sys_add(flag, inc);
 }
 
-// Positive integer from the environment, else `dflt` (0 or unset = default).
-static int env_int2(const char *name, int dflt) {
-  const char *v = std::getenv(name);
-  const int x = v ? std::atoi(v) : 0;
-  return x > 0 ? x : dflt;
-}
-
 int64_t push_units_per_layer(int64_t num_tokens, int64_t num_planes,
                              int64_t tile_tokens) {
   return num_planes * ((num_tokens + tile_tokens - 1) / tile_tokens);
@@ -460,7 +683,7 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
              const at::Tensor &src_slots, const at::Tensor &dst_slots,
              int64_t layer_begin, int64_t num_layers, int64_t replicas,
              const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
-             int64_t grid, const c10::optional<at::Tensor> &status) {
+             int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode) {
   TORCH_CHECK(src_slots.is_cuda() && dst_slots.is_cuda(),
               "slot mappings must live on the device");
   TORCH_CHECK(src_slots.scalar_type() == dst_slots.scalar_type(),
@@ -523,11 +746,57 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
   const long long units =
       push_units_per_layer(j.num_tokens, j.src.num_planes, j.tile_tokens) *
       static_cast<long long>(num_layers);
-  int g = grid > 0 ? static_cast<int>(grid)
-                   : env_int2("LMC_PUSH_GRID", num_sms(dev) * 16);
+  const auto stream = at::cuda::getCurrentCUDAStream(dev).stream();
+  TORCH_CHECK(mode >= 0 && mode <= 2, "pd_push: mode 0 (auto), 1 (bulk) or 2 (simt)");
+  int max_row = 0;
+  for (int p = 0; p < j.src.num_planes; ++p)
+    max_row = std::max(max_row, static_cast<int>(j.src.plane[p].row_bytes));
+  const bool bulk_ok = src.aligned() && dst.aligned() && max_row <= kBulkStageBytes;
+  TORCH_CHECK(mode != 1 || bulk_ok,
+              "pd_push: the bulk engine needs 16-byte aligned, contiguous rows of at most ",
+              kBulkStageBytes, " bytes on both sides");
+  if (mode != 2 && bulk_ok) {
+    BulkPushJob b;
+    std::memset(&b, 0, sizeof(b));
+    b.c.paged = j.src;
+    b.c.dst_paged = j.dst;
+    b.c.slots = j.src_slots;
+    b.c.dst_slots = j.dst_slots;
+    b.c.slot_is_i64 = j.slot_is_i64;
+    b.c.num_tokens = j.num_tokens;
+    b.c.layer_begin = j.layer_begin;
+    b.c.chunk_layer_begin = j.layer_begin;
+    b.c.num_layers = j.num_layers;
+    b.c.to_chunk = 1;
+    b.c.status = j.status;
+    b.dst_ptrs = j.dst.ptrs;
+    b.dst_layers = dst_layers;
+    b.replicas = j.replicas;
+    b.tile_tokens = j.tile_tokens;
+    b.stage_bytes = kBulkStageBytes;
+    for (int r = 0; r < kMaxReplicas; ++r) b.flags[r] = j.flags[r];
+    b.budget_ns = 2000000000ull;  // 2 s per mbarrier wait
+    const size_t smem = kTmaRingOffset +
+                        static_cast<size_t>(kBulkWarps) * kBulkStages * kBulkStageBytes;
+    static bool attr_set[64] = {false};
+    if (!attr_set[dev & 63]) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(pd_push_bulk_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem)));
+      attr_set[dev & 63] = true;
+    }
+    // as many CTAs as fit an SM's shared memory, on every SM
+    const int per_sm = std::max(1, static_cast<int>((228 * 1024) / (smem + 1024)));
+    const long long ctas = (units + kBulkWarps - 1) / kBulkWarps;
+    int g = grid > 0 ? static_cast<int>(grid) : num_sms(dev) * per_sm;
+    g = static_cast<int>(std::max(1LL, std::min<long long>(ctas, g)));
+    pd_push_bulk_kernel<<<g, kBulkWarps * 32, smem, stream>>>(b);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  int g = grid > 0 ? static_cast<int>(grid) : num_sms(dev) * 16;
   g = static_cast<int>(std::max(1LL, std::min<long long>(units, g)));
-  pd_push_kernel<<<g, kPushWarps * 32, 0,
-                   at::cuda::getCurrentCUDAStream(dev).stream()>>>(j);
+  pd_push_kernel<<<g, kPushWarps * 32, 0, stream>>>(j);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -585,6 +854,12 @@ void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
                 "fp8 push: head-major segments must hold whole 128-element pieces");
   }
   TORCH_CHECK(q_ptr % 16 == 0 && scale_ptr % 4 == 0, "fp8 push: staging alignment");
+  // row_off() computes 32-bit byte offsets inside one layer plane
+  for (int p = 0; p < src.desc().num_planes; ++p) {
+    const int64_t nblk = (src.desc().num_slots + src.desc().block_size - 1) / src.desc().block_size;
+    TORCH_CHECK(nblk * src.desc().plane[p].block_stride < (1LL << 32) - 1,
+                "fp8 push: each layer plane must span less than 4 GiB");
+  }
   if (src_slots.numel() == 0 || num_layers == 0) return;
   const c10::cuda::CUDAGuard guard(src_slots.device());
   PushQJob j;
@@ -604,7 +879,7 @@ void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
   const int dev = src_slots.device().index();
   const long long units =
       push_units_per_layer(j.num_tokens, j.src.num_planes, j.tile_tokens) * num_layers;
-  int g = grid > 0 ? static_cast<int>(grid) : env_int2("LMC_PUSH_GRID", num_sms(dev) * 16);
+  int g = grid > 0 ? static_cast<int>(grid) : num_sms(dev) * 16;
   g = static_cast<int>(std::max(1LL, std::min<long long>(units, g)));
   auto stream = at::cuda::getCurrentCUDAStream(dev).stream();
   if (group == 128)

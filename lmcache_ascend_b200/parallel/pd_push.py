@@ -33,6 +33,7 @@ status, and the staging contents are then not to be trusted.
 
 from __future__ import annotations
 
+import uuid
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
 
@@ -64,6 +65,10 @@ class ReceiverDesc:
     fp8_q_stride: int = 0               # bytes between staging buffers (rows)
     fp8_s_stride: int = 0               # bytes between staging buffers (scales)
     fp8_release_index: int = -1         # flag word the receiver bumps per released request
+    # registration epoch: a new one per PushReceiver, so a sender holding a
+    # mapping of an earlier registration (re-allocated or restarted decoder)
+    # is refused before it writes
+    epoch: str = ""
 
     def to_dict(self) -> dict:
         return self.__dict__.copy()
@@ -100,7 +105,8 @@ class PushReceiver:
             row_bytes=layout.row_bytes, planes=planes,
             flags=export_local(self._flags_buf.data_ptr(), dev).to_dict(), device=dev,
             seg_bytes=[p.seg_elems * es if p.segmented else 0 for p in layout.planes],
-            seg_stride=[p.seg_stride * es if p.segmented else 0 for p in layout.planes])
+            seg_stride=[p.seg_stride * es if p.segmented else 0 for p in layout.planes],
+            epoch=uuid.uuid4().hex)
         self.fp8_tokens, self.fp8_group = fp8_staging_tokens, fp8_group
         if fp8_staging_tokens > 0:
             mod = ops.native()
@@ -174,16 +180,26 @@ class PushReceiver:
         self.status.check("pd push receiver")
 
 
+_ENGINES = {"auto": 0, "bulk": 1, "simt": 2}
+
+
 class PushSender:
-    """``engine``: "auto" uses the TMA paged->paged copy (plus a flag release)
-    when the single receiver is this process on the same GPU, and the NVLink
-    push kernel otherwise; "push" always uses the push kernel."""
+    """``engine`` picks the kernel of the lossless push; every engine releases
+    the same per-layer flags, and the decoder may be on this GPU (loopback)
+    or on a peer GPU (NVLink), with the same kernel either way:
+
+    * "bulk": TMA bulk copies (`cp.async.bulk`, non-multicast) through a
+      shared-memory ring, runs of contiguous rows merged into one copy;
+      needs 16-byte aligned, contiguous (token-major) rows on both sides;
+    * "simt": 16-byte vector loads and stores per lane; any row layout,
+      including head-major segmented rows;
+    * "auto" (default): "bulk" when both layouts allow it, else "simt".
+    """
 
     def __init__(self, layout: PagedKVLayout, engine: str = "auto"):
-        if engine not in ("auto", "push"):
-            raise ValueError("engine must be 'auto' or 'push'")
+        if engine not in _ENGINES:
+            raise ValueError(f"engine must be one of {sorted(_ENGINES)}")
         self.engine = engine
-        self._local = False
         self.layout = layout
         self.device = layout.device
         self.peers = PeerMappings(self.device.index or 0)
@@ -191,6 +207,7 @@ class PushSender:
         self._dst = None
         self._flag_ptrs: List[int] = []
         self.replicas = 0
+        self._last_push: Optional[torch.cuda.Event] = None  # unmap only after it
 
     def connect(self, receivers: Sequence[ReceiverDesc]) -> None:
         """Map one or more receivers (same layout, fan-out) for pushing."""
@@ -223,11 +240,6 @@ class PushSender:
                          self.peers.resolve(IpcDesc.from_dict(r0.fp8_scales)),
                          r0.fp8_tokens, r0.fp8_group, max(1, r0.fp8_buffers),
                          r0.fp8_q_stride, r0.fp8_s_stride, rel)
-        import os
-
-        self._local = (self.engine == "auto" and len(receivers) == 1
-                       and IpcDesc.from_dict(r0.flags).pid == os.getpid()
-                       and r0.device == (self.device.index or 0))
 
     def push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, layer_begin: int = 0,
              num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0,
@@ -258,23 +270,28 @@ class PushSender:
             ops.native().pd_push_fp8(self.layout.native(), q_ptr + b * qst, s_ptr + b * sst,
                                      src_slots, layer_begin, nl, self._flag_ptrs[0],
                                      tile_tokens, grid, group, self.status.tensor)
+            self._mark_pushed()
             return
         if quant != "none":
             raise ValueError("quant must be 'none' or 'fp8'")
-        if self._local:
-            units = ops.native().push_units_per_layer(src_slots.numel(), self.layout.num_planes,
-                                                      tile_tokens)
-            ops.native().paged_copy(self.layout.native(), self._dst, src_slots, dst_slots,
-                                    layer_begin, layer_begin, nl, 0, self.status.tensor,
-                                    self._flag_ptrs[0], units)
-            return
         ops.native().pd_push(self.layout.native(), self._dst, src_slots, dst_slots,
                              layer_begin, nl, self.replicas, self._flag_ptrs, tile_tokens,
-                             grid, self.status.tensor)
+                             grid, self.status.tensor, _ENGINES[self.engine])
+        self._mark_pushed()
+
+    def _mark_pushed(self) -> None:
+        if self._last_push is None:
+            self._last_push = torch.cuda.Event()
+        self._last_push.record()
 
     def check(self) -> None:
         self.status.check("pd push sender")
 
     def close(self) -> None:
+        """Unmap the receivers, after the pushes enqueued so far have run
+        (the event is recorded on whichever stream launched the last push)."""
+        if self._last_push is not None:
+            self._last_push.synchronize()
         self.peers.close()
         self._dst = None
+        self.replicas = 0

@@ -271,6 +271,16 @@ class LMCacheEngine:
             raise RuntimeError("direct prefill push needs enable_pd")
         return pd
 
+    @staticmethod
+    def _host_and_device(slots: torch.Tensor, dev, dtype=None):
+        """(host copy, device copy) of a slot mapping; host tensors travel to
+        the device without blocking when pinned."""
+        host = slots if slots.device.type == "cpu" else slots.cpu()
+        d = slots.to(dev, non_blocking=True) if dev is not None else slots
+        if dtype is not None and d.dtype != dtype:
+            d = d.to(dtype)
+        return host, d
+
     @nvtx_range("lmc.store_direct_prefill")
     def store_direct_prefill(self, tokens: Optional[torch.Tensor] = None, *,
                              slot_mapping: torch.Tensor, dst_slot_mapping: torch.Tensor,
@@ -278,28 +288,89 @@ class LMCacheEngine:
                              num_layers: Optional[int] = None) -> int:
         """Prefiller: push this request's KV rows from the local paged cache
         straight into the decoder's paged blocks (``dst_slot_mapping``, the
-        decoder's block allocation) with the fused NVLink kernel.  Layerwise
-        callers pass ``layer_begin``/``num_layers`` after each layer's KV is
-        written.  Returns the number of tokens pushed (reference
-        cache_engine.py:2634 ``store_direct_prefill``)."""
+        decoder's block allocation) with the fused kernel, on the current
+        stream.  The decoder must grant the push first (its registration is
+        current and the slots are the ones it reserved for ``req_id``); a
+        refusal or a dead decoder raises before anything is launched.
+        Returns the number of tokens pushed (reference cache_engine.py:2634
+        ``store_direct_prefill``)."""
         if not self.is_healthy() or self._passive():
             return 0
         pd = self._pd_backend()
         n = int(slot_mapping.numel())
         dev = pd.push_sender.device if pd.push_sender is not None else None
-        src = slot_mapping.to(dev, non_blocking=True) if dev is not None else slot_mapping
-        dst = dst_slot_mapping.to(dev, non_blocking=True) if dev is not None else dst_slot_mapping
-        if dst.dtype != src.dtype:
-            dst = dst.to(src.dtype)
-        pd.direct_push(src, dst, req_id, layer_begin, num_layers)
+        _, src = self._host_and_device(slot_mapping, dev)
+        host_dst, dst = self._host_and_device(dst_slot_mapping, dev, src.dtype)
+        pd.direct_push(src, dst, req_id, layer_begin, num_layers, dst_slots_host=host_dst)
         self.stats.inc("stored_tokens", n)
         return n
+
+    def begin_direct_prefill(self, req_id: str, *, slot_mapping: torch.Tensor,
+                             dst_slot_mapping: Optional[torch.Tensor] = None,
+                             num_layers: Optional[int] = None, token_begin: int = 0,
+                             tile_tokens: int = 128) -> "DirectPrefillPush":
+        """Prefiller, layer-by-layer push during the prefill forward: get the
+        decoder's grant for every layer of ``req_id`` now (raises, with
+        nothing launched, on refusal), then call ``push_layer`` on the
+        returned handle as each layer's KV is written.
+
+        ``slot_mapping``: this prefiller's slots of the tokens to push.
+        ``dst_slot_mapping``: the decoder's slots for them, when the caller
+        knows them; ``None`` takes them from the decoder's reservation of
+        ``req_id`` (from reserved token ``token_begin`` on): ``slot_mapping``
+        then covers prompt positions 0 .. len-1 and the push covers the
+        reserved positions among them (``handle.num_tokens``)."""
+        pd = self._pd_backend()
+        if pd.push_sender is None:
+            raise RuntimeError("direct push needs a registered paged cache on the prefiller")
+        dev = pd.push_sender.device
+        L = pd.push_sender.layout.num_layers
+        nl = L if num_layers is None else num_layers
+        if dst_slot_mapping is None:
+            # slot_mapping covers prompt positions [0, len); the decoder's
+            # reservation starts at its own first_token
+            granted, first = pd.reserve_direct_push(req_id, -1, None, 0, nl, tile_tokens,
+                                                    token_begin, int(slot_mapping.numel()))
+            n = len(granted)
+            start = first + token_begin
+            _, src = self._host_and_device(slot_mapping[start:start + n], dev)
+            host = torch.tensor(granted, dtype=torch.int64).pin_memory() \
+                if torch.cuda.is_available() else torch.tensor(granted, dtype=torch.int64)
+            _, dst = self._host_and_device(host, dev, src.dtype)
+        else:
+            _, src = self._host_and_device(slot_mapping, dev)
+            host_dst, dst = self._host_and_device(dst_slot_mapping, dev, src.dtype)
+            pd.reserve_direct_push(req_id, int(src.numel()), host_dst, 0, nl, tile_tokens,
+                                   token_begin)
+        self.stats.inc("stored_tokens", int(src.numel()))
+        return DirectPrefillPush(pd, req_id, src, dst, nl, tile_tokens)
 
     def wait_direct_prefill(self, req_id: str, timeout_s: Optional[float] = None,
                             sync: bool = False) -> bool:
         """Decoder: enqueue the bounded per-layer wait for a direct push on the
         current stream (``sync`` also checks the device status on the host)."""
         return self._pd_backend().wait_direct(req_id, timeout_s, sync)
+
+    def reserve_direct_prefill(self, req_id: str, dst_slot_mapping,
+                               first_token: int = 0) -> None:
+        """Decoder: these paged-cache slots (for prompt positions
+        ``first_token`` ..) are allocated for ``req_id``; only a push into
+        exactly them is granted."""
+        self._pd_backend().reserve_direct(req_id, dst_slot_mapping, first_token)
+
+    def direct_prefill_granted(self, req_id: str) -> bool:
+        """Decoder: every reserved token of ``req_id`` was granted to the
+        prefiller (its flags can now be waited for)."""
+        return self._pd_backend().direct_granted(req_id)
+
+    def cancel_direct_prefill(self, req_id: str) -> None:
+        self._pd_backend().cancel_direct(req_id)
+
+    def wait_direct_prefill_layer(self, req_id: str, layer: int,
+                                  timeout_s: Optional[float] = None) -> bool:
+        """Decoder: enqueue the bounded wait for layers up to ``layer`` of a
+        granted direct push on the current stream (no host wait)."""
+        return self._pd_backend().wait_direct_layer(req_id, layer, timeout_s)
 
     def _emit_events(self, tokens, starts, ends, keys) -> None:
         toks = tokens.tolist() if isinstance(tokens, torch.Tensor) else list(tokens)
@@ -602,3 +673,59 @@ class LMCacheEngineBuilder:
             eng = cls._engines.pop(instance_id, None)
         if eng is not None:
             eng.close()
+
+
+class DirectPrefillPush:
+    """A granted layer-by-layer direct push of one request (prefiller side).
+
+    ``push_layer(l, ready)`` makes a side stream wait for ``ready`` (the event
+    after layer ``l``'s KV write; default: the current stream's position) and
+    launches layer ``l``'s push there, so the push overlaps the next layers'
+    forward.  ``finish()`` records completion; ``done()`` polls it; the
+    source blocks must stay allocated until it is True."""
+
+    def __init__(self, pd, req_id: str, src: torch.Tensor, dst: torch.Tensor,
+                 num_layers: int, tile_tokens: int):
+        self.pd, self.req_id = pd, req_id
+        self.src, self.dst = src, dst
+        self.num_tokens = int(src.numel())
+        self.num_layers, self.tile_tokens = num_layers, tile_tokens
+        self.pushed = 0
+        self._done_event: Optional[torch.cuda.Event] = None
+        self._finished = False
+        self.stream = None
+        if src.is_cuda:
+            self.stream = torch.cuda.Stream(device=src.device)
+            # the slot tables were copied on the caller's stream
+            staged = torch.cuda.Event()
+            staged.record()
+            self.stream.wait_event(staged)
+            src.record_stream(self.stream)
+            dst.record_stream(self.stream)
+
+    def push_layer(self, layer: int, ready: Optional[torch.cuda.Event] = None) -> None:
+        if self.stream is None:  # host-resident caches (CPU tier tests)
+            self.pd.push_granted_layers(self.src, self.dst, layer, 1, self.tile_tokens)
+            self.pushed += 1
+            return
+        if ready is None:
+            ready = torch.cuda.Event()
+            ready.record()
+        self.stream.wait_event(ready)
+        with torch.cuda.stream(self.stream):
+            self.pd.push_granted_layers(self.src, self.dst, layer, 1, self.tile_tokens)
+        self.pushed += 1
+
+    def finish(self) -> Optional[torch.cuda.Event]:
+        self._finished = True
+        if self.stream is None:
+            return None
+        ev = torch.cuda.Event()
+        ev.record(self.stream)
+        self._done_event = ev
+        return ev
+
+    def done(self) -> bool:
+        if not self._finished:
+            return False
+        return self._done_event is None or self._done_event.query()

@@ -75,16 +75,37 @@ class HandshakeResponse(msgspec.Struct, tag=True):
     error: str = ""
 
 
-class DirectPushNotif(msgspec.Struct, tag=True):
-    """Sent by the prefiller after enqueuing a direct paged push, so the
-    decoder knows how many flag units each layer will receive."""
+class DirectPushReserve(msgspec.Struct, tag=True):
+    """Sent by the prefiller BEFORE it launches any kernel that stores into
+    the decoder's paged blocks.  The decoder grants it only if ``epoch`` is
+    its current registration (its cache has not been re-registered or
+    re-allocated since the sender mapped it), every destination slot is in
+    range, and -- unless the decoder runs without reservations -- the
+    destination slots are exactly the ones the decoder reserved for
+    ``req_id`` (compared by digest).  The grant also tells the decoder how
+    many flag units each layer will receive."""
 
     req_id: str
-    num_tokens: int
+    epoch: str
+    num_tokens: int        # tokens of this push (-1 with want_slots: as many as reserved)
     layer_begin: int
     num_layers: int
     tile_tokens: int
-    keys: List[str] = []
+    dst_digest: str        # digest of the sender's destination slots ("" with want_slots)
+    dst_max_slot: int
+    sender_id: str = ""
+    token_begin: int = 0   # first token of the reservation this push covers
+    want_slots: bool = False  # the sender has no slots: the grant carries the reserved ones
+    prompt_end: int = -1   # with want_slots: the sender holds KV of prompt positions < this
+
+
+class DirectPushGrant(msgspec.Struct, tag=True):
+    ok: bool
+    epoch: str = ""
+    error: str = ""
+    retry: bool = False  # refused for now (no reservation yet); asking again may succeed
+    slots: List[int] = []  # with want_slots: the granted destination slots
+    first_token: int = 0   # prompt position of the reservation's first token
 
 
 class WriteDone(msgspec.Struct, tag=True):
@@ -100,8 +121,8 @@ class Ack(msgspec.Struct, tag=True):
 
 
 PDMsg = Union[AllocRequest, AllocResponse, ProxyNotif, PullReadyNotif, PullReadyDoneAck,
-              PullDoneSignal, HandshakeRequest, HandshakeResponse, DirectPushNotif, WriteDone,
-              Ack]
+              PullDoneSignal, HandshakeRequest, HandshakeResponse, DirectPushReserve,
+              DirectPushGrant, WriteDone, Ack]
 
 _enc = msgspec.msgpack.Encoder()
 _dec = msgspec.msgpack.Decoder(PDMsg)
@@ -113,3 +134,21 @@ def encode(msg) -> bytes:
 
 def decode(data: bytes):
     return _dec.decode(data)
+
+
+def slot_digest(slots) -> "tuple[str, int]":
+    """(digest, max slot) of a destination slot list (host tensor or
+    sequence).  Both sides of a direct push compute it over the same int64
+    little-endian bytes."""
+    import hashlib
+
+    import numpy as np
+    import torch
+
+    if isinstance(slots, torch.Tensor):
+        arr = slots.detach().to("cpu", torch.int64).numpy()
+    else:
+        arr = np.asarray(list(slots), dtype=np.int64)
+    arr = np.ascontiguousarray(arr.astype("<i8", copy=False))
+    h = hashlib.blake2b(arr.tobytes(), digest_size=16).hexdigest()
+    return h, int(arr.max()) if arr.size else -1

@@ -31,7 +31,12 @@ class ReceiverMixin:
         self.data: Dict[str, MemoryObj] = {}
         self.pending: Dict[str, MemoryObj] = {}
         self.delayed: Dict[str, Tuple[str, Tuple[str, int], MemoryObj]] = {}
-        self.direct: Dict[str, Tuple[torch.Tensor, int, int]] = {}
+        # granted direct pushes: req_id -> [device targets, layer_begin,
+        # num_layers, next layer to wait for]
+        self.direct: Dict[str, list] = {}
+        # destination slots the decoder reserved per request, and how many of
+        # its tokens were granted so far
+        self.reservations: Dict[str, dict] = {}
         self._done_socks: Dict[str, zmq.Socket] = {}
         self.init_url = self._rep_server(f"tcp://{bind_host}:{ip}", self._handle_init,
                                          "lmc-pd-init")
@@ -66,15 +71,99 @@ class ReceiverMixin:
             return M.Ack()
         if isinstance(msg, M.PullReadyNotif):
             return self._handle_pull_ready(msg)
-        if isinstance(msg, M.DirectPushNotif):
-            if self.push_receiver is None:
-                return M.Ack(False, "receiver has no registered paged cache")
-            tg = self.push_receiver.expect(msg.num_tokens, msg.layer_begin, msg.num_layers,
-                                           msg.tile_tokens)
-            with self._lock:
-                self.direct[msg.req_id] = (tg, msg.layer_begin, msg.num_layers)
-            return M.Ack()
+        if isinstance(msg, M.DirectPushReserve):
+            return self._handle_direct_reserve(msg)
         return M.Ack(False, f"unexpected message {type(msg).__name__}")
+
+    # ------------------------------------------------- direct paged push
+    def reserve_direct(self, req_id: str, dst_slots, first_token: int = 0) -> None:
+        """Decoder: ``dst_slots`` (host tensor or sequence, one per token) are
+        the paged-cache slots this decoder allocated for ``req_id``.  A
+        prefiller's direct push of that request is granted only into these
+        slots, in token order, possibly over several pushes (chunked prefill);
+        the request is complete for ``wait_direct*`` once every reserved token
+        was granted.  ``first_token``: prompt position of the first reserved
+        token (tokens before it are already in this decoder's cache)."""
+        import numpy as np
+
+        arr = (dst_slots.detach().to("cpu", torch.int64).numpy()
+               if isinstance(dst_slots, torch.Tensor) else np.asarray(list(dst_slots), np.int64))
+        with self._lock:
+            self.reservations[str(req_id)] = {"slots": arr, "granted": 0, "targets": None,
+                                              "first": int(first_token)}
+            self.direct.pop(str(req_id), None)
+
+    def cancel_direct(self, req_id: str) -> None:
+        with self._lock:
+            self.reservations.pop(str(req_id), None)
+            self.direct.pop(str(req_id), None)
+
+    def _handle_direct_reserve(self, msg: "M.DirectPushReserve") -> "M.DirectPushGrant":
+        pr = self.push_receiver
+        if pr is None:
+            return M.DirectPushGrant(False, error="receiver has no registered paged cache")
+        epoch = pr.desc.epoch
+        if msg.epoch != epoch:
+            self.stats.inc("pd_direct_refused_epoch")
+            return M.DirectPushGrant(False, epoch, "stale epoch: the paged cache was "
+                                                   "registered again since the sender mapped it")
+        nl_total = pr.layout.num_layers
+        if msg.layer_begin < 0 or msg.num_layers < 1 or \
+                msg.layer_begin + msg.num_layers > nl_total:
+            return M.DirectPushGrant(False, epoch, "layer range out of the paged cache")
+        with self._lock:
+            res = self.reservations.get(msg.req_id)
+            slots_out: List[int] = []
+            if res is None:
+                if self.config.pd_direct_require_reservation or msg.want_slots:
+                    return M.DirectPushGrant(False, epoch, "no reservation for this request",
+                                             retry=True)
+                n = msg.num_tokens
+                if msg.dst_max_slot >= pr.layout.num_slots:
+                    self.stats.inc("pd_direct_refused_range")
+                    return M.DirectPushGrant(False, epoch,
+                                             "destination slot out of the paged cache")
+                tg = pr.expect(n, msg.layer_begin, msg.num_layers, msg.tile_tokens)
+                self.direct[msg.req_id] = [tg, msg.layer_begin, msg.num_layers, msg.layer_begin]
+                self.stats.inc("pd_direct_granted")
+                return M.DirectPushGrant(True, epoch)
+            arr = res["slots"]
+            tb = msg.token_begin
+            if tb != res["granted"]:
+                return M.DirectPushGrant(False, epoch, f"push starts at token {tb}, the "
+                                                       f"reservation continues at "
+                                                       f"{res['granted']}")
+            n = len(arr) - tb if msg.num_tokens < 0 else msg.num_tokens
+            n = min(n, len(arr) - tb)
+            if msg.want_slots and msg.prompt_end >= 0:
+                n = min(n, msg.prompt_end - (res["first"] + tb))
+            if n <= 0:
+                return M.DirectPushGrant(False, epoch, "nothing left of the reservation")
+            part = arr[tb:tb + n]
+            if msg.want_slots:
+                slots_out = part.tolist()
+            else:
+                digest, _ = M.slot_digest(part)
+                if n != msg.num_tokens or digest != msg.dst_digest:
+                    self.stats.inc("pd_direct_refused_slots")
+                    return M.DirectPushGrant(False, epoch, "destination slots differ from "
+                                                           "the decoder's reservation")
+            if int(part.max()) >= pr.layout.num_slots:
+                return M.DirectPushGrant(False, epoch, "reserved slot out of the paged cache")
+            res["targets"] = pr.expect(n, msg.layer_begin, msg.num_layers, msg.tile_tokens)
+            res["granted"] = tb + n
+            res["layers"] = (msg.layer_begin, msg.num_layers)
+            if res["granted"] >= len(arr):  # every reserved token is on its way
+                self.reservations.pop(msg.req_id, None)
+                lb, nl = res["layers"]
+                self.direct[msg.req_id] = [res["targets"], lb, nl, lb]
+        self.stats.inc("pd_direct_granted")
+        return M.DirectPushGrant(True, epoch, slots=slots_out, first_token=res["first"])
+
+    def direct_granted(self, req_id: str) -> bool:
+        """Every reserved token of ``req_id`` was granted to a prefiller."""
+        with self._lock:
+            return str(req_id) in self.direct
 
     def _shapes(self, shape: List[int], n: int, last_toks: int, fmt: int):
         shp = list(shape)
@@ -204,25 +293,53 @@ class ReceiverMixin:
             self.stats.inc("pd_retrieved_chunks")
         return obj  # the caller owns the backend's reference
 
-    def wait_direct(self, req_id: str, timeout_s: Optional[float] = None,
-                    sync: bool = False) -> bool:
-        """Enqueue the bounded per-layer flag wait for a direct push on the
-        current stream.  With ``sync`` also waits on the host and checks the
-        status word.  Returns False if the push was never announced."""
-        deadline = time.monotonic() + (timeout_s or self.config.pd_flag_timeout_s)
+    def _granted(self, req_id: str, timeout_s: float):
+        deadline = time.monotonic() + timeout_s
         while True:
             with self._lock:
-                ent = self.direct.pop(req_id, None)
+                ent = self.direct.get(req_id)
             if ent is not None or time.monotonic() > deadline:
-                break
+                return ent
             time.sleep(0.0005)
+
+    def wait_direct(self, req_id: str, timeout_s: Optional[float] = None,
+                    sync: bool = False) -> bool:
+        """Enqueue the bounded flag wait for every layer of a granted direct
+        push (not yet waited for) on the current stream.  With ``sync`` also
+        waits on the host and checks the status word.  Returns False if the
+        push was never granted within ``timeout_s``."""
+        to = timeout_s or self.config.pd_flag_timeout_s
+        ent = self._granted(req_id, to)
         if ent is None:
             return False
-        tg, lb, _ = ent
-        self.push_receiver.wait(tg, lb, timeout_s or self.config.pd_flag_timeout_s)
+        tg, lb, nl, nxt = ent
+        with self._lock:
+            self.direct.pop(req_id, None)
+        if nxt < lb + nl:
+            self.push_receiver.wait(tg[nxt - lb:], nxt, to)
         if sync:
             torch.cuda.current_stream().synchronize()
             self.push_receiver.check()
+        return True
+
+    def wait_direct_layer(self, req_id: str, layer: int,
+                          timeout_s: Optional[float] = None) -> bool:
+        """Enqueue the bounded flag wait of layers up to ``layer`` (inclusive)
+        of a granted direct push on the current stream, so the kernels queued
+        after it (attention of that layer) see the pushed rows.  No host
+        wait.  Returns False if the push was never granted."""
+        to = timeout_s or self.config.pd_flag_timeout_s
+        ent = self._granted(req_id, to)
+        if ent is None:
+            return False
+        tg, lb, nl, nxt = ent
+        last = min(layer, lb + nl - 1)
+        if last >= nxt:
+            self.push_receiver.wait(tg[nxt - lb:last - lb + 1], nxt, to)
+            ent[3] = last + 1
+        if ent[3] >= lb + nl:
+            with self._lock:
+                self.direct.pop(req_id, None)
         return True
 
     def _close_receiver(self) -> None:

@@ -32,6 +32,7 @@ class SenderMixin:
         self.peer_init_url = peer_init_url or f"tcp://{host}:{pi[self.tp_rank % len(pi)]}"
         self.peer_alloc_url = peer_alloc_url or f"tcp://{host}:{pa[self.tp_rank % len(pa)]}"
         self.remote_peer_id: Optional[str] = None
+        self._receiver_epoch: Optional[str] = None  # decoder registration we mapped
         self._alloc_fail_until = 0.0
         self.pull_pending: Dict[str, Tuple[List[MemoryObj], float]] = {}
         self._proxy_sock = None
@@ -65,7 +66,9 @@ class SenderMixin:
         if resp.receiver_desc is not None and self.push_sender is not None:
             from ....parallel.pd_push import ReceiverDesc
 
-            self.push_sender.connect([ReceiverDesc.from_dict(resp.receiver_desc)])
+            rd = ReceiverDesc.from_dict(resp.receiver_desc)
+            self.push_sender.connect([rd])
+            self._receiver_epoch = rd.epoch
         self.remote_peer_id = resp.peer_id
 
     def breaker_open(self) -> bool:
@@ -176,25 +179,98 @@ class SenderMixin:
                 self._release_pull(p)
 
     # ------------------------------------------------------- direct push
+    def _drop_peer_mapping(self) -> None:
+        """Forget the decoder's mapping (after its epoch changed): wait for
+        the pushes already enqueued through it, then unmap."""
+        if self.push_sender is not None:
+            self.push_sender.close()
+        self.remote_peer_id = None
+        self._receiver_epoch = None
+
+    def reserve_direct_push(self, req_id: str, num_tokens: int, dst_slots_host,
+                            layer_begin: int = 0, num_layers: Optional[int] = None,
+                            tile_tokens: int = 128, token_begin: int = 0,
+                            prompt_end: int = -1) -> Tuple[List[int], int]:
+        """Ask the decoder to grant a direct push of ``req_id`` before anything
+        is launched.  ``dst_slots_host`` (host tensor or sequence) are the
+        destination slots the sender was given; ``None`` asks the decoder for
+        the slots it reserved, from reserved token ``token_begin`` on, at most
+        ``num_tokens`` (-1: all) and not past prompt position ``prompt_end``.
+        Returns (granted destination slots, prompt position of the
+        reservation's first token).
+        Raises -- and trips the per-peer circuit breaker -- when the decoder
+        does not answer, answers with a stale registration epoch twice, or
+        refuses (no reservation in time, slots that differ from its
+        reservation, slots out of range).  No kernel that stores into the
+        decoder's memory runs unless this returned."""
+        if self.push_sender is None:
+            raise RuntimeError("direct push needs a registered paged cache on the prefiller")
+        want = dst_slots_host is None
+        digest, max_slot = ("", -1) if want else M.slot_digest(dst_slots_host)
+        deadline = time.monotonic() + self.config.pd_reserve_timeout_s
+        reconnects = 0
+        try:
+            while True:
+                self._ensure_peer_connection()
+                if self.push_sender.replicas == 0 or not getattr(self, "_receiver_epoch", None):
+                    raise RuntimeError("the decoder shared no paged-cache descriptor")
+                L = self.push_sender.layout.num_layers
+                nl = L - layer_begin if num_layers is None else num_layers
+                resp = self._req(self.peer_alloc_url, M.DirectPushReserve(
+                    str(req_id), self._receiver_epoch, int(num_tokens), int(layer_begin),
+                    int(nl), int(tile_tokens), digest, max_slot, self.peer_id,
+                    int(token_begin), want, int(prompt_end)))
+                if isinstance(resp, M.DirectPushGrant) and resp.ok:
+                    self.stats.inc("pd_direct_grants")
+                    if want:
+                        return list(resp.slots), int(resp.first_token)
+                    return (dst_slots_host.tolist() if isinstance(dst_slots_host, torch.Tensor)
+                            else list(dst_slots_host)), int(resp.first_token)
+                if isinstance(resp, M.DirectPushGrant) and resp.epoch and \
+                        resp.epoch != self._receiver_epoch and reconnects < 1:
+                    reconnects += 1  # the decoder re-registered: map it again
+                    self._drop_peer_mapping()
+                    continue
+                if isinstance(resp, M.DirectPushGrant) and resp.retry and \
+                        time.monotonic() < deadline:
+                    time.sleep(0.001)
+                    continue
+                raise RuntimeError(f"decoder refused direct push of {req_id}: "
+                                   f"{getattr(resp, 'error', resp)}")
+        except (TimeoutError, RuntimeError, zmq.ZMQError):
+            self.stats.inc("pd_direct_refusals")
+            self.remote_peer_id = None  # handshake again next time
+            self._trip_breaker()
+            raise
+
     def direct_push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, req_id: str,
                     layer_begin: int = 0, num_layers: Optional[int] = None,
-                    tile_tokens: int = 128) -> None:
-        """Push the prefiller's paged KV rows ``src_slots`` straight into the
-        decoder's paged blocks ``dst_slots`` (fused NVLink kernel), then tell
-        the decoder how many flag units to expect."""
-        self._ensure_peer_connection()
-        if self.push_sender is None or self.push_sender.replicas == 0:
-            raise RuntimeError("direct push needs registered paged caches on both sides")
+                    tile_tokens: int = 128, dst_slots_host=None) -> None:
+        """Reserve (``reserve_direct_push``), then push the prefiller's paged
+        KV rows ``src_slots`` straight into the decoder's paged blocks
+        ``dst_slots`` with the fused kernel on the current stream.
+        ``dst_slots_host`` is the host copy of ``dst_slots`` the grant is
+        checked against (taken from ``dst_slots`` when omitted)."""
+        if self.breaker_open():
+            self.stats.inc("pd_breaker_skips")
+            raise RuntimeError("PD circuit breaker open: decoder recently refused or failed")
+        host = dst_slots_host if dst_slots_host is not None else dst_slots.cpu()
+        self.reserve_direct_push(req_id, int(src_slots.numel()), host, layer_begin,
+                                 num_layers, tile_tokens)
         L = self.push_sender.layout.num_layers
         nl = L - layer_begin if num_layers is None else num_layers
         self.push_sender.push(src_slots, dst_slots, layer_begin, nl, tile_tokens)
-        ack = self._req(self.peer_alloc_url,
-                        M.DirectPushNotif(str(req_id), int(src_slots.numel()), layer_begin, nl,
-                                          tile_tokens))
-        if not isinstance(ack, M.Ack) or not ack.ok:
-            raise RuntimeError(f"decoder rejected direct push: {ack}")
         self.stats.inc("pd_direct_push_bytes",
                        src_slots.numel() * nl * sum(self.push_sender.layout.row_bytes))
+
+    def push_granted_layers(self, src_slots: torch.Tensor, dst_slots: torch.Tensor,
+                            layer_begin: int, num_layers: int, tile_tokens: int = 128) -> None:
+        """Launch layers of a push that ``reserve_direct_push`` granted (for
+        the layer-by-layer push during prefill: one grant per request, then
+        one launch per layer with no round trip)."""
+        self.push_sender.push(src_slots, dst_slots, layer_begin, num_layers, tile_tokens)
+        self.stats.inc("pd_direct_push_bytes",
+                       src_slots.numel() * num_layers * sum(self.push_sender.layout.row_bytes))
 
     def _close_sender(self) -> None:
         with self._lock:

@@ -216,7 +216,7 @@ def test_head_major_layout_gather_scatter(mode):
     assert torch.equal(back, ref)
 
 
-@pytest.mark.parametrize("engine", ["auto", "push"])
+@pytest.mark.parametrize("engine", ["auto", "simt"])
 def test_head_major_push(engine):
     from lmcache_ascend_b200.parallel.pd_push import PushReceiver, PushSender
 

@@ -68,6 +68,7 @@ def test_direct_prefill_push_engine_api():
         ss = block_slots(T, BS, NB, seed=5, device="cuda", dtype=torch.int32)
         rs = block_slots(T, BS, NB, seed=6, device="cuda", dtype=torch.int32)
         for layer in range(L):  # layer by layer, as during prefill
+            recv.reserve_direct_prefill(f"req-{layer}", rs.cpu())  # the decoder's allocation
             send.store_direct_prefill(slot_mapping=ss, dst_slot_mapping=rs,
                                       req_id=f"req-{layer}", layer_begin=layer, num_layers=1)
             assert recv.wait_direct_prefill(f"req-{layer}", timeout_s=5.0)

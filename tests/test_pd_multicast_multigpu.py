@@ -1,6 +1,7 @@
 """NVLS fan-out: one prefiller pushes through the multicast staging buffer,
-every other member receives the rows (2+ GPUs; skipped otherwise, and where
-the system has no NVLink multicast)."""
+every other member receives the rows, and back-to-back pushes wait for the
+members' staging release (2+ GPUs; skipped otherwise, and where the system
+has no NVLink multicast)."""
 
 import os
 import socket
@@ -69,6 +70,19 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         fan.check()
         ok = ok and same()
+        # pushes 3 and 4 with new rows and no host barrier in between: the
+        # root's push waits (on its stream, bounded) until every member
+        # released the previous push through the root's release counter
+        for seed in (5, 6):
+            src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, dev, seed=seed)
+            tg = fan.expect(T)
+            if rank == 0:
+                fan.push(PagedKVLayout(src), ss, release_timeout_s=5.0)
+            fan.wait(tg, timeout_s=5.0)
+            fan.scatter(PagedKVLayout(dst), ds, T)
+            torch.cuda.synchronize()
+            fan.check()
+            ok = ok and same()
         dist.barrier()
         q.put((rank, "ok" if ok else "mismatch"))
     except Exception as e:  # report, do not hang the parent

@@ -29,7 +29,7 @@ def _rows(kv, slots):
 
 @pytest.mark.parametrize("pattern", ["blocks", "random"])
 @pytest.mark.parametrize("tile", [32, 128])
-@pytest.mark.parametrize("engine", ["auto", "push"])
+@pytest.mark.parametrize("engine", ["auto", "bulk", "simt"])
 def test_loopback_push_exact(pattern, tile, engine):
     L, NB, BS = 6, 32, 128
     src = make_separate_kv(L, NB, BS, 2, 128, torch.bfloat16, DEV, seed=1)
@@ -65,7 +65,7 @@ def test_layerwise_push_and_partial_wait():
     ss = block_slots(T, BS, NB, seed=9, device=DEV, dtype=torch.int32)
     ds = block_slots(T, BS, NB, seed=10, device=DEV, dtype=torch.int32)
     recv = PushReceiver(PagedKVLayout(dst))
-    send = PushSender(PagedKVLayout(src), engine="push")
+    send = PushSender(PagedKVLayout(src), engine="auto")
     send.connect([recv.desc])
     for layer in range(L):
         tg = recv.expect(T, layer_begin=layer, num_layers=1)
@@ -120,7 +120,10 @@ def _fp8_ref(rows: torch.Tensor, group: int) -> torch.Tensor:
     # IEEE fp32 quotients (PyTorch divides by a scalar through its reciprocal):
     # a float64 quotient rounded once to fp32 is the correctly rounded one
     inv = torch.where(amax > 0, (448.0 / amax.double()).float(), torch.zeros_like(amax))
-    scale = (amax.double() / 448.0).float()
+    # a group too small for a finite inverse scale is sent as zeros, scale 0
+    tiny = torch.isinf(inv)
+    inv = torch.where(tiny, torch.zeros_like(inv), inv)
+    scale = torch.where(tiny, torch.zeros_like(amax), (amax.double() / 448.0).float())
     q = (x * inv).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
     return (q.float() * scale).to(torch.bfloat16).view_as(rows)
 
@@ -132,11 +135,14 @@ def test_fp8_push_matches_reference_and_halves_bytes(group, tile):
     src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=11)
     dst = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=12)
     src[1][0][3] = 0  # an all-zero block: scale 0
+    # a block of bf16 subnormals (amax below 448 / FLT_MAX): zeros, not NaN
+    src[2][1][5] = torch.full_like(src[2][1][5], 1e-38)
+    src[2][1][5][::3] = 0
     T = 900
     ss = block_slots(T, BS, NB, seed=13, device=DEV, dtype=torch.int32)
     ds = random_slots(T, NB * BS, seed=14, device=DEV, dtype=torch.int32)
     recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=1024, fp8_group=group)
-    send = PushSender(PagedKVLayout(src), engine="push")
+    send = PushSender(PagedKVLayout(src), engine="auto")
     send.connect([recv.desc])
     tg = recv.expect(T, tile_tokens=tile)
     send.push(ss, ds, tile_tokens=tile, quant="fp8")
@@ -146,6 +152,7 @@ def test_fp8_push_matches_reference_and_halves_bytes(group, tile):
     send.check()
     recv.check()
     for a, b in zip(_rows(src, ss), _rows(dst, ds)):
+        assert not bool(torch.isnan(b).any())
         assert torch.equal(b, _fp8_ref(a, group))
         # bounded error: at most 2^-4 of the group's amax per element
         err = (b.float() - a.float()).view(T, -1, group).abs()
@@ -164,7 +171,7 @@ def test_fp8_requests_rotate_through_staging_buffers():
     recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=512, fp8_buffers=2)
     T = 300
     src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=30)
-    send = PushSender(PagedKVLayout(src), engine="push")
+    send = PushSender(PagedKVLayout(src), engine="auto")
     send.connect([recv.desc])
     for i in range(5):
         g = torch.Generator(device=DEV).manual_seed(70 + i)
@@ -194,7 +201,7 @@ def test_fp8_staging_not_released_reports_timeout():
     src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=61)
     dst = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, DEV, seed=62)
     recv = PushReceiver(PagedKVLayout(dst), fp8_staging_tokens=256, fp8_buffers=2)
-    send = PushSender(PagedKVLayout(src), engine="push")
+    send = PushSender(PagedKVLayout(src), engine="auto")
     send.connect([recv.desc])
     ss = block_slots(200, BS, NB, seed=63, device=DEV, dtype=torch.int32)
     send.push(ss, ss, quant="fp8", staging_timeout_s=0.2)
@@ -206,3 +213,18 @@ def test_fp8_staging_not_released_reports_timeout():
     with pytest.raises(RuntimeError):
         send.check()
     send.close()
+
+
+def test_fp8_push_rejects_planes_of_4gib():
+    """The fp8 push addresses rows with 32-bit offsets inside a layer plane:
+    a layout whose plane spans 4 GiB or more is refused before any launch
+    (the layout below only describes such a plane; nothing is allocated)."""
+    from lmcache_ascend_b200 import ops
+
+    nb, bs, rb = 1 << 16, 128, 512            # 65536 blocks x 64 KiB = 4 GiB
+    ptrs = torch.full((2,), 1 << 40, dtype=torch.int64, device=DEV)
+    lay = ops.native().PagedLayout(ptrs, [bs * rb, bs * rb], [rb, rb], [rb, rb], bs, nb * bs,
+                                   [], [])
+    slots = torch.zeros(16, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match="4 GiB"):
+        ops.native().pd_push_fp8(lay, 0, 0, slots, 0, 1, 0, 128, 0, 128, None)

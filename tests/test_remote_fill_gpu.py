@@ -20,7 +20,7 @@ def test_remote_fill_over_push_kernel():
     src = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, "cuda", seed=1)
     dst = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, "cuda", seed=2)
     recv = PushReceiver(PagedKVLayout(dst))
-    send = PushSender(PagedKVLayout(src), engine="push")
+    send = PushSender(PagedKVLayout(src), engine="auto")
     send.connect([recv.desc])
     T = 1500
     ds = block_slots(T, BS, NB, seed=3, device="cuda")

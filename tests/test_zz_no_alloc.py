@@ -7,7 +7,9 @@ its staging buffer in a fixed device array inside the library, so the caller
 passes only inputs and outputs.  The test calls it through its exported C
 symbol (ctypes) and checks, on two calls in a row and in both directions,
 that it produces exactly what the existing staged op
-(`fused_multi_layer_kv_transfer`, caller-provided staging tensor) produces.
+(`fused_multi_layer_kv_transfer`, caller-provided staging tensor) produces,
+and exactly what the PyTorch oracle of the layout (`gather_ref` /
+`scatter_ref`, plain indexing) produces.
 It also checks that an oversized transfer is rejected with an error.
 This file is named to be collected last.
 """
@@ -83,6 +85,9 @@ def test_noalloc_matches_staged_op_two_calls(fmt):
         torch.cuda.synchronize()
         assert rc == 0, msg
         assert torch.equal(got, want), f"store call {call}"
+        oracle = torch.zeros(lay.chunk_shape(T), dtype=lay.dtype)
+        lay.gather_ref(oracle, slots)
+        assert torch.equal(got, oracle), f"store call {call} vs the PyTorch oracle"
         # load direction, into two fresh caches
         kv_a, kv_b = _fresh(kv), _fresh(kv)
         lay_a, lay_b = PagedKVLayout(kv_a, use_mla=mla), PagedKVLayout(kv_b, use_mla=mla)
@@ -91,9 +96,12 @@ def test_noalloc_matches_staged_op_two_calls(fmt):
         rc, msg = _call(lib, lay_b, slots, want, False)
         torch.cuda.synchronize()
         assert rc == 0, msg
-        for a, b in zip(kv_a, kv_b):
-            for x, y in zip(a if isinstance(a, tuple) else (a,), b if isinstance(b, tuple) else (b,)):
+        kv_c = _fresh(kv)
+        PagedKVLayout(kv_c, use_mla=mla).scatter_ref(want, slots)
+        for a, b, c in zip(kv_a, kv_b, kv_c):
+            for x, y, z in zip(*(t if isinstance(t, tuple) else (t,) for t in (a, b, c))):
                 assert torch.equal(x, y), f"load call {call}"
+                assert torch.equal(y, z), f"load call {call} vs the PyTorch oracle"
 
 
 def test_noalloc_rejects_oversize():
