@@ -101,6 +101,8 @@ def parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="skip the prefill-forward + layer-by-layer push overlap measurement")
     ap.add_argument("--overlap-iters", type=int, default=2)
+    ap.add_argument("--no-config5", action="store_true",
+                    help="skip the DeepSeek-V3.2 MLA latent + C8 indexer push (config 5)")
     ap.add_argument("--fp8-tile", type=int, default=512,
                     help="tokens per fp8 push unit (one flag release per unit)")
     return ap.parse_args()
@@ -593,6 +595,17 @@ def main():
                                       iters=a.overlap_iters, warmup=1)
         barrier()
 
+    # ------------------- config 5: DeepSeek-V3.2 latent + C8 indexer push
+    config5 = None
+    if not a.no_config5:
+        torch.cuda.empty_cache()
+        barrier()
+        from lmcache_ascend_b200.bench_config5 import run_config5
+
+        config5 = run_config5(dev, rank, world, gloo, warmup=max(3, a.warmup),
+                              peer_copy_gbps=peer_copy["gbps_per_pair"] if peer_copy else None)
+        barrier()
+
     if rank == 0:
         per_pair = value / pairs
         if world == 1:
@@ -621,7 +634,7 @@ def main():
              "config": cfg, "bytes_per_pair_per_step": bytes_per_pair,
              "per_pair_gbps": round(per_pair, 2), "roofline": roof, "baseline": baseline,
              "clocks": ck, "e2e": e2e, "gpu_launches": launches, "ttft": ttft,
-             "push_fp8": fp8, "prefill_overlap": overlap,
+             "push_fp8": fp8, "prefill_overlap": overlap, "config5_dsv32_mla_c8": config5,
              **({"multicast": mcast} if mcast is not None else {})})
     if sender is not None:
         sender.close()

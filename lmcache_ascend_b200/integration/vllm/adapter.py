@@ -78,11 +78,18 @@ class RequestTracker:
     num_saved_tokens: int = 0
     disagg_spec: Optional[dict] = None
     num_pushed_tokens: int = 0  # prompt tokens handed to the direct push so far
+    group_block_ids: List[List[int]] = field(default_factory=list)  # groups 1..
 
-    def update(self, new_token_ids: Sequence[int], new_block_ids: Optional[Sequence[int]]):
+    def update(self, new_token_ids: Sequence[int], new_block_ids: Optional[Sequence[int]],
+               new_group_blocks: Optional[Sequence[Sequence[int]]] = None):
         self.token_ids.extend(new_token_ids)
         if new_block_ids:
             self.allocated_block_ids.extend(new_block_ids)
+        for g, blocks in enumerate(new_group_blocks or ()):
+            while len(self.group_block_ids) <= g:
+                self.group_block_ids.append([])
+            if blocks:
+                self.group_block_ids[g].extend(blocks)
 
 
 @dataclass
@@ -96,6 +103,12 @@ class ReqMeta:
     disagg_spec: Optional[dict] = None
     # direct paged push: {"mode": "send"|"recv", "pd_req_id": ID, ...}
     direct: Optional[dict] = None
+    # KV cache groups after the first (e.g. the DSA indexer cache): slots of
+    # the same tokens in each group's own block table
+    group_slot_mappings: List[torch.Tensor] = field(default_factory=list)
+
+    def slots_of_group(self, g: int) -> torch.Tensor:
+        return self.slot_mapping if g == 0 else self.group_slot_mappings[g - 1]
 
     @staticmethod
     def build(tracker: RequestTracker, block_size: int, chunk_size: int,
@@ -121,9 +134,13 @@ class ReqMeta:
         blocks = torch.tensor(tracker.allocated_block_ids, dtype=torch.long)
         t = torch.arange(ntoks)
         slot = blocks[t // block_size] * block_size + t % block_size
-        return ReqMeta(tracker.req_id, torch.tensor(tracker.token_ids[:ntoks], dtype=torch.long),
-                       slot, save, load_spec if loading else None, is_last_prefill,
-                       tracker.disagg_spec)
+        r = ReqMeta(tracker.req_id, torch.tensor(tracker.token_ids[:ntoks], dtype=torch.long),
+                    slot, save, load_spec if loading else None, is_last_prefill,
+                    tracker.disagg_spec)
+        for gb in tracker.group_block_ids:
+            b = torch.tensor(gb, dtype=torch.long)
+            r.group_slot_mappings.append(b[t // block_size] * block_size + t % block_size)
+        return r
 
 
 @dataclass
@@ -169,6 +186,25 @@ def config_from_extra(extra: Optional[Dict[str, Any]]) -> LMCacheEngineConfig:
     if over:
         cfg.update(over)
     return cfg
+
+
+class _GroupedLookup:
+    """Lookup over every KV cache group's engine: a prefix counts as cached
+    only as far as every group holds it."""
+
+    def __init__(self, engines):
+        self.engines = engines
+
+    def lookup(self, tokens, lookup_id=None, pin: bool = False, **kw) -> int:
+        hit = None
+        for e in self.engines:
+            n = e.lookup(tokens, lookup_id=lookup_id, pin=pin, **kw)
+            hit = n if hit is None else min(hit, n)
+        return hit or 0
+
+    def lookup_unpin(self, lookup_id) -> None:
+        for e in self.engines:
+            e.lookup_unpin(lookup_id)
 
 
 class _DoneEvent:
@@ -231,6 +267,9 @@ class LMCacheConnectorV1Impl:
         self._push_failed: set = set()
         self._finished_pushers: set = set()  # finished in vLLM, blocks held for the push
         self._layer_index: Dict[str, int] = {}
+        self._engines: List[Any] = []       # one engine per KV cache group
+        self._group_names: List[List[str]] = []
+        self._layer_group: Dict[str, int] = {}
 
     # ============================================================ scheduler
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int) -> Tuple[int, bool]:
@@ -308,6 +347,8 @@ class LMCacheConnectorV1Impl:
             tokens = list(new.prompt_token_ids or [])
             blocks = list(new.block_ids[0]) if new.block_ids else []
             tr = RequestTracker(new.req_id, len(tokens), tokens, blocks)
+            if new.block_ids and len(new.block_ids) > 1:
+                tr.group_block_ids = [list(b) for b in new.block_ids[1:]]
             self._trackers[new.req_id] = tr
             pid = direct_push_id(new) if self.kv_role == "kv_producer" else None
             if pid is not None and self.engine_supports_direct():
@@ -334,7 +375,9 @@ class LMCacheConnectorV1Impl:
                 continue
             new_blocks = cached.new_block_ids[i]
             tr.update(cached.new_token_ids[i] if cached.new_token_ids else [],
-                      list(new_blocks[0]) if new_blocks else None)
+                      list(new_blocks[0]) if new_blocks else None,
+                      [list(b) for b in new_blocks[1:]] if new_blocks and len(new_blocks) > 1
+                      else None)
             done = cached.num_computed_tokens[i] + scheduler_output.num_scheduled_tokens[req_id]
             if tr.disagg_spec is not None:  # chunked prefill of a direct push
                 r = self._direct_send_meta(tr, done)
@@ -386,22 +429,52 @@ class LMCacheConnectorV1Impl:
             return 0
 
         self._layer_names = sorted(kv_caches, key=layer_index)
-        self._layer_index = {n: i for i, n in enumerate(self._layer_names)}
-        caches = [kv_caches[n] for n in self._layer_names]
         from ...v1.kv_layer_groups import KVLayerGroupsManager
 
         self.layer_groups = KVLayerGroupsManager()
         self.layer_groups.build_kv_layer_groups({n: kv_caches[n] for n in self._layer_names})
-        if self.layer_groups.num_groups > 1:
-            raise ValueError("layers with different KV cache shapes/dtypes "
-                             f"({self.layer_groups.num_groups} groups) need one engine per group")
+        ng = self.layer_groups.num_groups
+        # group g's layers, in layer order; index of a layer inside its group
+        self._group_names = [list(grp.layer_names) for grp in self.layer_groups.kv_layer_groups]
+        self._layer_group = {n: g for g, names in enumerate(self._group_names) for n in names}
+        self._layer_index = {n: i for names in self._group_names for i, n in enumerate(names)}
         eng = self._ensure_engine()
-        first = caches[0]
+        caches0 = [kv_caches[n] for n in self._group_names[0]]
+        first = caches0[0] if isinstance(caches0[0], torch.Tensor) else caches0[0][0]
         if self.metadata.kv_dtype is None:
             self.metadata.kv_dtype = first.dtype
-        eng.post_init(kvcaches=caches)
+        eng.post_init(kvcaches=caches0)
+        self._engines = [eng]
+        for g in range(1, ng):
+            self._engines.append(self._group_engine(g, [kv_caches[n]
+                                                        for n in self._group_names[g]]))
         if self.rank == 0 and self._lookup_server is None:
-            self._lookup_server = LookupServer(eng, self.lookup_url)
+            self._lookup_server = LookupServer(_GroupedLookup(self._engines), self.lookup_url)
+
+    def _group_engine(self, g: int, caches):
+        """Engine of KV cache group ``g`` > 0 (e.g. the DSA indexer): its own
+        paged layout, chunk keys under its own instance id, a CPU tier sized
+        by its share of the bytes per token."""
+        import copy
+
+        from ...v1.cache_engine import LMCacheEngine
+        from ...v1.gpu_connector import CreateGPUConnector
+
+        grp = self.layer_groups.kv_layer_groups
+        per_tok = [x.num_layers * x.hidden_dim_size * (2 if len(x.shape) == 5 else 1)
+                   for x in grp]
+        cfg = copy.deepcopy(self.config)
+        cfg.lmcache_instance_id = f"{self.config.lmcache_instance_id}-g{g}"
+        cfg.max_local_cpu_size = max(0.01, self.config.max_local_cpu_size * per_tok[g] /
+                                     max(1, sum(per_tok)))
+        cfg.enable_pd = False  # the direct push moves the first group
+        md = copy.deepcopy(self.metadata)
+        md.model_name = f"{self.metadata.model_name}#g{g}"
+        first = caches[0] if isinstance(caches[0], torch.Tensor) else caches[0][0]
+        md.kv_dtype = first.dtype
+        eng = LMCacheEngine(cfg, md, CreateGPUConnector(cfg, md))
+        eng.post_init(kvcaches=caches)
+        return eng
 
     def bind_connector_metadata(self, meta: LMCacheConnectorMetadata) -> None:
         self._meta = meta
@@ -437,22 +510,26 @@ class LMCacheConnectorV1Impl:
                 continue
             n = spec.lmcache_cached_tokens
             skip = (spec.vllm_cached_tokens // self.chunk_size) * self.chunk_size
-            toks, slots = r.token_ids[:n], r.slot_mapping[:n]
+            toks = r.token_ids[:n]
             mask = self._mask(n, skip)
-            if self.config.use_layerwise:
-                g = eng.retrieve_layer(toks, mask, slot_mapping=slots)
-                next(g)
-                self._layer_load_gens.append(g)
-            else:
-                ret = eng.retrieve(toks, mask, slot_mapping=slots)
-                got = int(ret.sum())
-                if got < n - skip:
-                    logger.warning("req %s: loaded %d of %d expected tokens", r.req_id, got,
-                                   n - skip)
+            for gi, geng in enumerate(self._engines):
+                slots = r.slots_of_group(gi)[:n]
+                if self.config.use_layerwise:
+                    g = geng.retrieve_layer(toks, mask, slot_mapping=slots)
+                    next(g)
+                    self._layer_load_gens.append((gi, g))
+                else:
+                    ret = geng.retrieve(toks, mask, slot_mapping=slots)
+                    got = int(ret.sum())
+                    if got < n - skip:
+                        logger.warning("req %s group %d: loaded %d of %d expected tokens",
+                                       r.req_id, gi, got, n - skip)
 
     def wait_for_layer_load(self, layer_name: str) -> None:
-        for g in self._layer_load_gens:
-            next(g, None)
+        gi = self._layer_group.get(layer_name, 0)
+        for g_, gen in self._layer_load_gens:
+            if g_ == gi:
+                next(gen, None)
 
     def _begin_direct_pushes(self, eng) -> None:
         """Prefiller, first layer of a step: one grant per pushing request
@@ -488,19 +565,24 @@ class LMCacheConnectorV1Impl:
                 h.push_layer(idx)
         if not self.config.use_layerwise:
             return
-        eng = self._ensure_engine()
-        if layer_name == self._layer_names[0]:
-            self._layer_store_gens = []
+        self._ensure_engine()
+        gi = self._layer_group.get(layer_name, 0)
+        if self._layer_index.get(layer_name, 0) == 0:  # first layer of its group
+            if gi == 0:
+                self._layer_store_gens = []
+            geng = self._engines[gi]
             for r in self._meta.requests:
                 if r.save_spec is None:
                     continue
                 n = r.token_ids.numel()
-                g = eng.store_layer(r.token_ids, self._mask(n, r.save_spec.skip_leading_tokens),
-                                    slot_mapping=r.slot_mapping)
+                g = geng.store_layer(r.token_ids,
+                                     self._mask(n, r.save_spec.skip_leading_tokens),
+                                     slot_mapping=r.slots_of_group(gi))
                 next(g)  # before the first layer
-                self._layer_store_gens.append(g)
-        for g in self._layer_store_gens:
-            next(g, None)
+                self._layer_store_gens.append((gi, g))
+        for g_, gen in self._layer_store_gens:
+            if g_ == gi:
+                next(gen, None)
 
     def wait_for_save(self) -> None:
         if self._meta is None or self.kv_role == "kv_consumer":
@@ -509,9 +591,9 @@ class LMCacheConnectorV1Impl:
             h.finish()  # the blocks stay with vLLM until get_finished reports it
             self._sending.setdefault(req_id, []).append(h)
         self._step_handles = []
-        eng = self._ensure_engine()
+        self._ensure_engine()
         if self.config.use_layerwise:
-            for g in self._layer_store_gens:
+            for _, g in self._layer_store_gens:
                 for _ in g:
                     pass
             self._layer_store_gens = []
@@ -520,8 +602,9 @@ class LMCacheConnectorV1Impl:
             if r.save_spec is None or not r.save_spec.can_save:
                 continue
             n = r.token_ids.numel()
-            eng.store(r.token_ids, self._mask(n, r.save_spec.skip_leading_tokens),
-                      slot_mapping=r.slot_mapping, req_id=r.req_id)
+            for gi, geng in enumerate(self._engines):
+                geng.store(r.token_ids, self._mask(n, r.save_spec.skip_leading_tokens),
+                           slot_mapping=r.slots_of_group(gi), req_id=r.req_id)
 
     def _poll_receiving(self) -> set:
         """Decoder: requests whose pushed KV has fully arrived.  Once every
@@ -604,8 +687,17 @@ class LMCacheConnectorV1Impl:
         out, self.load_error_block_ids = self.load_error_block_ids, set()
         return out
 
+    @property
+    def lookup_engine(self):
+        """What the scheduler's lookups should ask: the engine, or every
+        group's engine when the model has several KV cache groups."""
+        return _GroupedLookup(self._engines) if len(self._engines) > 1 else self.engine
+
     def shutdown(self) -> None:
         if self._lookup_server is not None:
             self._lookup_server.close()
         if self._lookup is not None:
             self._lookup.close()
+        for e in self._engines[1:]:
+            e.close()
+        self._engines = self._engines[:1]

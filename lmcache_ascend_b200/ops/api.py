@@ -487,13 +487,23 @@ def decode_fast_new(*args, **kwargs):
 
 # ----------------------------------------------------------------- K8
 def rotary_embedding_k_fused(old_positions, new_positions, key, head_size, cos_sin_cache,
-                             is_neox) -> None:
+                             is_neox, slot_mapping=None) -> None:
+    """Rotate keys in place from ``old_positions`` to ``new_positions``.
+    ``slot_mapping`` (optional): token t's row is ``key[slot_mapping[t]]``
+    (``key`` a [cache rows, H*D] view of a paged plane; slot -1 skips)."""
     if key.is_cuda:
         native().rotary_embedding_k_fused(old_positions, new_positions, key, head_size,
-                                          cos_sin_cache, is_neox)
+                                          cos_sin_cache, is_neox, slot_mapping)
         return
-    key.copy_(R.rope_delta_ref(old_positions, new_positions, key, head_size, cos_sin_cache,
-                               is_neox).to(key.dtype))
+    if slot_mapping is None:
+        key.copy_(R.rope_delta_ref(old_positions, new_positions, key, head_size,
+                                   cos_sin_cache, is_neox).to(key.dtype))
+        return
+    sm = slot_mapping.long()
+    keep = sm >= 0
+    rows = key[sm[keep]]
+    key[sm[keep]] = R.rope_delta_ref(old_positions[keep], new_positions[keep], rows, head_size,
+                                     cos_sin_cache, is_neox).to(key.dtype)
 
 
 # ----------------------------------------------------------------- misc

@@ -216,6 +216,8 @@ struct BulkPushJob {
   int32_t stage_bytes;
   unsigned *flags[kMaxReplicas];   // per replica: layer flag array (or null)
   unsigned long long budget_ns;    // bound on each mbarrier wait
+  uint32_t bulk_planes;            // bit p: plane p moves by TMA bulk copies, else by
+                                   // per-lane loads/stores (rows not 16-byte aligned)
 };
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -225,6 +227,24 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 template <int N>
 __device__ __forceinline__ void bulk_wait_complete() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One row of `rb` bytes with the widest granule both addresses allow.
+__device__ __forceinline__ void copy_row_granules(char *dst, const char *src, int rb) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) |
+                      static_cast<uintptr_t>(rb);
+  if ((a & 15) == 0) {
+    for (int o = 0; o < rb; o += 16)
+      *reinterpret_cast<int4 *>(dst + o) = *reinterpret_cast<const int4 *>(src + o);
+  } else if ((a & 7) == 0) {
+    for (int o = 0; o < rb; o += 8)
+      *reinterpret_cast<long long *>(dst + o) = *reinterpret_cast<const long long *>(src + o);
+  } else if ((a & 3) == 0) {
+    for (int o = 0; o < rb; o += 4)
+      *reinterpret_cast<int *>(dst + o) = *reinterpret_cast<const int *>(src + o);
+  } else {
+    for (int o = 0; o < rb; ++o) dst[o] = src[o];
+  }
 }
 
 // Position of a warp in its own sequence of pieces.
@@ -261,6 +281,16 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
   }
   __syncwarp();
 
+  auto plane_of_unit = [&](int i) {
+    const int u = gw + i * nw;
+    return (u - (u / units_per_layer) * units_per_layer) / tiles;
+  };
+  auto is_bulk = [&](int i) { return (j.bulk_planes >> plane_of_unit(i)) & 1u; };
+  // the bulk pipeline visits only units of bulk planes
+  auto skip_small = [&](int i) {
+    while (gw + i * nw < total && !is_bulk(i)) ++i;
+    return i;
+  };
   auto valid = [&](const PieceCursor &q) { return gw + q.i * nw < total; };
   // piece -> (layer index in launch, plane, tokens); `last`: ends its unit
   auto piece_unit = [&](const PieceCursor &q, bool &last) {
@@ -281,7 +311,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
   };
   auto advance = [&](PieceCursor &q, bool last) {
     if (last) {
-      ++q.i;
+      q.i = skip_small(q.i + 1);
       q.piece = 0;
     } else {
       ++q.piece;
@@ -342,7 +372,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
       if (!placed && ql[i] < 0) ql[i] = layer, qk[i] = k, placed = true;
   };
 
-  PieceCursor lc{0, 0}, sc{0, 0};
+  PieceCursor lc{skip_small(0), 0}, sc{skip_small(0), 0};
   int kl = 0;
   for (; kl < S - 1 && valid(lc); ++kl) {
     bool last;
@@ -393,6 +423,47 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
   }
   bulk_wait_complete<0>();
   release_upto(0x7fffffff);
+
+  // Units of planes whose rows are not 16-byte aligned (the 4-byte scale
+  // plane of a C8 indexer, say): one token per lane, widest aligned granule,
+  // published right after the warp's stores (generic proxy only).
+  if (j.bulk_planes == (1u << np) - 1u) return;
+  for (int i = 0; gw + i * nw < total; ++i) {
+    if (is_bulk(i)) continue;
+    const int u = gw + i * nw;
+    const int li = u / units_per_layer;
+    const int p = (u - li * units_per_layer) / tiles;
+    const int t0 = (u - li * units_per_layer - p * tiles) * j.tile_tokens;
+    const int n = min(c.num_tokens - t0, j.tile_tokens);
+    const int layer = c.layer_begin + li;
+    const PlaneDesc sp = plane_of(c.paged, p);
+    const PlaneDesc dp = plane_of(c.dst_paged, p);
+    const char *sb = reinterpret_cast<const char *>(c.paged.ptrs[layer * np + p]);
+    for (int t = lane; t < n; t += 32) {
+      const int64_t ss = push_slot(c.slots, c.slot_is_i64, t0 + t);
+      const int64_t dd = push_slot(c.dst_slots, c.slot_is_i64, t0 + t);
+      if (ss < 0 || dd < 0) continue;
+      if (ss >= c.paged.num_slots || dd >= c.dst_paged.num_slots) {
+        report_status(c.status, kStatusBadSlot, t0 + t, ss, dd);
+        continue;
+      }
+      const char *src = sb + (ss / c.paged.block_size) * sp.block_stride +
+                        (ss % c.paged.block_size) * sp.slot_stride;
+      const int64_t doff = (dd / c.dst_paged.block_size) * dp.block_stride +
+                           (dd % c.dst_paged.block_size) * dp.slot_stride;
+      for (int rep = 0; rep < j.replicas; ++rep) {
+        char *db = reinterpret_cast<char *>(
+            j.dst_ptrs[static_cast<int64_t>(rep) * j.dst_layers * np + layer * np + p]);
+        copy_row_granules(db + doff, src, sp.row_bytes);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      fence_acq_rel_sys();
+      for (int r = 0; r < j.replicas; ++r)
+        if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -748,10 +819,15 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
       static_cast<long long>(num_layers);
   const auto stream = at::cuda::getCurrentCUDAStream(dev).stream();
   TORCH_CHECK(mode >= 0 && mode <= 2, "pd_push: mode 0 (auto), 1 (bulk) or 2 (simt)");
-  int max_row = 0;
+  // planes that move by TMA bulk copies: 16-byte aligned rows, strides and
+  // bases on both sides, rows that fit a stage; the others go per lane inside
+  // the same kernel (at least one bulk plane is needed to pick this engine)
+  uint32_t bulk_planes = 0;
   for (int p = 0; p < j.src.num_planes; ++p)
-    max_row = std::max(max_row, static_cast<int>(j.src.plane[p].row_bytes));
-  const bool bulk_ok = src.aligned() && dst.aligned() && max_row <= kBulkStageBytes;
+    if (src.plane_aligned(p) && dst.plane_aligned(p) &&
+        j.src.plane[p].row_bytes <= kBulkStageBytes)
+      bulk_planes |= 1u << p;
+  const bool bulk_ok = bulk_planes != 0 && !src.segmented() && !dst.segmented();
   TORCH_CHECK(mode != 1 || bulk_ok,
               "pd_push: the bulk engine needs 16-byte aligned, contiguous rows of at most ",
               kBulkStageBytes, " bytes on both sides");
@@ -776,6 +852,7 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
     b.stage_bytes = kBulkStageBytes;
     for (int r = 0; r < kMaxReplicas; ++r) b.flags[r] = j.flags[r];
     b.budget_ns = 2000000000ull;  // 2 s per mbarrier wait
+    b.bulk_planes = bulk_planes;
     const size_t smem = kTmaRingOffset +
                         static_cast<size_t>(kBulkWarps) * kBulkStages * kBulkStageBytes;
     static bool attr_set[64] = {false};

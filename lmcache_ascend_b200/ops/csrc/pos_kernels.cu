@@ -18,6 +18,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 namespace lmc {
 
 template <typename T>
@@ -35,20 +37,29 @@ template <>
 __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
 // grid.x = tokens (grid-stride), block threads cover heads * rot/2 pairs
+// Row of token t: t itself, or rows[t] when the keys live in a paged cache
+// (rows = slot mapping; a negative slot skips the token).
+template <typename PT>
+__device__ __forceinline__ int64_t key_row(const PT *rows, int t) {
+  return rows == nullptr ? static_cast<int64_t>(t) : static_cast<int64_t>(rows[t]);
+}
+
 template <typename KT, typename CT, typename PT>
 __global__ void rope_delta_kernel(const PT *__restrict__ old_pos,
                                   const PT *__restrict__ new_pos, KT *key,
                                   const CT *__restrict__ cache, int num_tokens,
                                   int num_heads, int head_size, int rot_dim,
-                                  int64_t key_stride, bool neox) {
+                                  int64_t key_stride, bool neox, const PT *rows) {
   const int half = rot_dim / 2;
   const int pairs = num_heads * half;
   for (int t = blockIdx.x; t < num_tokens; t += gridDim.x) {
+    const int64_t row = key_row(rows, t);
+    if (row < 0) continue;
     const int64_t po = static_cast<int64_t>(old_pos[t]);
     const int64_t pn = static_cast<int64_t>(new_pos[t]);
     const CT *co = cache + po * rot_dim;
     const CT *cn = cache + pn * rot_dim;
-    KT *kt = key + static_cast<int64_t>(t) * key_stride;
+    KT *kt = key + row * key_stride;
     for (int q = threadIdx.x; q < pairs; q += blockDim.x) {
       const int h = q / half;
       const int i = q - h * half;
@@ -67,45 +78,70 @@ __global__ void rope_delta_kernel(const PT *__restrict__ old_pos,
   }
 }
 
+// N consecutive cos/sin values as fp32: 16-byte loads for an fp32 cache
+// (the caller's offsets keep them 16-byte aligned), element loads otherwise.
+template <typename CT, int N>
+__device__ __forceinline__ void load_cs(const CT *p, float (&o)[N]) {
+  if constexpr (std::is_same<CT, float>::value && N % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k) {
+      const float4 v = reinterpret_cast<const float4 *>(p)[k];
+      o[4 * k] = v.x;
+      o[4 * k + 1] = v.y;
+      o[4 * k + 2] = v.z;
+      o[4 * k + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < N; ++k) o[k] = to_f(p[k]);
+  }
+}
+
 // Vector path: one warp per token (grid-stride); a unit is VE = 16 / sizeof(KT)
-// consecutive rotary dims of one head, moved with 16-byte loads and stores.
-// neox: the unit's first halves at [i0, i0 + VE) and partners at half + i0;
-// GPT-J: the unit holds VE / 2 adjacent (2p, 2p + 1) pairs.  Same arithmetic
-// as rope_delta_kernel, so both paths give identical results.
+// consecutive rotary dims of one head, moved with 16-byte loads and stores,
+// and its cos/sin rows read as vectors too.  neox: the unit's first halves at
+// [i0, i0 + VE) and partners at half + i0; GPT-J: the unit holds VE / 2
+// adjacent (2p, 2p + 1) pairs.  Same arithmetic as rope_delta_kernel, so both
+// paths give identical results.
 template <typename KT, typename CT, typename PT, bool kNeox>
 __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
     const PT *__restrict__ old_pos, const PT *__restrict__ new_pos, KT *key,
     const CT *__restrict__ cache, int num_tokens, int num_heads, int head_size, int rot_dim,
-    int64_t key_stride) {
+    int64_t key_stride, const PT *rows) {
   constexpr int VE = 16 / sizeof(KT);
+  constexpr int NP = kNeox ? VE : VE / 2;  // rotation pairs per unit
   const int half = rot_dim / 2;
   const int per_head = kNeox ? half / VE : rot_dim / VE;
   const int units = num_heads * per_head;
   const int lane = threadIdx.x & 31;
   const int nw = gridDim.x * (blockDim.x >> 5);
   for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tokens; t += nw) {
+    const int64_t row = key_row(rows, t);
+    if (row < 0) continue;
     const int64_t po = static_cast<int64_t>(old_pos[t]);
     const int64_t pn = static_cast<int64_t>(new_pos[t]);
     const CT *co = cache + po * rot_dim;
     const CT *cn = cache + pn * rot_dim;
-    KT *kt = key + static_cast<int64_t>(t) * key_stride;
+    KT *kt = key + row * key_stride;
     for (int u = lane; u < units; u += 32) {
       const int h = u / per_head;
       const int g = u - h * per_head;
       KT *kh = kt + static_cast<int64_t>(h) * head_size;
+      const int i0 = kNeox ? g * VE : g * VE / 2;  // first rotation pair of the unit
+      float ca[NP], sa[NP], cb[NP], sb[NP];
+      load_cs<CT, NP>(cn + i0, ca);
+      load_cs<CT, NP>(cn + half + i0, sa);
+      load_cs<CT, NP>(co + i0, cb);
+      load_cs<CT, NP>(co + half + i0, sb);
       if (kNeox) {
-        const int i0 = g * VE;
         uint4 a = *reinterpret_cast<const uint4 *>(kh + i0);
         uint4 b = *reinterpret_cast<const uint4 *>(kh + half + i0);
         KT *x1 = reinterpret_cast<KT *>(&a);
         KT *x2 = reinterpret_cast<KT *>(&b);
 #pragma unroll
         for (int j = 0; j < VE; ++j) {
-          const int i = i0 + j;
-          const float ca = to_f(cn[i]), sa = to_f(cn[half + i]);
-          const float cb = to_f(co[i]), sb = to_f(co[half + i]);
-          const float cd = ca * cb + sa * sb;
-          const float sd = sa * cb - ca * sb;
+          const float cd = ca[j] * cb[j] + sa[j] * sb[j];
+          const float sd = sa[j] * cb[j] - ca[j] * sb[j];
           const float v1 = to_f(x1[j]), v2 = to_f(x2[j]);
           x1[j] = from_f<KT>(v1 * cd - v2 * sd);
           x2[j] = from_f<KT>(v2 * cd + v1 * sd);
@@ -118,11 +154,8 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
         KT *x = reinterpret_cast<KT *>(&a);
 #pragma unroll
         for (int j = 0; j < VE / 2; ++j) {
-          const int i = e0 / 2 + j;
-          const float ca = to_f(cn[i]), sa = to_f(cn[half + i]);
-          const float cb = to_f(co[i]), sb = to_f(co[half + i]);
-          const float cd = ca * cb + sa * sb;
-          const float sd = sa * cb - ca * sb;
+          const float cd = ca[j] * cb[j] + sa[j] * sb[j];
+          const float sd = sa[j] * cb[j] - ca[j] * sb[j];
           const float v1 = to_f(x[2 * j]), v2 = to_f(x[2 * j + 1]);
           x[2 * j] = from_f<KT>(v1 * cd - v2 * sd);
           x[2 * j + 1] = from_f<KT>(v2 * cd + v1 * sd);
@@ -136,13 +169,15 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
 template <typename KT, typename CT, typename PT>
 static void launch_rope_t(const PT *op, const PT *np, at::Tensor &key, const at::Tensor &cache,
                           int T, int H, int D, int rot, int64_t stride, bool neox,
-                          cudaStream_t s) {
+                          cudaStream_t s, const PT *rows) {
   constexpr int VE = 16 / sizeof(KT);
   const int half = rot / 2;
   const bool vec = (reinterpret_cast<uintptr_t>(key.data_ptr()) % 16 == 0) &&
                    (stride * static_cast<int64_t>(sizeof(KT))) % 16 == 0 &&
                    (D * static_cast<int>(sizeof(KT))) % 16 == 0 &&
-                   (neox ? half % VE == 0 : rot % VE == 0);
+                   (neox ? half % VE == 0 : rot % VE == 0) &&
+                   reinterpret_cast<uintptr_t>(cache.data_ptr()) % 16 == 0 &&
+                   (rot * static_cast<int>(sizeof(CT))) % 16 == 0;
   auto *kp = reinterpret_cast<KT *>(key.data_ptr());
   const auto *cp = reinterpret_cast<const CT *>(cache.data_ptr());
   if (vec) {
@@ -152,34 +187,40 @@ static void launch_rope_t(const PT *op, const PT *np, at::Tensor &key, const at:
     const int blocks = std::max(1, std::min((T + 7) / 8, sms * 8));
     if (neox)
       rope_delta_vec_kernel<KT, CT, PT, true><<<blocks, 256, 0, s>>>(op, np, kp, cp, T, H, D,
-                                                                     rot, stride);
+                                                                     rot, stride, rows);
     else
       rope_delta_vec_kernel<KT, CT, PT, false><<<blocks, 256, 0, s>>>(op, np, kp, cp, T, H, D,
-                                                                      rot, stride);
+                                                                      rot, stride, rows);
     return;
   }
   const int threads = std::min(1024, std::max(32, ((H * rot / 2) + 31) / 32 * 32));
   const int blocks = std::min(T, 148 * 16);
   rope_delta_kernel<KT, CT, PT><<<blocks, threads, 0, s>>>(op, np, kp, cp, T, H, D, rot, stride,
-                                                           neox);
+                                                           neox, rows);
 }
 
 template <typename KT, typename CT>
 static void launch_rope(const at::Tensor &op, const at::Tensor &np, at::Tensor &key,
                         const at::Tensor &cache, int T, int H, int D, int rot,
-                        int64_t stride, bool neox, cudaStream_t s) {
+                        int64_t stride, bool neox, cudaStream_t s,
+                        const c10::optional<at::Tensor> &rows) {
   if (op.scalar_type() == at::kLong)
     launch_rope_t<KT, CT, int64_t>(op.data_ptr<int64_t>(), np.data_ptr<int64_t>(), key, cache,
-                                   T, H, D, rot, stride, neox, s);
+                                   T, H, D, rot, stride, neox, s,
+                                   rows.has_value() ? rows->data_ptr<int64_t>() : nullptr);
   else
     launch_rope_t<KT, CT, int32_t>(op.data_ptr<int32_t>(), np.data_ptr<int32_t>(), key, cache,
-                                   T, H, D, rot, stride, neox, s);
+                                   T, H, D, rot, stride, neox, s,
+                                   rows.has_value() ? rows->data_ptr<int32_t>() : nullptr);
 }
 
+// `slot_mapping` (optional, the positions' dtype): token t's key row is
+// key[slot_mapping[t]] -- key is then a [cache rows, H*D] view of a paged
+// cache plane -- and tokens with a negative slot are skipped.
 void rotary_embedding_k_fused(const at::Tensor &old_positions,
                               const at::Tensor &new_positions, at::Tensor &key,
                               int64_t head_size, const at::Tensor &cos_sin_cache,
-                              bool is_neox) {
+                              bool is_neox, const c10::optional<at::Tensor> &slot_mapping) {
   TORCH_CHECK(key.is_cuda() && old_positions.is_cuda() && new_positions.is_cuda() &&
                   cos_sin_cache.is_cuda(),
               "rope: all tensors must be on the device");
@@ -189,9 +230,20 @@ void rotary_embedding_k_fused(const at::Tensor &old_positions,
               "rope: positions must both be int32 or int64");
   const int T = static_cast<int>(old_positions.numel());
   TORCH_CHECK(new_positions.numel() == T, "rope: position length mismatch");
-  TORCH_CHECK(key.dim() >= 2 && key.size(0) == T, "rope: key must be [T, H*D]");
+  const bool mapped = slot_mapping.has_value();
+  if (mapped) {
+    TORCH_CHECK(slot_mapping->is_cuda() && slot_mapping->is_contiguous() &&
+                    slot_mapping->scalar_type() == old_positions.scalar_type() &&
+                    slot_mapping->numel() == T,
+                "rope: slot_mapping must be a contiguous device tensor of the positions' "
+                "dtype and length");
+    TORCH_CHECK(key.dim() == 2, "rope: with a slot mapping, key is [cache rows, H*D]");
+  } else {
+    TORCH_CHECK(key.dim() >= 2 && key.size(0) == T, "rope: key must be [T, H*D]");
+  }
   TORCH_CHECK(key.stride(-1) == 1, "rope: key rows must be contiguous");
-  const int64_t hidden = key.numel() / T;
+  const int64_t rows_in_key = key.size(0);
+  const int64_t hidden = rows_in_key > 0 ? key.numel() / rows_in_key : 0;
   TORCH_CHECK(hidden % head_size == 0, "rope: hidden not a multiple of head_size");
   const int H = static_cast<int>(hidden / head_size);
   const int rot = static_cast<int>(cos_sin_cache.size(1));
@@ -210,13 +262,13 @@ void rotary_embedding_k_fused(const at::Tensor &old_positions,
 #define LMC_ROPE_CASE(KTYPE, KCT)                                                  \
   if (ct == at::kFloat)                                                            \
     launch_rope<KTYPE, float>(op, np, key, cos_sin_cache, T, H, D, rot, stride,    \
-                              is_neox, s);                                         \
+                              is_neox, s, slot_mapping);                           \
   else if (ct == at::kBFloat16)                                                    \
     launch_rope<KTYPE, __nv_bfloat16>(op, np, key, cos_sin_cache, T, H, D, rot,    \
-                                      stride, is_neox, s);                         \
+                                      stride, is_neox, s, slot_mapping);           \
   else if (ct == at::kHalf)                                                        \
     launch_rope<KTYPE, __half>(op, np, key, cos_sin_cache, T, H, D, rot, stride,   \
-                               is_neox, s);                                        \
+                               is_neox, s, slot_mapping);                          \
   else                                                                             \
     TORCH_CHECK(false, "rope: unsupported cos_sin_cache dtype");
   if (kt == at::kBFloat16) {

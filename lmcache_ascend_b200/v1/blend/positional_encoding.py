@@ -4,14 +4,15 @@ self-check (reference lmcache_ascend/v1/blend/positional_encoding.py:95-250).
 ``FusedRope(old, new, k)`` rotates cached keys from the positions they were
 stored at to the positions they take in the new prompt, in place, with the
 native K8 kernel on CUDA tensors (oracle on CPU).  ``get_fused_rope``
-validates the RoPE parameters (full rotary dim, no scaling) and checks the
-fused op against plain RoPE before handing it out; it returns None when the
-check fails so blending is disabled rather than silently wrong.
+refuses RoPE variants the kernel does not implement (partial rotary dim,
+scaling) and checks the fused op on random keys and positions against the
+oracle before handing it out; it returns None when the check fails so
+blending is disabled rather than silently wrong.
 """
 
 from __future__ import annotations
 
-from typing import Any, Callable, Dict, Optional
+from typing import Any, Callable, Dict, List, Optional, Tuple
 
 import torch
 
@@ -67,56 +68,68 @@ class FusedRope:
         return self.fused_encode(old_positions, new_positions, k)
 
 
-def validate_rope_params(head_size: int, rotary_dim: int, max_position: int, base: float,
-                         is_neox_style: bool = True, rope_scaling: Optional[Dict[str, Any]] = None,
-                         dtype=None, partial_rotary_factor: float = 1.0) -> bool:
-    if rotary_dim != head_size:
-        logger.error("KV blending supports rotary_dim == head_size only")
-        return False
-    if rope_scaling is not None:
-        logger.error("KV blending does not support rope scaling")
-        return False
-    if partial_rotary_factor != 1.0:
-        logger.error("KV blending does not support a partial rotary factor")
-        return False
-    return True
+def unsupported_rope(head_size: int, rotary_dim: int, rope_scaling: Optional[Dict[str, Any]],
+                     partial_rotary_factor: float) -> List[str]:
+    """Reasons the fused re-rotation cannot serve this model's RoPE (empty
+    list: supported).  The kernel rotates the whole head with unscaled
+    frequencies, so a partial rotary dim or any rope scaling rules it out."""
+    why = []
+    if rotary_dim != head_size or partial_rotary_factor != 1.0:
+        why.append(f"partial rotary embedding (rotary_dim {rotary_dim} of {head_size}, "
+                   f"factor {partial_rotary_factor})")
+    if rope_scaling:
+        why.append(f"rope scaling {rope_scaling}")
+    return why
 
 
-def validate_reverse_correctness(rope: BasicRope, reverse_rope: BasicReverseRope,
-                                 fused_rope: FusedRope, head_size: int, device) -> bool:
-    hidden = head_size * 8
-    n = 10
-    g = torch.Generator().manual_seed(0)
-    q = torch.rand(n, hidden, generator=g).to(device=device, dtype=torch.bfloat16)
-    k = torch.rand(n, hidden, generator=g).to(device=device, dtype=torch.bfloat16)
-    pos = torch.arange(n, device=device)
-    q1, k1 = rope(pos, q.clone(), k.clone())
-    q1, k1 = reverse_rope(pos, q1, k1)
-    err_q = (q - q1).abs().max().item()
-    err_k = (k - k1).abs().max().item()
-    pos2 = torch.arange(100, 100 + n, device=device)
-    _, k_at2 = rope(pos2, q.clone(), k.clone())
-    _, k_at1 = rope(pos, q.clone(), k.clone())
-    k_fused = fused_rope(pos, pos2, k_at1.clone())
-    err_f = (k_at2.float() - k_fused.float()).abs().max().item()
-    logger.info("rope self-check: reverse q %.4g k %.4g fused %.4g", err_q, err_k, err_f)
-    return err_q < 0.1 and err_k < 0.1 and err_f < 0.1
+def self_check(fused_rope: "FusedRope", max_position: int, device, heads: int = 4,
+               tokens: int = 64, seed: int = 1234) -> Tuple[bool, float, float]:
+    """Re-rotate random bf16 keys from random positions to random new ones
+    and compare with keys rotated at the new positions directly (oracle),
+    then rotate back and compare with the start.
+
+    Tolerance: each side of the comparison went through at most two bf16
+    roundings (2^-8 relative each) plus the fp32 angle error, which grows
+    with the position (about position x 2^-23 radians), all relative to the
+    largest key magnitude.  Returns (passed, max error, tolerance)."""
+    D = fused_rope.head_size
+    g = torch.Generator().manual_seed(seed)
+    k = torch.randn(tokens, heads * D, generator=g).to(torch.bfloat16)
+    half = max(1, max_position // 2)
+    old = torch.randint(0, half, (tokens,), generator=g)
+    new = torch.randint(0, half, (tokens,), generator=g) + torch.randint(0, 2, (tokens,),
+                                                                        generator=g) * (half - 1)
+    new = new.clamp(max=max_position - 1)
+    cache = fused_rope.cos_sin_cache.cpu()
+    neox = fused_rope.is_neox_style
+    at_old = rope_apply_ref(old, k.float(), D, cache, neox).to(torch.bfloat16)
+    at_new = rope_apply_ref(new, k.float(), D, cache, neox).to(torch.bfloat16)
+    moved = fused_rope(old.to(device), new.to(device), at_old.clone().to(device)).cpu()
+    back = fused_rope(new.to(device), old.to(device), moved.clone().to(device)).cpu()
+    scale = float(k.float().abs().max())
+    tol = (2.0 ** -7 + max_position * 2.0 ** -23) * scale * 2
+    err = max(float((moved.float() - at_new.float()).abs().max()),
+              float((back.float() - at_old.float()).abs().max()))
+    return err <= tol, err, tol
 
 
 def get_fused_rope(head_size: int, rotary_dim: int, max_position: int, base: float,
                    is_neox_style: bool = True, rope_scaling: Optional[Dict[str, Any]] = None,
                    dtype=None, partial_rotary_factor: float = 1.0,
                    device=None) -> Optional[Callable[..., Any]]:
-    if not validate_rope_params(head_size, rotary_dim, max_position, base, is_neox_style,
-                                rope_scaling, dtype, partial_rotary_factor):
-        logger.warning("unsupported rope parameters: CacheBlend disabled")
+    """The fused K re-rotation for this RoPE, or None (blending disabled)
+    when the RoPE is not supported or the op fails its self-check."""
+    why = unsupported_rope(head_size, rotary_dim, rope_scaling, partial_rotary_factor)
+    if why:
+        logger.warning("CacheBlend disabled: %s", "; ".join(why))
         return None
     device = device or ("cuda" if torch.cuda.is_available() else "cpu")
     cache = make_cos_sin_cache(max_position, rotary_dim, base).to(device)
-    rope = BasicRope(cache, head_size, is_neox_style)
     fused = FusedRope(cache, head_size, is_neox_style)
-    if not validate_reverse_correctness(rope, BasicReverseRope(cache, head_size, is_neox_style),
-                                        fused, head_size, device):
-        logger.error("fused/reverse rotary encoding failed its self-check: blending disabled")
+    ok, err, tol = self_check(fused, max_position, device)
+    logger.info("fused RoPE self-check: max error %.3g (tolerance %.3g)", err, tol)
+    if not ok:
+        logger.error("fused RoPE failed its self-check (%.3g > %.3g): blending disabled",
+                     err, tol)
         return None
     return fused

@@ -132,6 +132,78 @@ class _LazyLayers:
         self.owned = []
 
 
+@dataclass
+class SparseLayerRequest:
+    """One layer of a sparse load: paged slot ``slot_mapping[i]`` receives
+    token ``selected_token_idx[i]`` of the request (device tensors, same
+    integer dtype and length)."""
+
+    selected_token_idx: torch.Tensor
+    slot_mapping: torch.Tensor
+
+
+@dataclass
+class SparseRetrieveState:
+    """Warm metadata of one long-context request for sparse (top-k) loads,
+    kept by the caller between decode steps: the request's cached chunks,
+    one held object per chunk, and the device table of their addresses.
+    Later steps reuse it without touching the storage tiers; a longer
+    context extends it (``extend``), and a failed extension leaves it as it
+    was (reference rollback guard: lmcache_ascend/v1/cache_engine.py:257-300)."""
+
+    keys: List[CacheEngineKey] = field(default_factory=list)
+    ends: List[int] = field(default_factory=list)
+    objs: List[MemoryObj] = field(default_factory=list)
+    ptrs: Optional[torch.Tensor] = None
+    chunk_tokens: int = 0
+
+    @property
+    def total_tokens(self) -> int:
+        return self.ends[-1] if self.ends else 0
+
+    def release(self) -> None:
+        objs, self.objs = self.objs, []
+        for o in objs:
+            o.ref_count_down()
+        self.keys, self.ends, self.ptrs = [], [], None
+
+
+class _SparseAppend:
+    """Transaction over a SparseRetrieveState: an extension may replace the
+    state's partial last chunk and append chunks.  ``commit`` releases the
+    replaced chunk; ``rollback`` (unless committed) releases what was
+    appended and puts the state back exactly as it was."""
+
+    def __init__(self, st: SparseRetrieveState):
+        self.st = st
+        self.snap = (list(st.keys), list(st.ends), list(st.objs), st.ptrs)
+        self.dropped: List[MemoryObj] = []
+        self.done = False
+
+    def drop_last(self) -> None:
+        st = self.st
+        st.keys.pop()
+        st.ends.pop()
+        self.dropped.append(st.objs.pop())
+
+    def commit(self) -> None:
+        self.done = True
+        for o in self.dropped:
+            o.ref_count_down()
+        self.dropped = []
+
+    def rollback(self) -> None:
+        if self.done:
+            return
+        st = self.st
+        keep = {id(o) for o in self.snap[2]}
+        for o in st.objs:
+            if id(o) not in keep:
+                o.ref_count_down()
+        st.keys[:], st.ends[:], st.objs[:] = self.snap[0], self.snap[1], self.snap[2]
+        st.ptrs = self.snap[3]
+
+
 class LMCacheEngine:
     def __init__(self, config: LMCacheEngineConfig, metadata: LMCacheEngineMetadata,
                  gpu_connector: GPUConnectorInterface,
@@ -521,13 +593,13 @@ class LMCacheEngine:
         for layer in range(L):
             lkeys = [k.split_layers(L)[layer] for _, _, k in chunks]
             size = sum(o.get_size() for o in per_layer[layer])
-            q.reserve(size)
+            q.admit(size)
             try:
                 futs = self.storage_manager.batched_put(lkeys, per_layer[layer])
             except BaseException as e:
-                q.fail(e)
+                q.record_failure(e)
                 raise
-            q.add(size, futs, req_id=req_id, keys=lkeys)
+            q.submit(size, futs, req_id=req_id, keys=lkeys)
             for o in per_layer[layer]:
                 o.ref_count_down()
         yield
@@ -536,21 +608,137 @@ class LMCacheEngine:
     def layerwise_put_queue(self):
         """Bound on layerwise puts in flight to asynchronous tiers."""
         if getattr(self, "_put_queue", None) is None:
-            from .layerwise_cpu_fill import LayerwisePutQueue
+            from .layerwise_cpu_fill import PutWindow
 
             c = self.config
-            self._put_queue = LayerwisePutQueue(c.layerwise_put_max_bytes,
-                                                c.layerwise_put_max_batches,
-                                                c.layerwise_put_timeout_secs)
+            self._put_queue = PutWindow(c.layerwise_put_max_bytes,
+                                        c.layerwise_put_max_batches,
+                                        c.layerwise_put_timeout_secs)
         return self._put_queue
 
     def wait_layerwise_puts(self, req_ids: Optional[List[str]] = None) -> None:
         """Fence the layerwise puts of ``req_ids`` (all puts when None)."""
         q = self.layerwise_put_queue
         if req_ids is None:
-            q.drain()
+            q.fence_all()
         else:
-            q.drain_requests(req_ids)
+            q.fence(req_ids)
+
+    # -------------------------------------------------- sparse retrieve
+    def _extend_sparse_state(self, st: SparseRetrieveState, txn: "_SparseAppend", tokens,
+                             mask, kwargs) -> None:
+        """Fetch the chunks of ``tokens`` past ``st.total_tokens`` (prefix
+        semantics: stop at the first miss) and rebuild the pointer table.  A
+        partial last chunk of a shorter context is fetched again whole."""
+        chunks = self._chunks(tokens, mask, kwargs.get("request_configs"),
+                              kwargs.get("hashes"), kwargs.get("offsets"))
+        if st.ends and chunks and chunks[-1][1] > st.total_tokens and \
+                st.total_tokens % self.config.chunk_size:
+            txn.drop_last()
+        new = [(s_, e, k) for s_, e, k in chunks if e > st.total_tokens]
+        if not new:
+            return
+        if new[0][0] != st.total_tokens:
+            raise ValueError("sparse state and token chunks disagree on chunk boundaries")
+        objs = self.storage_manager.batched_get([k for _, _, k in new])
+        got = 0
+        while got < len(objs) and objs[got] is not None:
+            got += 1
+        for o in objs[got:]:
+            if o is not None:
+                o.ref_count_down()
+        for (_, e, k), o in zip(new[:got], objs[:got]):
+            st.keys.append(k)
+            st.ends.append(e)
+            st.objs.append(o)
+        if st.objs:
+            st.chunk_tokens = st.chunk_tokens or self.config.chunk_size
+            dev = self.gpu_connector.layout.device
+            table = torch.tensor([o.data_ptr() for o in st.objs], dtype=torch.int64)
+            st.ptrs = table.to(dev) if dev.type == "cuda" else table
+
+    def _quarantine_sparse(self, st: SparseRetrieveState, why: str) -> None:
+        """A sparse copy's completion is unknown: keep its source chunks
+        referenced until the process restarts (they may still be read) and
+        stop serving."""
+        self.__dict__.setdefault("_quarantined", []).append(tuple(st.objs))
+        for o in st.objs:
+            o.ref_count_up()
+        self.mark_unhealthy(f"sparse load failed ({why}); its source chunks are retained")
+
+    def retrieve_layer_head_token_wise(self, tokens: torch.Tensor,
+                                       mask: Optional[torch.Tensor] = None, *,
+                                       sparse_state: SparseRetrieveState, **kwargs
+                                       ) -> Generator[Optional[torch.Tensor], Any, None]:
+        """Sparse (top-k) layerwise retrieve for long contexts whose KV stays
+        in the CPU tier (reference lmcache_ascend/v1/cache_engine.py:7457):
+
+            g = engine.retrieve_layer_head_token_wise(tokens, sparse_state=st)
+            cached = next(g)            # bool mask of tokens the state covers
+            for layer in range(L):
+                g.send(SparseLayerRequest(selected_idx, dst_slots))
+            done = next(g)              # bool mask of tokens loaded
+
+        The first step (or a longer context) fetches the missing chunks once
+        into ``st``; later steps only launch copies: each layer's selected
+        rows move straight from the pinned chunks into the paged slots (one
+        launch per layer, rows read through the device pointer table).  A
+        copy that fails quarantines the chunks and marks the engine
+        unhealthy, since the transfer may still be reading them."""
+        n = len(tokens)
+        ret = torch.zeros(n, dtype=torch.bool)
+        if not self.is_healthy():
+            yield ret
+            return
+        st = sparse_state
+        txn = _SparseAppend(st)
+        try:
+            self._extend_sparse_state(st, txn, tokens, mask, kwargs)
+            txn.commit()
+        finally:
+            txn.rollback()
+        ret[:st.total_tokens] = True
+        layout = self.gpu_connector.layout
+        loaded = torch.zeros(n, dtype=torch.bool)
+        req = yield ret
+        from ..ops import api
+
+        status = kwargs.get("status")
+        for layer in range(layout.num_layers):
+            if req is None:
+                break
+            if st.objs:
+                try:
+                    idx = req.selected_token_idx
+                    sm = req.slot_mapping
+                    if layout.device.type == "cuda":
+                        idx = idx.to(layout.device, sm.dtype)
+                        api._xfer(layout, None, sm.to(layout.device), False,
+                                  chunk_ptrs=st.ptrs, chunk_tokens=st.chunk_tokens,
+                                  chunk_on_device=st.objs[0].tensor.is_cuda,
+                                  layer_begin=layer, num_layers=1, chunk_layer_begin=layer,
+                                  chunk_idx=idx, chunk_idx_limit=st.total_tokens,
+                                  mode=api.MODE_SIMT if not st.objs[0].tensor.is_cuda
+                                  else api.MODE_AUTO, status=status)
+                    else:
+                        self._sparse_layer_ref(layout, st, layer, idx, sm)
+                    sel = req.selected_token_idx.long().cpu()
+                    loaded[sel[(sel >= 0) & (sel < st.total_tokens)]] = True
+                except BaseException as e:
+                    self._quarantine_sparse(st, repr(e))
+                    raise
+            req = yield None
+        self.stats.inc("sparse_retrieved_rows", int(loaded.sum()))
+        yield loaded
+
+    @staticmethod
+    def _sparse_layer_ref(layout, st: SparseRetrieveState, layer: int, idx, slots) -> None:
+        """CPU oracle of one sparse layer copy (host-resident caches)."""
+        full = torch.cat([o.tensor for o in st.objs], dim=2)
+        keep = (idx >= 0) & (idx < st.total_tokens)
+        rows = full.index_select(2, idx[keep].long())
+        layout.scatter_ref(rows, slots[keep], layer_begin=layer, num_layers=1,
+                           chunk_layer_begin=layer)
 
     def retrieve_layer(self, tokens: torch.Tensor, mask: Optional[torch.Tensor] = None,
                        **kwargs) -> Generator[Optional[torch.Tensor], None, None]:
@@ -631,7 +819,7 @@ class LMCacheEngine:
             self._worker.join(timeout=5)
         if getattr(self, "_put_queue", None) is not None:
             try:
-                self._put_queue.drain()  # fence puts before the allocator goes away
+                self._put_queue.fence_all()  # fence puts before the allocator goes away
             except BaseException as e:
                 logger.warning("layerwise puts failed before close: %s", e)
         self._closed = True

@@ -1,170 +1,197 @@
-"""Layerwise CPU fill: page leases and a bounded queue of asynchronous puts.
+"""Layerwise CPU fill: held CPU pages and a window of asynchronous puts.
 
-Behaviour of the reference (lmcache_ascend/v1/layerwise_cpu_fill.py:16-174):
+Contract (the reference's lmcache_ascend/v1/layerwise_cpu_fill.py:16-174
+defines the same two duties; the design below is this repo's own):
 
-* :class:`CPUFillLease` keeps CPU chunk pages alive (one reference each, the
-  same page counted once) while a reader outside the allocator's view, such
-  as a remote fill or a DMA engine, still reads them.  It proves ownership
-  only; the caller waits for the producer's copies separately.  Released once.
-* :class:`LayerwisePutQueue` bounds the puts that layerwise stores submit to
-  slower tiers, so the model thread is not fenced every forward: admission
-  waits only at a batch boundary when the byte or batch limit is reached (one
-  oversized batch is admitted into an empty queue), completed puts are reaped
-  out of order, failures are sticky (a later local hit does not prove the put
-  persisted), and fences can target the puts of given requests, including
-  puts of chunks a request reused from an earlier request.
+* :class:`PageHold` -- while something the allocator cannot see (a DMA
+  engine, a remote fill) still reads CPU chunk pages, those pages must not
+  be reused.  A hold takes one reference on every distinct page it is given
+  and gives all of them back exactly once.
+* :class:`PutWindow` -- layerwise stores hand each layer's chunks to the
+  slower tiers as asynchronous puts.  The window bounds what is in flight
+  (bytes and batches), so the model thread only waits when a bound is hit;
+  it learns of completions through future callbacks (no polling), keeps the
+  first failure (a put that failed leaves a later lookup hit unproven, so the
+  error stays raised), and fences by request, including requests that reuse
+  chunks whose puts are still running.
 """
 
 from __future__ import annotations
 
 import threading
 import time
-from collections import deque
-from concurrent.futures import Future, wait
-from typing import Any, Deque, Dict, Iterable, List, Optional, Sequence, Set, Tuple
+from concurrent.futures import Future
+from typing import Any, Dict, Iterable, List, Optional, Sequence, Set
 
 
-class CPUFillLease:
+class PageHold:
+    """One reference on each distinct CPU page in ``pages`` until
+    :meth:`release` (idempotent; also the context-manager exit)."""
+
     def __init__(self, pages: Sequence[Any]):
-        self._lock = threading.Lock()
-        self._pages: List[Any] = []
-        seen: Set[int] = set()
-        try:
-            for p in pages:
-                if id(p) in seen:
-                    continue
-                seen.add(id(p))
-                raw = getattr(p, "raw_data", None)
-                if not p.is_valid or raw is None or raw.device.type != "cpu":
-                    raise ValueError("a CPU fill lease needs valid CPU pages")
-                p.ref_count_up()
-                self._pages.append(p)
-        except BaseException:
-            self.release()
-            raise
+        distinct: Dict[int, Any] = {}
+        for p in pages:
+            distinct.setdefault(id(p), p)
+        for p in distinct.values():  # check everything before touching counts
+            raw = getattr(p, "raw_data", None)
+            if not getattr(p, "is_valid", False) or raw is None or raw.device.type != "cpu":
+                raise ValueError("a page hold needs valid CPU pages")
+        self._held = tuple(distinct.values())
+        for p in self._held:
+            p.ref_count_up()
+        self._gone = threading.Event()
 
     @property
     def num_pages(self) -> int:
-        return len(self._pages)
+        return 0 if self._gone.is_set() else len(self._held)
 
     def release(self) -> None:
-        with self._lock:
-            pages, self._pages = self._pages, []
-        for p in pages:
+        if self._gone.is_set():
+            return
+        self._gone.set()
+        held, self._held = self._held, ()
+        for p in held:
             p.ref_count_down()
 
-    def __enter__(self) -> "CPUFillLease":
+    def __enter__(self) -> "PageHold":
         return self
 
     def __exit__(self, *exc) -> None:
         self.release()
 
 
-class LayerwisePutQueue:
+class _Batch:
+    __slots__ = ("size", "left", "reqs", "keys")
+
+    def __init__(self, size: int, n: int):
+        self.size, self.left = size, n
+        self.reqs: Set[str] = set()
+        self.keys: List[Any] = []
+
+
+class PutWindow:
+    """Bounded set of in-flight put batches.
+
+    ``admit(size)`` blocks until a batch of ``size`` bytes fits (an empty
+    window always takes one batch, however large); ``submit`` registers the
+    batch's futures; ``fence(req_ids)`` / ``fence_all()`` wait for puts.  Every
+    wait is bounded by ``timeout`` seconds; running out is a failure too.
+    """
+
     def __init__(self, max_bytes: int, max_batches: int, timeout: float):
         if max_bytes <= 0 or max_batches <= 0 or timeout < 0:
-            raise ValueError("put queue limits must be positive and the timeout >= 0")
-        self.max_bytes = int(max_bytes)
-        self.max_batches = int(max_batches)
+            raise ValueError("put window limits must be positive and the timeout >= 0")
+        self.max_bytes, self.max_batches = int(max_bytes), int(max_batches)
         self.timeout = float(timeout)
-        self.pending: Deque[Tuple[int, Tuple[Future, ...]]] = deque()
-        self.pending_bytes = 0
-        self.error: Optional[BaseException] = None
-        self._by_req: Dict[str, Set[Future]] = {}
-        self._by_key: Dict[Any, Set[Future]] = {}
+        self._cv = threading.Condition()
+        self._live: Set[_Batch] = set()
+        self._bytes = 0
+        self._by_req: Dict[str, Set[_Batch]] = {}
+        self._by_key: Dict[Any, Set[_Batch]] = {}
+        self._error: Optional[BaseException] = None
 
-    def fail(self, error: BaseException) -> None:
-        """Latch a failure seen outside the futures (a synchronous submit)."""
-        if self.error is None:
-            self.error = error
+    # ---------------------------------------------------------- state
+    @property
+    def inflight_batches(self) -> int:
+        with self._cv:
+            return len(self._live)
 
-    def _raise(self) -> None:
-        if self.error is not None:
-            raise self.error
+    @property
+    def inflight_bytes(self) -> int:
+        with self._cv:
+            return self._bytes
 
-    def poll(self) -> None:
-        """Reap finished batches (in any order) without waiting."""
-        self._raise()
-        finished: Set[Future] = set()
-        keep: Deque[Tuple[int, Tuple[Future, ...]]] = deque()
-        keep_bytes = 0
-        try:
-            for size, futs in self.pending:
-                all_done = True
-                for f in futs:
-                    if f.done():
-                        f.result()  # raises the put's error
-                        finished.add(f)
-                    else:
-                        all_done = False
-                if not all_done:
-                    keep.append((size, futs))
-                    keep_bytes += size
-        except BaseException as e:
-            self.error = e
-            raise
-        self.pending, self.pending_bytes = keep, keep_bytes
-        if finished:
-            for table in (self._by_req, self._by_key):
-                for k in list(table):
-                    table[k] -= finished
-                    if not table[k]:
-                        del table[k]
+    @property
+    def error(self) -> Optional[BaseException]:
+        return self._error
 
-    def _wait_oldest(self, deadline: float) -> None:
-        _, left = wait(self.pending[0][1], timeout=max(0.0, deadline - time.monotonic()))
-        if left:
-            self.error = TimeoutError("layerwise puts did not complete in time")
-            raise self.error
-        self.poll()
+    def record_failure(self, err: BaseException) -> None:
+        """Latch a failure seen outside the futures (a submit that raised)."""
+        with self._cv:
+            if self._error is None:
+                self._error = err
+            self._cv.notify_all()
 
-    def reserve(self, size: int) -> None:
-        """Wait until a batch of ``size`` bytes may be submitted."""
-        self.poll()
+    def check(self) -> None:
+        if self._error is not None:
+            raise self._error
+
+    # ------------------------------------------------------ completion
+    def _retire(self, b: _Batch) -> None:  # under the lock
+        self._live.discard(b)
+        self._bytes -= b.size
+        for table, names in ((self._by_req, b.reqs), (self._by_key, b.keys)):
+            for n in names:
+                s = table.get(n)
+                if s is not None:
+                    s.discard(b)
+                    if not s:
+                        del table[n]
+
+    def _on_done(self, b: _Batch, fut: Future) -> None:
+        err = fut.exception() if not fut.cancelled() else RuntimeError("put cancelled")
+        with self._cv:
+            if err is not None and self._error is None:
+                self._error = err
+            b.left -= 1
+            if b.left == 0:
+                self._retire(b)
+            self._cv.notify_all()
+
+    # -------------------------------------------------------- waiting
+    def _wait(self, ready, what: str) -> None:
+        """Wait (bounded) until ``ready()`` holds; raises the latched error."""
         deadline = time.monotonic() + self.timeout
-        while self.pending and (len(self.pending) >= self.max_batches or
-                                self.pending_bytes + size > self.max_bytes):
-            self._wait_oldest(deadline)
+        with self._cv:
+            while True:
+                if self._error is not None:
+                    raise self._error
+                if ready():
+                    return
+                left = deadline - time.monotonic()
+                if left <= 0:
+                    self._error = TimeoutError(f"layerwise puts: {what} timed out")
+                    raise self._error
+                self._cv.wait(left)
 
-    def add(self, size: int, futures: Sequence[Future], *, req_id: str = "",
-            keys: Iterable[Any] = ()) -> None:
-        """Track a submitted batch (after :meth:`reserve`)."""
-        futs = tuple(f for f in futures if f is not None)
+    def admit(self, size: int) -> None:
+        self._wait(lambda: not self._live or (len(self._live) < self.max_batches and
+                                              self._bytes + size <= self.max_bytes),
+                   "admission")
+
+    def submit(self, size: int, futures: Sequence[Optional[Future]], *, req_id: str = "",
+               keys: Iterable[Any] = ()) -> None:
+        """Register a batch the caller just submitted (after :meth:`admit`)."""
+        futs = [f for f in futures if f is not None]
         if not futs:
             return
-        self.pending.append((int(size), futs))
-        self.pending_bytes += int(size)
-        if req_id:
-            self._by_req.setdefault(req_id, set()).update(futs)
-        for k in keys:
-            self._by_key.setdefault(k, set()).update(futs)
+        b = _Batch(int(size), len(futs))
+        with self._cv:
+            self._live.add(b)
+            self._bytes += b.size
+            if req_id:
+                b.reqs.add(req_id)
+                self._by_req.setdefault(req_id, set()).add(b)
+            for k in keys:
+                b.keys.append(k)
+                self._by_key.setdefault(k, set()).add(b)
+        for f in futs:  # may run the callback at once (already finished)
+            f.add_done_callback(lambda fut, b=b: self._on_done(b, fut))
 
-    def track_keys(self, req_id: str, keys: Iterable[Any]) -> None:
-        """A request reuses chunks whose puts may still run: fence them with it."""
-        if not req_id or not self._by_key:
+    def inherit(self, req_id: str, keys: Iterable[Any]) -> None:
+        """``req_id`` reuses chunks whose puts may still run: its fence
+        covers them too."""
+        if not req_id:
             return
-        for k in keys:
-            futs = self._by_key.get(k)
-            if futs:
-                self._by_req.setdefault(req_id, set()).update(futs)
+        with self._cv:
+            for k in keys:
+                for b in self._by_key.get(k, ()):
+                    b.reqs.add(req_id)
+                    self._by_req.setdefault(req_id, set()).add(b)
 
-    def drain_requests(self, req_ids: Iterable[str]) -> None:
-        """Wait for the puts of these requests only."""
-        self.poll()
-        futs: Set[Future] = set()
-        for r in req_ids:
-            futs |= self._by_req.get(r, set())
-        if futs:
-            _, left = wait(futs, timeout=self.timeout)
-            if left:
-                self.error = TimeoutError("layerwise puts did not complete in time")
-                raise self.error
-        self.poll()
+    def fence(self, req_ids: Iterable[str]) -> None:
+        ids = list(req_ids)
+        self._wait(lambda: not any(self._by_req.get(r) for r in ids), "request fence")
 
-    def drain(self) -> None:
-        """Wait for every pending put (before the allocator is torn down)."""
-        self.poll()
-        deadline = time.monotonic() + self.timeout
-        while self.pending:
-            self._wait_oldest(deadline)
-        self.poll()
+    def fence_all(self) -> None:
+        self._wait(lambda: not self._live, "drain")

@@ -1,8 +1,8 @@
-"""Layerwise CPU-fill lease and the bounded put queue (host-side, CPU)."""
+"""Layerwise CPU fill: page holds and the put window (host-side, CPU)."""
 
 import threading
 import time
-from concurrent.futures import Future, ThreadPoolExecutor
+from concurrent.futures import Future
 
 import pytest
 import torch
@@ -10,72 +10,98 @@ import torch
 from lmcache_ascend_b200.config import LMCacheEngineConfig, LMCacheEngineMetadata
 from lmcache_ascend_b200.v1.cache_engine import LMCacheEngine
 from lmcache_ascend_b200.v1.gpu_connector import VLLMPagedMemLayerwiseGPUConnector
-from lmcache_ascend_b200.v1.layerwise_cpu_fill import CPUFillLease, LayerwisePutQueue
+from lmcache_ascend_b200.v1.layerwise_cpu_fill import PageHold, PutWindow
 from lmcache_ascend_b200.v1.memory_management import TensorMemoryAllocator
 
 from .utils import make_separate_kv, random_slots
 
 
-def test_lease_holds_pages_once_and_releases_once():
+def test_page_hold_counts_each_page_once_and_checks_before_counting():
     alloc = TensorMemoryAllocator(torch.empty(1 << 16, dtype=torch.uint8))
     a = alloc.allocate([64], torch.float32)
     b = alloc.allocate([64], torch.float32)
-    lease = CPUFillLease([a, b, a])
-    assert lease.num_pages == 2 and a.get_ref_count() == 2
-    a.ref_count_down()
-    b.ref_count_down()  # the producers drop theirs; the lease keeps the pages
-    assert alloc.num_active == 2
-    lease.release()
-    lease.release()
+    with PageHold([a, b, a, b, a]) as hold:
+        assert hold.num_pages == 2 and a.get_ref_count() == 2 and b.get_ref_count() == 2
+        a.ref_count_down()
+        b.ref_count_down()  # the producers are done; only the hold keeps them
+        assert alloc.num_active == 2
+    assert alloc.num_active == 0 and hold.num_pages == 0
+    hold.release()  # a second release gives nothing back twice
     assert alloc.num_active == 0
-    c = alloc.allocate([64], torch.float32)
-    c.free()
+    good = alloc.allocate([64], torch.float32)
+    dead = alloc.allocate([64], torch.float32)
+    dead.free()
     with pytest.raises(ValueError):
-        CPUFillLease([c])
+        PageHold([good, dead])
+    assert good.get_ref_count() == 1  # nothing was taken before the check failed
+    good.ref_count_down()
 
 
-def _done(v=None):
+def _finished(value=None, error=None):
     f = Future()
-    f.set_result(v)
+    if error is not None:
+        f.set_exception(error)
+    else:
+        f.set_result(value)
     return f
 
 
-def test_put_queue_admission_reaping_and_sticky_errors():
-    q = LayerwisePutQueue(max_bytes=100, max_batches=2, timeout=0.5)
+def test_window_bounds_bytes_and_batches_with_callbacks():
+    w = PutWindow(max_bytes=100, max_batches=2, timeout=2.0)
     slow = Future()
-    q.reserve(60)
-    q.add(60, [slow], req_id="r1", keys=["k1"])
-    q.add(10, [_done()], req_id="r2", keys=["k2"])
-    q.poll()  # r2 finished out of order: reaped, r1 still charged
-    assert len(q.pending) == 1 and q.pending_bytes == 60
+    w.admit(60)
+    w.submit(60, [slow], req_id="r1", keys=["k1"])
+    w.admit(10)
+    w.submit(10, [_finished()], req_id="r2", keys=["k2"])  # done at once: retired
+    assert (w.inflight_batches, w.inflight_bytes) == (1, 60)
     threading.Timer(0.1, slow.set_result, args=(None,)).start()
     t0 = time.monotonic()
-    q.reserve(60)  # 60 + 60 > 100: waits for r1
-    assert time.monotonic() - t0 >= 0.05 and not q.pending
-    q.reserve(500)  # oversized batch admitted into an empty queue
-    bad = Future()
-    bad.set_exception(RuntimeError("disk full"))
-    q.add(5, [bad])
-    with pytest.raises(RuntimeError):
-        q.poll()
-    with pytest.raises(RuntimeError):  # sticky
-        q.reserve(1)
-
-
-def test_put_queue_request_fences_and_timeout():
-    q = LayerwisePutQueue(max_bytes=1 << 20, max_batches=8, timeout=0.2)
-    slow, other = Future(), Future()
-    q.add(1, [slow], req_id="a", keys=["k"])
-    q.add(1, [other], req_id="b", keys=["z"])
-    q.track_keys("c", ["k"])  # c reuses a's chunk: fenced together
-    threading.Timer(0.05, slow.set_result, args=(None,)).start()
-    q.drain_requests(["c"])  # does not wait for b
-    assert not other.done()
+    w.admit(60)  # 60 + 60 > 100: waits for the callback of r1's future
+    assert time.monotonic() - t0 >= 0.05 and w.inflight_batches == 0
+    w.admit(10_000)  # an empty window takes any one batch
+    w.submit(10_000, [Future(), Future()])
     with pytest.raises(TimeoutError):
-        q.drain()
+        _blocked_admit()
 
 
-def test_engine_store_layer_puts_go_through_the_queue(tmp_path):
+def _blocked_admit():
+    w = PutWindow(max_bytes=10, max_batches=1, timeout=0.05)
+    w.submit(5, [Future()])
+    w.admit(5)
+
+
+def test_window_errors_are_sticky():
+    w = PutWindow(max_bytes=1 << 20, max_batches=8, timeout=1.0)
+    w.submit(5, [_finished(error=OSError("disk full"))], req_id="r")
+    with pytest.raises(OSError):
+        w.check()
+    with pytest.raises(OSError):  # every later wait raises it too
+        w.admit(1)
+    with pytest.raises(OSError):
+        w.fence(["anything"])
+    w2 = PutWindow(1 << 20, 8, 0.05)
+    w2.submit(1, [Future()])
+    with pytest.raises(TimeoutError):
+        w2.fence_all()
+    with pytest.raises(TimeoutError):  # the timeout is latched as well
+        w2.check()
+
+
+def test_request_fences_and_reused_chunks():
+    w = PutWindow(max_bytes=1 << 20, max_batches=8, timeout=1.0)
+    a_put, b_put = Future(), Future()
+    w.submit(1, [a_put], req_id="a", keys=["chunk-a"])
+    w.submit(1, [b_put], req_id="b", keys=["chunk-b"])
+    w.inherit("c", ["chunk-a"])  # c reuses a's chunk
+    threading.Timer(0.05, a_put.set_result, args=(None,)).start()
+    w.fence(["c"])  # covers a's put, not b's
+    assert a_put.done() and not b_put.done()
+    b_put.set_result(None)
+    w.fence_all()
+    assert w.inflight_batches == 0
+
+
+def test_engine_store_layer_puts_go_through_the_window(tmp_path):
     L, NB, BS = 3, 32, 16
     kv = make_separate_kv(L, NB, BS, 2, 32, torch.float32, "cpu", seed=1)
     cfg = LMCacheEngineConfig.from_defaults(chunk_size=64, max_local_cpu_size=0.02,
@@ -89,6 +115,6 @@ def test_engine_store_layer_puts_go_through_the_queue(tmp_path):
                              req_id="r"):
         pass
     eng.wait_layerwise_puts(["r"])
-    assert not eng.layerwise_put_queue.pending
+    assert eng.layerwise_put_queue.inflight_batches == 0
     assert eng.lookup(tokens) == 128
     eng.close()

@@ -65,3 +65,41 @@ def test_fused_rope_vector_path_matches_scalar_path(neox, dtype, rot):
     ref = R.rope_delta_ref(old.cpu(), new.cpu(), k.cpu(), D, cache.cpu(), neox)
     tol = 1e-2 if dtype != torch.float32 else 1e-5
     assert torch.allclose(a.float().cpu(), ref, atol=tol * 4, rtol=tol)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_rope_on_paged_mla_rope_part_by_slot(dtype):
+    """CacheBlend on a paged MLA latent cache: only the 64 rope dims of each
+    576-element row rotate, rows addressed by slot (slot -1 skipped), the
+    512 latent dims and untouched slots stay bit-identical."""
+    NB, BS, T = 64, 64, 700
+    lat = torch.randn(NB, BS, 576, device="cuda").to(dtype)
+    before = lat.clone()
+    flat = lat.view(NB * BS, 576)
+    key = flat[:, 512:]  # [rows, 64], row stride 576
+    slots = torch.randperm(NB * BS, device="cuda")[:T]
+    slots[::9] = -1
+    cache = R.make_cos_sin_cache(16384, 64, base=10000.0).cuda()
+    old = torch.randint(0, 8192, (T,), device="cuda")
+    new = old + torch.randint(0, 8192, (T,), device="cuda")
+    ops.native().rotary_embedding_k_fused(old, new, key, 64, cache, True, slots)
+    torch.cuda.synchronize()
+    keep = slots >= 0
+    s = slots[keep]
+    ref = R.rope_delta_ref(old[keep].cpu(), new[keep].cpu(),
+                           before.view(NB * BS, 576)[s, 512:].cpu(), 64, cache.cpu(), True)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    got = lat.view(NB * BS, 576)
+    assert torch.allclose(got[s, 512:].float().cpu(), ref, atol=tol * 4, rtol=tol)
+    assert torch.equal(got[:, :512], before.view(NB * BS, 576)[:, :512])
+    untouched = torch.ones(NB * BS, dtype=torch.bool, device="cuda")
+    untouched[s] = False
+    assert torch.equal(got[untouched], before.view(NB * BS, 576)[untouched])
+    # the CPU oracle path of the op gives the same rows
+    cpu = before.view(NB * BS, 576).cpu().clone()
+    from lmcache_ascend_b200.ops import api
+
+    api.rotary_embedding_k_fused(old.cpu(), new.cpu(), cpu[:, 512:], 64, cache.cpu(), True,
+                                 slots.cpu())
+    assert torch.allclose(got.float().cpu(), cpu.float(), atol=tol * 4, rtol=tol)

@@ -163,3 +163,61 @@ def test_kv_consumer_loads_but_never_saves():
         LMCacheConnectorV1Impl("worker", cfg, "m", BS, kv_role="kv_sideways")
     worker.shutdown()
     worker.engine.close()
+
+
+def test_two_group_model_latent_and_indexer():
+    """A DSA-shaped model registers two KV cache groups (MLA latent layers
+    and indexer layers, different shapes and dtypes); each group gets its own
+    block table from vLLM, is stored by its own engine, and a prefix hit
+    loads both groups into the new request's blocks.  The scheduler's lookup
+    counts a prefix only as far as every group holds it."""
+    cfg = LMCacheEngineConfig.from_defaults(chunk_size=64, max_local_cpu_size=0.05)
+    worker = LMCacheConnectorV1Impl("worker", cfg, "dsa", BS, use_mla=True)
+    kv = {}
+    for i in range(2):
+        kv[f"model.layers.{i}.self_attn.attn"] = torch.zeros(NB, BS, 96)           # latent
+        kv[f"model.layers.{i}.self_attn.indexer.k_cache"] = torch.zeros(NB, BS, 32,
+                                                                        dtype=torch.bfloat16)
+    worker.register_kv_caches(kv)
+    assert len(worker._engines) == 2
+    sched = LMCacheConnectorV1Impl("scheduler", cfg, "dsa", BS, use_mla=True,
+                                   engine=worker.lookup_engine)
+    prompt = list(range(200))
+    lat_a, idx_a = list(range(0, 13)), list(range(60, 73))
+    g = torch.Generator().manual_seed(5)
+    t = torch.arange(200)
+    s_lat = torch.tensor(lat_a)[t // BS] * BS + t % BS
+    s_idx = torch.tensor(idx_a)[t // BS] * BS + t % BS
+    for name, x in kv.items():
+        s = s_idx if "indexer" in name else s_lat
+        x.view(NB * BS, -1)[s] = torch.randn(200, x.shape[-1], generator=g).to(x.dtype)
+    want = {n: x.view(NB * BS, -1)[s_idx if "indexer" in n else s_lat].clone()
+            for n, x in kv.items()}
+    req = SimpleNamespace(request_id="A", prompt_token_ids=prompt)
+    sched.get_num_new_matched_tokens(req, 0)
+    new = SimpleNamespace(req_id="A", prompt_token_ids=prompt, block_ids=(lat_a, idx_a),
+                          num_computed_tokens=0)
+    meta = sched.build_connector_meta(_sched_out([new], scheduled={"A": 200}))
+    assert len(meta.requests[0].group_slot_mappings) == 1
+    _step(worker, meta)
+    # request B: same prompt, new blocks in both groups
+    req_b = SimpleNamespace(request_id="B", prompt_token_ids=prompt)
+    need, _ = sched.get_num_new_matched_tokens(req_b, 0)
+    assert need == 199
+    sched.update_state_after_alloc(req_b, None, need)
+    lat_b, idx_b = list(range(20, 33)), list(range(80, 93))
+    new_b = SimpleNamespace(req_id="B", prompt_token_ids=prompt, block_ids=(lat_b, idx_b),
+                            num_computed_tokens=0)
+    meta = sched.build_connector_meta(_sched_out([new_b], scheduled={"B": 1}))
+    _step(worker, meta)
+    s_lat_b = torch.tensor(lat_b)[t // BS] * BS + t % BS
+    s_idx_b = torch.tensor(idx_b)[t // BS] * BS + t % BS
+    for n, x in kv.items():
+        got = x.view(NB * BS, -1)[s_idx_b if "indexer" in n else s_lat_b]
+        assert torch.equal(got, want[n]), n
+    # drop the indexer group's chunks: the grouped lookup no longer reports a hit
+    worker._engines[1].clear()
+    req_c = SimpleNamespace(request_id="C", prompt_token_ids=prompt)
+    assert sched.get_num_new_matched_tokens(req_c, 0) == (0, False)
+    worker.shutdown()
+    worker.engine.close()
