@@ -146,6 +146,11 @@ class ReqMeta:
 @dataclass
 class LMCacheConnectorMetadata:
     requests: List[ReqMeta] = field(default_factory=list)
+    # preemption checkpoints: KV of a preempted request to copy out before
+    # vLLM reuses its blocks ({"req_id", "generation", "token_ids",
+    # "slot_mapping"}), and generations to forget
+    preemption_captures: List[dict] = field(default_factory=list)
+    preemption_cancels: List[Tuple[str, int]] = field(default_factory=list)
 
     def add_request(self, r: ReqMeta) -> None:
         self.requests.append(r)
@@ -254,6 +259,12 @@ class LMCacheConnectorV1Impl:
         self._layer_load_gens: List = []
         self._layer_store_gens: List = []
         self._layer_idx = 0
+        # preemption checkpoints (scheduler side): live request objects,
+        # computed-token count and preemption generation per request
+        self._requests: Dict[str, Any] = {}
+        self._computed: Dict[str, int] = {}
+        self._generation: Dict[str, int] = {}
+        self._checkpointer = None                   # worker: PreemptionCheckpointer
         # direct paged push state
         self._direct_recv: Dict[str, dict] = {}     # scheduler: decoder requests awaiting blocks
         self._direct_senders: set = set()           # scheduler: prefiller requests that push
@@ -272,8 +283,18 @@ class LMCacheConnectorV1Impl:
         self._layer_group: Dict[str, int] = {}
 
     # ============================================================ scheduler
+    @staticmethod
+    def _all_tokens(request) -> List[int]:
+        """Prompt plus generated tokens (a resumed request's prefix)."""
+        allt = getattr(request, "all_token_ids", None)
+        return list(allt) if allt is not None else list(request.prompt_token_ids or [])
+
+    def on_new_request(self, request) -> None:
+        self._requests[request.request_id] = request
+
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int) -> Tuple[int, bool]:
-        tokens = list(request.prompt_token_ids or [])
+        self._requests.setdefault(request.request_id, request)
+        tokens = self._all_tokens(request)
         if not tokens:
             return 0, False
         pid = direct_push_id(request)
@@ -327,12 +348,38 @@ class LMCacheConnectorV1Impl:
         tr.num_pushed_tokens = done
         return r
 
+    def _capture_specs(self, scheduler_output, meta: LMCacheConnectorMetadata) -> None:
+        """Preempted requests: their blocks still hold the KV computed so far
+        (vLLM reuses them in this step's forward); the worker copies it out in
+        ``handle_preemptions`` and publishes it under the request's token
+        chain, so the resumed request finds it as a prefix hit."""
+        for req_id in getattr(scheduler_output, "preempted_req_ids", None) or ():
+            tr = self._trackers.get(req_id)
+            n = self._computed.get(req_id, 0)
+            req = self._requests.get(req_id)
+            if tr is None or n <= 0:
+                continue
+            tokens = self._all_tokens(req) if req is not None else tr.token_ids
+            n = min(n, len(tokens), len(tr.allocated_block_ids) * self.block_size)
+            gen = self._generation.get(req_id, 0) + 1
+            self._generation[req_id] = gen
+            meta.preemption_captures.append({
+                "req_id": req_id, "generation": gen,
+                "token_ids": torch.tensor(tokens[:n], dtype=torch.long),
+                "slot_mapping": slots_of(tr.allocated_block_ids, self.block_size, 0, n)})
+
     def build_connector_meta(self, scheduler_output) -> LMCacheConnectorMetadata:
         meta = LMCacheConnectorMetadata()
+        self._capture_specs(scheduler_output, meta)
         for req_id in getattr(scheduler_output, "finished_req_ids", ()) or ():
             self._trackers.pop(req_id, None)
             self._load_specs.pop(req_id, None)
             self._direct_recv.pop(req_id, None)
+            self._requests.pop(req_id, None)
+            self._computed.pop(req_id, None)
+            gen = self._generation.pop(req_id, None)
+            if gen is not None:
+                meta.preemption_cancels.append((req_id, gen))
         # decoder: requests whose blocks were just allocated for the push
         for req_id, rec in list(self._direct_recv.items()):
             if "blocks" not in rec:
@@ -361,6 +408,7 @@ class LMCacheConnectorV1Impl:
                 continue
             spec = self._load_specs.pop(new.req_id, None)
             done = new.num_computed_tokens + scheduler_output.num_scheduled_tokens[new.req_id]
+            self._computed[new.req_id] = done
             if spec is not None and spec.can_load:
                 tr.num_saved_tokens = (spec.lmcache_cached_tokens // self.chunk_size) * \
                     self.chunk_size  # already cached: do not store again
@@ -369,16 +417,36 @@ class LMCacheConnectorV1Impl:
             if r is not None:
                 meta.add_request(r)
         cached = scheduler_output.scheduled_cached_reqs
+        resumed = set(getattr(cached, "resumed_req_ids", None) or ())
         for i, req_id in enumerate(getattr(cached, "req_ids", []) or []):
             tr = self._trackers.get(req_id)
             if tr is None:
                 continue
             new_blocks = cached.new_block_ids[i]
+            done = cached.num_computed_tokens[i] + scheduler_output.num_scheduled_tokens[req_id]
+            self._computed[req_id] = done
+            if req_id in resumed:
+                # back from preemption: a fresh block table; load what the
+                # checkpoint (or any earlier store) holds of its prefix
+                req = self._requests.get(req_id)
+                tokens = self._all_tokens(req) if req is not None else tr.token_ids
+                tr.token_ids = list(tokens)
+                tr.allocated_block_ids = list(new_blocks[0]) if new_blocks else []
+                tr.group_block_ids = [list(b) for b in new_blocks[1:]] if new_blocks else []
+                spec = self._load_specs.pop(req_id, None)
+                if spec is not None and spec.can_load:
+                    tr.num_saved_tokens = max(tr.num_saved_tokens,
+                                              (spec.lmcache_cached_tokens // self.chunk_size)
+                                              * self.chunk_size)
+                    r = ReqMeta.build(tr, self.block_size, self.chunk_size, spec, done,
+                                      self.config.save_unfull_chunk, skip_save=True)
+                    if r is not None:
+                        meta.add_request(r)
+                continue
             tr.update(cached.new_token_ids[i] if cached.new_token_ids else [],
                       list(new_blocks[0]) if new_blocks else None,
                       [list(b) for b in new_blocks[1:]] if new_blocks and len(new_blocks) > 1
                       else None)
-            done = cached.num_computed_tokens[i] + scheduler_output.num_scheduled_tokens[req_id]
             if tr.disagg_spec is not None:  # chunked prefill of a direct push
                 r = self._direct_send_meta(tr, done)
                 if r is not None:
@@ -397,6 +465,7 @@ class LMCacheConnectorV1Impl:
 
     def request_finished(self, request, block_ids) -> Tuple[bool, Optional[dict]]:
         self._trackers.pop(request.request_id, None)
+        self._requests.pop(request.request_id, None)
         self._direct_recv.pop(request.request_id, None)
         if self._lookup is not None:
             self._lookup.unpin(request.request_id)
@@ -479,6 +548,41 @@ class LMCacheConnectorV1Impl:
     def bind_connector_metadata(self, meta: LMCacheConnectorMetadata) -> None:
         self._meta = meta
 
+    @property
+    def checkpointer(self):
+        if self._checkpointer is None:
+            from ...v1.preemption_checkpoint import PreemptionCheckpointer
+
+            self._checkpointer = PreemptionCheckpointer(self._ensure_engine())
+        return self._checkpointer
+
+    def handle_preemptions(self, meta: Optional[LMCacheConnectorMetadata] = None) -> None:
+        """Before vLLM reuses a preempted request's blocks: copy its computed
+        KV out (every TP rank its own shard) and publish it under the
+        request's token chain; forget generations of finished requests
+        (reference vllm_v1_adapter.py:1546-1614).  Stores still in flight for
+        those requests are drained first, since they read the same blocks."""
+        meta = meta if meta is not None else self._meta
+        if meta is None or self.kv_role == "kv_consumer":
+            return
+        ck = self.checkpointer
+        for req_id, gen in meta.preemption_cancels:
+            ck.cancel(req_id, gen)
+        if not meta.preemption_captures:
+            return
+        eng = self._ensure_engine()
+        if self.config.store_async:
+            eng.wait_for_pending_stores(timeout=self.config.blocking_timeout_secs)
+        for cap in meta.preemption_captures:
+            try:
+                n = ck.capture(cap["req_id"], cap["generation"], cap["token_ids"].tolist(),
+                               cap["slot_mapping"])
+                if n:
+                    ck.seal(cap["req_id"], cap["generation"], cap["token_ids"].tolist())
+            except Exception as e:  # the request recomputes instead
+                logger.warning("preemption checkpoint of %s failed: %s", cap["req_id"], e)
+                ck.cancel(cap["req_id"], cap["generation"])
+
     def clear_connector_metadata(self) -> None:
         self._meta = None
 
@@ -512,6 +616,14 @@ class LMCacheConnectorV1Impl:
             skip = (spec.vllm_cached_tokens // self.chunk_size) * self.chunk_size
             toks = r.token_ids[:n]
             mask = self._mask(n, skip)
+            if not eng.agree_restorable(toks):
+                # some TP rank cannot load this prefix: no rank loads it, and
+                # vLLM recomputes the tokens of these blocks
+                logger.warning("req %s: TP ranks disagree on a %d-token hit; recomputing",
+                               r.req_id, n)
+                self.load_error_block_ids.update(
+                    (r.slot_mapping[skip:n] // self.block_size).unique().tolist())
+                continue
             for gi, geng in enumerate(self._engines):
                 slots = r.slots_of_group(gi)[:n]
                 if self.config.use_layerwise:

@@ -68,6 +68,12 @@ class LMCacheB200ConnectorV1(KVConnectorBase_V1):
         super().clear_connector_metadata()
         self._impl.clear_connector_metadata()
 
+    def handle_preemptions(self, kv_connector_metadata: KVConnectorMetadata):
+        self._impl.handle_preemptions(kv_connector_metadata)
+
+    def on_new_request(self, request):
+        self._impl.on_new_request(request)
+
     def start_load_kv(self, forward_context, **kwargs: Any) -> None:
         self._impl.start_load_kv(forward_context, **kwargs)
 
@@ -98,6 +104,8 @@ class LMCacheB200ConnectorV1(KVConnectorBase_V1):
         m = self._impl.build_connector_meta(scheduler_output)
         out = LMCacheB200ConnectorMetadata()
         out.requests = m.requests
+        out.preemption_captures = m.preemption_captures
+        out.preemption_cancels = m.preemption_cancels
         return out
 
     def request_finished(self, request, block_ids: list[int]):

@@ -548,6 +548,15 @@ class LMCacheEngine:
             return key.layer_key(L - 1)
         return key
 
+    def agree_restorable(self, tokens: torch.Tensor) -> bool:
+        """Every TP rank holds all chunks of ``tokens`` (restore agreement,
+        reference cache_engine.py:9685-9742).  Each rank checks its own tiers;
+        with ``collective_all_true_fn`` (a TP-group all-reduce every rank runs
+        in the same step) the answer is the same on every rank."""
+        local = self.lookup(tokens) >= len(tokens)
+        fn = self.collective_all_true_fn
+        return bool(fn(local)) if fn is not None else local
+
     def lookup_unpin(self, lookup_id: Any) -> None:
         with self._engine_state_lock:
             for k in self._lookup_pins.pop(lookup_id, []):

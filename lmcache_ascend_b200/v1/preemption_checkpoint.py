@@ -15,8 +15,9 @@ docs/preemption_checkpoint.md):
   a resumed request finds them through the ordinary lookup / retrieve path
   (which also covers tokens stored earlier, e.g. the prompt).  Published
   chunks are ordinary CPU-tier entries: evictable, and written back to slower
-  tiers by the storage manager (bounded by the layerwise put queue when the
-  engine runs layerwise).
+  tiers by the storage manager; the write-back of a seal goes through the
+  engine's put window (bounded bytes and batches in flight, sticky errors,
+  fenced per request as ``ckpt:<req_id>``).
 * ``cancel`` drops a generation's private fragments; a newer generation of
   the same request supersedes older ones (stale seals are ignored).
 * ``available`` reports how many leading tokens of a request can be restored;
@@ -125,11 +126,19 @@ class PreemptionCheckpointer:
         keys_by_end = {e: k for _, e, k in eng._chunks(acc[:agree])}
         stored, covered = 0, cap.start
         sm = eng.storage_manager
+        window = eng.layerwise_put_queue  # bounds the write-back to slower tiers
         for s, e, obj in cap.chunks:
             k = keys_by_end.get(e)
             full = (e - s) == cs or eng.config.save_unfull_chunk
             if e <= agree and k is not None and full and s == covered:
-                sm.batched_put([k], [obj])
+                size = obj.get_size()
+                window.admit(size)
+                try:
+                    futs = sm.batched_put([k], [obj])
+                except BaseException as err:
+                    window.record_failure(err)
+                    raise
+                window.submit(size, futs, req_id=f"ckpt:{req_id}", keys=[k])
                 stored += 1
                 covered = e
             obj.ref_count_down()  # the tier holds its own reference
