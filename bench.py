@@ -89,7 +89,7 @@ def parse():
     ap.add_argument("--head-dim", type=int, default=128)
     ap.add_argument("--block-size", type=int, default=128)
     ap.add_argument("--grid", type=int, default=0)
-    ap.add_argument("--tile", type=int, default=128)
+    ap.add_argument("--tile", type=int, default=512)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ttft", action="store_true",
                     help="skip the TTFT-on-prefix-hit measurement (Qwen3-32B, 16k hit)")

@@ -89,8 +89,9 @@ def main() -> None:
         dst = dst_layout_on(i, k)
         mode = 1 if kind == "push_bulk" else 2
         src = layouts[i].native()
-        return lambda: mod.pd_push(src, dst, slots[i], slots[k], 0, L, 1, [], 128, 0, None,
-                                   mode)
+        cnt = torch.zeros(1 << 16, dtype=torch.int32, device=torch.device("cuda", i))
+        return lambda: mod.pd_push(src, dst, slots[i], slots[k], 0, L, 1, [], 512, 0, None,
+                                   mode, cnt)
 
     def run(kind, pairs):
         ops_ = [(i, make_op(kind, i, k)) for i, k in pairs]

@@ -966,4 +966,55 @@ void cachegen_dequantize(const at::Tensor &sym, const at::Tensor &scale, const a
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------------------
+// Stream compaction for the serialised payload: the encoder writes each
+// stream into a fixed-capacity slot; this packs them back to back on the
+// device (warp per stream), so a chunk's payload leaves the GPU in one copy
+// instead of a masked select plus one transfer per bin group.
+//   dst[off[s] .. off[s] + len[s]) = src_base[slot_of(s)][0 .. len[s])
+// where stream s of group g (streams [first[g], first[g + 1])) lives at
+// src[g] + (s - first[g]) * cap[g].
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) cg_compact_kernel(
+    const int64_t *__restrict__ src, const int64_t *__restrict__ cap,
+    const int64_t *__restrict__ first, int groups, const int32_t *__restrict__ len,
+    const int64_t *__restrict__ off, uint8_t *__restrict__ dst, int64_t n) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t s = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; s < n;
+       s += nw) {
+    int g = 0;
+    while (g + 1 < groups && s >= first[g + 1]) ++g;
+    const uint8_t *a = reinterpret_cast<const uint8_t *>(src[g]) + (s - first[g]) * cap[g];
+    uint8_t *d = dst + off[s];
+    const int m = len[s];
+    for (int i = lane; i < m; i += 32) d[i] = a[i];
+  }
+}
+
+void cachegen_compact(const at::Tensor &src, const at::Tensor &cap, const at::Tensor &first,
+                      const at::Tensor &lengths, const at::Tensor &offsets, at::Tensor &dst) {
+  TORCH_CHECK(src.is_cuda() && cap.is_cuda() && first.is_cuda() && lengths.is_cuda() &&
+                  offsets.is_cuda() && dst.is_cuda(),
+              "compact: device tensors");
+  TORCH_CHECK(src.scalar_type() == at::kLong && cap.scalar_type() == at::kLong &&
+                  first.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong &&
+                  lengths.scalar_type() == at::kInt && dst.scalar_type() == at::kByte,
+              "compact: int64 tables, int32 lengths, uint8 destination");
+  TORCH_CHECK(src.numel() == cap.numel() && first.numel() == src.numel() &&
+                  lengths.numel() == offsets.numel() && lengths.is_contiguous() &&
+                  offsets.is_contiguous() && dst.is_contiguous(),
+              "compact: table sizes");
+  const int64_t n = lengths.numel();
+  if (n == 0) return;
+  const c10::cuda::CUDAGuard guard(dst.device());
+  const int64_t blocks = std::min<int64_t>((n * 32 + 255) / 256, 148 * 16);
+  cg_compact_kernel<<<static_cast<int>(blocks), 256, 0,
+                      at::cuda::getCurrentCUDAStream().stream()>>>(
+      src.data_ptr<int64_t>(), cap.data_ptr<int64_t>(), first.data_ptr<int64_t>(),
+      static_cast<int>(src.numel()), lengths.data_ptr<int32_t>(), offsets.data_ptr<int64_t>(),
+      dst.data_ptr<uint8_t>(), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace lmc

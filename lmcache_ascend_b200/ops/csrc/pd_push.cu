@@ -173,31 +173,35 @@ __global__ void __launch_bounds__(kPushWarps * 32)
 // ---------------------------------------------------------------------------
 // Bulk (TMA) push: the default engine for 16-byte aligned, contiguous rows.
 //
-// Each warp of a CTA is an independent pipeline over the units it owns
-// (unit = (layer, plane, tile of `tile_tokens` tokens), the same units and
-// flag counts as pd_push_kernel).  A unit is cut into pieces of at most 64
-// tokens that fit one shared-memory stage; for each piece the warp's lanes
-// plan runs of tokens contiguous on both sides (plan_runs), load them from
-// this GPU's paged cache with `cp.async.bulk.shared::cta.global` (mbarrier
-// completion; never multicast), and write them to the destination's paged
-// blocks -- local or peer memory -- with `cp.async.bulk.global.shared::cta`,
-// one bulk group per piece.
+// Work: every unit (layer, plane, tile of `tile_tokens` tokens; the units and
+// flag counts of pd_push_kernel) is cut into pieces of at most 64 tokens that
+// fit one shared-memory stage, with the same number of pieces for every tile
+// of a plane (the last tile's surplus pieces are empty).  The pieces of the
+// launch are numbered layer-major and each warp takes one contiguous range
+// of them, so every warp moves the same amount whatever the tile size, and
+// consecutive pieces of a warp are neighbours in memory.
 //
-// Two waits, decoupled:
-//  * stage reuse: before loading piece k + S - 1 into the stage piece k - 1
-//    used, `cp.async.bulk.wait_group.read 1` (piece k - 1's stores have read
-//    their shared memory; their writes may still be in flight);
-//  * flags: a unit is published once its writes have completed.  A finished
-//    unit waits in a small queue; when its last piece is kLag pieces old,
-//    `cp.async.bulk.wait_group kLag` (writes of every piece <= k - kLag done,
-//    which by then costs nothing) is followed by a proxy fence, a system
-//    fence and red.release.sys.add on the decoder's layer flag.
+// Per piece the warp's lanes plan runs of tokens contiguous on both sides
+// (plan_runs), load them from this GPU's paged cache with
+// `cp.async.bulk.shared::cta.global` (mbarrier completion; never multicast)
+// and write them to the destination's paged blocks -- local or peer memory
+// -- with `cp.async.bulk.global.shared::cta`, one bulk group per piece.
+// Stage reuse waits for `cp.async.bulk.wait_group.read 1` only.
+//
+// Flags: a unit may be shared by two warps.  When a warp is done with its
+// part of a unit and those writes have completed (`cp.async.bulk.wait_group
+// kLag`, kLag pieces later, which by then costs nothing), lane 0 adds its
+// piece count to the unit's counter in this GPU's memory (acq_rel, GPU
+// scope); the warp that brings the count to the unit's piece total resets
+// the counter for the next launch and publishes the unit: system fence, then
+// red.release.sys.add on the decoder's layer flag.  The counters therefore
+// start and end every launch at zero.
 // ---------------------------------------------------------------------------
 constexpr int kBulkWarps = 2;
 constexpr int kBulkStages = 2;
 constexpr int kBulkStageBytes = 8192;
-constexpr int kBulkLag = 4;       // pieces between a unit's end and its release
-constexpr int kBulkPending = 4;   // units that may wait for their release
+constexpr int kBulkLag = 4;       // pieces between the end of a unit part and its release
+constexpr int kBulkPending = 4;   // unit parts that may wait for their release
 constexpr int kTmaRingOffset = 128;  // mbarriers (warps * stages * 8 bytes) come first
 static_assert(kBulkWarps * kBulkStages * 8 <= kTmaRingOffset, "mbarrier area too small");
 
@@ -218,6 +222,7 @@ struct BulkPushJob {
   unsigned long long budget_ns;    // bound on each mbarrier wait
   uint32_t bulk_planes;            // bit p: plane p moves by TMA bulk copies, else by
                                    // per-lane loads/stores (rows not 16-byte aligned)
+  unsigned *counters;              // [units of this launch], zero between launches
 };
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -227,6 +232,15 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 template <int N>
 __device__ __forceinline__ void bulk_wait_complete() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
 }
 
 // One row of `rb` bytes with the widest granule both addresses allow.
@@ -247,10 +261,14 @@ __device__ __forceinline__ void copy_row_granules(char *dst, const char *src, in
   }
 }
 
-// Position of a warp in its own sequence of pieces.
-struct PieceCursor {
-  int i;      // i-th unit of this warp: unit index = gw + i * nw
-  int piece;  // piece within the unit
+// A piece, decoded from its index in the launch.
+struct PieceAt {
+  int unit;    // unit index in the launch: (layer * planes + plane) * tiles + tile
+  int layer;   // layer index in the launch
+  int plane;
+  int ppu;     // pieces of this unit
+  bool last;   // last piece of its unit
+  Unit u;      // tokens of the piece (u.n <= 0: an empty trailing piece)
 };
 
 __global__ void __launch_bounds__(kBulkWarps * 32)
@@ -265,175 +283,193 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
   const CopyJob &c = j.c;
   const int np = c.paged.num_planes;
   const int tiles = (c.num_tokens + j.tile_tokens - 1) / j.tile_tokens;
-  const int units_per_layer = np * tiles;
-  const int total = units_per_layer * c.num_layers;
   const int gw = blockIdx.x * kBulkWarps + warp;
   const int nw = gridDim.x * kBulkWarps;
-  if (gw >= total) return;
-  // tokens per piece of plane p: as many rows as fit one stage, at most 64
+  // pieces per unit and tokens per piece of each plane (0 pieces: not bulk)
   auto piece_tokens = [&](int p) {
     const int t = j.stage_bytes / plane_of(c.paged, p).row_bytes;
     return t > 64 ? 64 : (t < 1 ? 1 : t);
   };
+  auto ppu_of = [&](int p) {
+    if (p >= np || !((j.bulk_planes >> p) & 1u)) return 0;
+    return (j.tile_tokens + piece_tokens(p) - 1) / piece_tokens(p);
+  };
+  const int ppu0 = ppu_of(0), ppu1 = ppu_of(1), ppu2 = ppu_of(2);
+  const long long per_layer = static_cast<long long>(tiles) * (ppu0 + ppu1 + ppu2);
+  const long long total = per_layer * c.num_layers;
+  const long long base = total / nw, extra = total % nw;
+  const long long first = gw * base + min(static_cast<long long>(gw), extra);
+  const long long count = base + (gw < extra ? 1 : 0);
+
+  auto piece_at = [&](long long q) {
+    PieceAt r;
+    const int li = static_cast<int>(q / per_layer);
+    long long rem = q - li * per_layer;
+    int p = 0, ppu = ppu0;
+    if (rem >= static_cast<long long>(tiles) * ppu0) {
+      rem -= static_cast<long long>(tiles) * ppu0;
+      p = 1;
+      ppu = ppu1;
+      if (rem >= static_cast<long long>(tiles) * ppu1) {
+        rem -= static_cast<long long>(tiles) * ppu1;
+        p = 2;
+        ppu = ppu2;
+      }
+    }
+    const int tile = static_cast<int>(rem / ppu);
+    const int pc = static_cast<int>(rem - static_cast<long long>(tile) * ppu);
+    const int per = piece_tokens(p);
+    const int tend = min(c.num_tokens, (tile + 1) * j.tile_tokens);
+    r.unit = (li * np + p) * tiles + tile;
+    r.layer = li;
+    r.plane = p;
+    r.ppu = ppu;
+    r.last = pc == ppu - 1;
+    r.u.layer = li;
+    r.u.plane = p;
+    r.u.t0 = tile * j.tile_tokens + pc * per;
+    r.u.n = min(per, tend - r.u.t0);
+    return r;
+  };
+
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
   __syncwarp();
 
-  auto plane_of_unit = [&](int i) {
-    const int u = gw + i * nw;
-    return (u - (u / units_per_layer) * units_per_layer) / tiles;
-  };
-  auto is_bulk = [&](int i) { return (j.bulk_planes >> plane_of_unit(i)) & 1u; };
-  // the bulk pipeline visits only units of bulk planes
-  auto skip_small = [&](int i) {
-    while (gw + i * nw < total && !is_bulk(i)) ++i;
-    return i;
-  };
-  auto valid = [&](const PieceCursor &q) { return gw + q.i * nw < total; };
-  // piece -> (layer index in launch, plane, tokens); `last`: ends its unit
-  auto piece_unit = [&](const PieceCursor &q, bool &last) {
-    const int u = gw + q.i * nw;
-    const int li = u / units_per_layer;
-    const int rem = u - li * units_per_layer;
-    const int p = rem / tiles;
-    const int t0 = (rem - p * tiles) * j.tile_tokens;
-    const int n = min(c.num_tokens - t0, j.tile_tokens);
-    const int per = piece_tokens(p);
-    Unit r;
-    r.layer = li;
-    r.plane = p;
-    r.t0 = t0 + q.piece * per;
-    r.n = min(per, t0 + n - r.t0);
-    last = r.t0 + r.n >= t0 + n;
-    return r;
-  };
-  auto advance = [&](PieceCursor &q, bool last) {
-    if (last) {
-      q.i = skip_small(q.i + 1);
-      q.piece = 0;
-    } else {
-      ++q.piece;
+  auto issue_loads = [&](long long k) {
+    const PieceAt pa = piece_at(first + k);
+    const int s = static_cast<int>(k % S);
+    unsigned bytes = 0;
+    LaneRuns r;
+    r.len[0] = r.len[1] = 0;
+    if (pa.u.n > 0) {
+      r = plan_runs(c, pa.u, lane, c.num_tokens);
+      bytes = warp_sum_u32((r.len[0] + r.len[1]) * plane_of(c.paged, pa.plane).row_bytes);
     }
-  };
-
-  auto issue_loads = [&](const PieceCursor &q, int k) {
-    bool last;
-    const Unit u = piece_unit(q, last);
-    const int s = k % S;
-    const LaneRuns r = plan_runs(c, u, lane, c.num_tokens);
-    const unsigned rb = plane_of(c.paged, u.plane).row_bytes;
-    const unsigned bytes = warp_sum_u32((r.len[0] + r.len[1]) * rb);
     if (lane == 0) mbar_arrive_expect_tx(&bars[s], bytes);
     __syncwarp();
+    const unsigned rb = plane_of(c.paged, pa.plane).row_bytes;
     unsigned char *buf = ring + static_cast<size_t>(s) * j.stage_bytes;
 #pragma unroll
     for (int h = 0; h < 2; ++h)
       if (r.len[h]) bulk_g2s(buf + (h * 32 + lane) * rb, r.src[h], r.len[h] * rb, &bars[s]);
   };
 
-  // Finished units waiting for their release, oldest first: (absolute layer,
-  // index of the unit's last piece); -1 = empty.  Constant indices only, so
-  // the queue lives in registers.
-  int ql[kBulkPending], qk[kBulkPending];
+  // Unit parts waiting for their writes, oldest first: unit (-1: empty slot),
+  // pieces done by this warp, layer, index of the part's last piece.
+  // Constant indices only, so the queue lives in registers.
+  int qu[kBulkPending], qc[kBulkPending], ql[kBulkPending];
+  long long qk[kBulkPending];
 #pragma unroll
-  for (int i = 0; i < kBulkPending; ++i) ql[i] = -1, qk[i] = 0;
-  auto publish_front = [&]() {
+  for (int i = 0; i < kBulkPending; ++i) qu[i] = -1, qc[i] = 0, ql[i] = 0, qk[i] = 0;
+  auto settle_front = [&](int ppu_front) {
     if (lane == 0) {
-      fence_acq_rel_sys();
-      for (int r = 0; r < j.replicas; ++r)
-        if (j.flags[r]) red_release_sys_add(j.flags[r] + ql[0], 1u);
+      const unsigned before = atom_add_acq_rel_gpu(j.counters + qu[0],
+                                                   static_cast<unsigned>(qc[0]));
+      if (before + static_cast<unsigned>(qc[0]) == static_cast<unsigned>(ppu_front)) {
+        j.counters[qu[0]] = 0u;  // ready for the next launch
+        fence_acq_rel_sys();
+        const int layer = c.layer_begin + ql[0];
+        for (int r = 0; r < j.replicas; ++r)
+          if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
+      }
     }
 #pragma unroll
-    for (int i = 0; i + 1 < kBulkPending; ++i) ql[i] = ql[i + 1], qk[i] = qk[i + 1];
-    ql[kBulkPending - 1] = -1;
+    for (int i = 0; i + 1 < kBulkPending; ++i)
+      qu[i] = qu[i + 1], qc[i] = qc[i + 1], ql[i] = ql[i + 1], qk[i] = qk[i + 1];
+    qu[kBulkPending - 1] = -1;
   };
-  // Publish every queued unit whose writes are known complete (last piece
-  // <= kdone); the caller waited for those bulk groups.
-  auto release_upto = [&](int kdone) {
-    if (ql[0] < 0 || qk[0] > kdone) return;
-    // each lane's completed bulk writes (async proxy) before the generic
-    // release lane 0 issues
-    fence_proxy_async_global();
+  auto ppu_unit = [&](int unit) {
+    const int p = (unit / tiles) % np;
+    return p == 0 ? ppu0 : (p == 1 ? ppu1 : ppu2);
+  };
+  // settle every queued part whose last piece is <= kdone (its writes are done)
+  auto settle_upto = [&](long long kdone) {
+    if (qu[0] < 0 || qk[0] > kdone) return;
+    fence_proxy_async_global();  // completed bulk writes before the generic atomics
     __syncwarp();
 #pragma unroll
     for (int i = 0; i < kBulkPending; ++i)
-      if (ql[0] >= 0 && qk[0] <= kdone) publish_front();
+      if (qu[0] >= 0 && qk[0] <= kdone) settle_front(ppu_unit(qu[0]));
   };
-  auto enqueue = [&](int layer, int k) {
-    if (ql[kBulkPending - 1] >= 0) {  // full: drain every outstanding write
+  auto enqueue = [&](int unit, int cnt, int layer, long long k) {
+    if (qu[kBulkPending - 1] >= 0) {  // full: drain every outstanding write
       bulk_wait_complete<0>();
-      release_upto(0x7fffffff);
+      settle_upto(0x7fffffffffffffffll);
     }
     bool placed = false;
 #pragma unroll
     for (int i = 0; i < kBulkPending; ++i)
-      if (!placed && ql[i] < 0) ql[i] = layer, qk[i] = k, placed = true;
+      if (!placed && qu[i] < 0) qu[i] = unit, qc[i] = cnt, ql[i] = layer, qk[i] = k,
+                                placed = true;
   };
 
-  PieceCursor lc{skip_small(0), 0}, sc{skip_small(0), 0};
-  int kl = 0;
-  for (; kl < S - 1 && valid(lc); ++kl) {
-    bool last;
-    piece_unit(lc, last);
-    issue_loads(lc, kl);
-    advance(lc, last);
-  }
-  for (int k = 0; valid(sc); ++k) {
-    const int s = k % S;
-    const unsigned parity = (k / S) & 1;
+  long long kl = 0;
+  for (; kl < S - 1 && kl < count; ++kl) issue_loads(kl);
+  int cur_unit = -1, cur_cnt = 0, cur_layer = 0;
+  for (long long k = 0; k < count; ++k) {
+    const int s = static_cast<int>(k % S);
+    const unsigned parity = static_cast<unsigned>((k / S) & 1);
     if (!mbar_wait_bounded(&bars[s], parity, j.budget_ns)) {
-      if (lane == 0) report_status(c.status, kStatusMbarTimeout, gw, k, 0);
+      if (lane == 0) report_status(c.status, kStatusMbarTimeout, gw, static_cast<long long>(k),
+                                   0);
       break;
     }
-    bool last;
-    const Unit u = piece_unit(sc, last);
-    const LaneRuns r = plan_runs(c, u, lane, c.num_tokens);
-    const unsigned rb = plane_of(c.paged, u.plane).row_bytes;
-    const unsigned char *buf = ring + static_cast<size_t>(s) * j.stage_bytes;
-    const int layer = c.layer_begin + u.layer;
-    const int64_t slot0 = static_cast<int64_t>(layer) * np + u.plane;
-    const char *base0 = reinterpret_cast<const char *>(j.dst_ptrs[slot0]);
-    for (int rep = 0; rep < j.replicas; ++rep) {
-      const char *base = reinterpret_cast<const char *>(
-          j.dst_ptrs[static_cast<int64_t>(rep) * j.dst_layers * np + slot0]);
+    const PieceAt pa = piece_at(first + k);
+    if (pa.u.n > 0) {
+      const LaneRuns r = plan_runs(c, pa.u, lane, c.num_tokens);
+      const unsigned rb = plane_of(c.paged, pa.plane).row_bytes;
+      const unsigned char *buf = ring + static_cast<size_t>(s) * j.stage_bytes;
+      const int layer = c.layer_begin + pa.layer;
+      const int64_t slot0 = static_cast<int64_t>(layer) * np + pa.plane;
+      const char *base0 = reinterpret_cast<const char *>(j.dst_ptrs[slot0]);
+      for (int rep = 0; rep < j.replicas; ++rep) {
+        const char *dbase = reinterpret_cast<const char *>(
+            j.dst_ptrs[static_cast<int64_t>(rep) * j.dst_layers * np + slot0]);
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
-        if (r.len[h])
-          bulk_s2g(const_cast<char *>(base) + (r.dst[h] - base0),
-                   buf + (h * 32 + lane) * rb, r.len[h] * rb);
+        for (int h = 0; h < 2; ++h)
+          if (r.len[h])
+            bulk_s2g(const_cast<char *>(dbase) + (r.dst[h] - base0),
+                     buf + (h * 32 + lane) * rb, r.len[h] * rb);
+      }
     }
     bulk_commit();
-    advance(sc, last);
-    if (last) enqueue(layer, k);
-    if (ql[0] >= 0 && qk[0] <= k - kBulkLag) {
-      bulk_wait_complete<kBulkLag>();  // pieces <= k - kBulkLag written
-      release_upto(k - kBulkLag);
+    if (pa.unit != cur_unit) {
+      cur_unit = pa.unit;
+      cur_cnt = 0;
+      cur_layer = pa.layer;
     }
-    if (valid(lc)) {
+    ++cur_cnt;
+    if (pa.last || k == count - 1) {  // this warp is done with its part of the unit
+      enqueue(cur_unit, cur_cnt, cur_layer, k);
+      cur_unit = -1;
+    }
+    if (qu[0] >= 0 && qk[0] <= k - kBulkLag) {
+      bulk_wait_complete<kBulkLag>();  // pieces <= k - kBulkLag written
+      settle_upto(k - kBulkLag);
+    }
+    if (kl < count) {
       bulk_wait_read<1>();  // piece k - 1 has read its stage
       __syncwarp();
-      bool ll;
-      piece_unit(lc, ll);
-      issue_loads(lc, kl);
-      advance(lc, ll);
+      issue_loads(kl);
       ++kl;
     }
   }
   bulk_wait_complete<0>();
-  release_upto(0x7fffffff);
+  settle_upto(0x7fffffffffffffffll);
 
   // Units of planes whose rows are not 16-byte aligned (the 4-byte scale
   // plane of a C8 indexer, say): one token per lane, widest aligned granule,
   // published right after the warp's stores (generic proxy only).
   if (j.bulk_planes == (1u << np) - 1u) return;
-  for (int i = 0; gw + i * nw < total; ++i) {
-    if (is_bulk(i)) continue;
-    const int u = gw + i * nw;
-    const int li = u / units_per_layer;
-    const int p = (u - li * units_per_layer) / tiles;
-    const int t0 = (u - li * units_per_layer - p * tiles) * j.tile_tokens;
+  const int units = np * tiles * c.num_layers;
+  for (int u = gw; u < units; u += nw) {
+    const int li = u / (np * tiles);
+    const int p = (u - li * np * tiles) / tiles;
+    if ((j.bulk_planes >> p) & 1u) continue;
+    const int t0 = (u - li * np * tiles - p * tiles) * j.tile_tokens;
     const int n = min(c.num_tokens - t0, j.tile_tokens);
     const int layer = c.layer_begin + li;
     const PlaneDesc sp = plane_of(c.paged, p);
@@ -754,7 +790,8 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
              const at::Tensor &src_slots, const at::Tensor &dst_slots,
              int64_t layer_begin, int64_t num_layers, int64_t replicas,
              const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
-             int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode) {
+             int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode,
+             const c10::optional<at::Tensor> &counters) {
   TORCH_CHECK(src_slots.is_cuda() && dst_slots.is_cuda(),
               "slot mappings must live on the device");
   TORCH_CHECK(src_slots.scalar_type() == dst_slots.scalar_type(),
@@ -853,6 +890,20 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
     for (int r = 0; r < kMaxReplicas; ++r) b.flags[r] = j.flags[r];
     b.budget_ns = 2000000000ull;  // 2 s per mbarrier wait
     b.bulk_planes = bulk_planes;
+    // per-unit completion counters, zero between launches: the caller's
+    // (reused across its launches on one stream), else a fresh zeroed one
+    at::Tensor cnt;
+    if (counters.has_value()) {
+      TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kInt &&
+                      counters->is_contiguous() && counters->numel() >= units &&
+                      counters->device() == src_slots.device(),
+                  "pd_push: counters must be a contiguous device int32 tensor with one "
+                  "entry per unit (", units, ")");
+      cnt = *counters;
+    } else {
+      cnt = at::zeros({std::max<long long>(1, units)}, src_slots.options().dtype(at::kInt));
+    }
+    b.counters = reinterpret_cast<unsigned *>(cnt.data_ptr());
     const size_t smem = kTmaRingOffset +
                         static_cast<size_t>(kBulkWarps) * kBulkStages * kBulkStageBytes;
     static bool attr_set[64] = {false};
@@ -862,9 +913,10 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
                                           static_cast<int>(smem)));
       attr_set[dev & 63] = true;
     }
-    // as many CTAs as fit an SM's shared memory, on every SM
+    // as many CTAs as fit an SM's shared memory, on every SM (each warp takes
+    // an equal range of pieces, so the grid is not bounded by the units)
     const int per_sm = std::max(1, static_cast<int>((228 * 1024) / (smem + 1024)));
-    const long long ctas = (units + kBulkWarps - 1) / kBulkWarps;
+    const long long ctas = num_sms(dev) * static_cast<long long>(per_sm);
     int g = grid > 0 ? static_cast<int>(grid) : num_sms(dev) * per_sm;
     g = static_cast<int>(std::max(1LL, std::min<long long>(ctas, g)));
     pd_push_bulk_kernel<<<g, kBulkWarps * 32, smem, stream>>>(b);

@@ -36,7 +36,8 @@ int64_t push_units_per_layer(int64_t num_tokens, int64_t num_planes, int64_t til
 void pd_push(const PagedLayout &src, const PagedLayout &dst, const at::Tensor &src_slots,
              const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
              int64_t replicas, const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
-             int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode);
+             int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode,
+             const c10::optional<at::Tensor> &counters);
 int64_t fp8_staging_bytes(const PagedLayout &layout, int64_t num_tokens, int64_t num_layers,
                           int64_t group, bool scales);
 void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
@@ -56,6 +57,8 @@ void pd_flag_add(int64_t flag_ptr, int64_t inc);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
+void cachegen_compact(const at::Tensor &src, const at::Tensor &cap, const at::Tensor &first,
+                      const at::Tensor &lengths, const at::Tensor &offsets, at::Tensor &dst);
 at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins);
 void encode_fast_new(const at::Tensor &cdf, const at::Tensor &input_sym,
                      at::Tensor &output_buffer, at::Tensor &output_lengths,
@@ -155,7 +158,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dst_slots"), py::arg("layer_begin"), py::arg("num_layers"),
         py::arg("replicas") = 1, py::arg("flag_ptrs") = std::vector<int64_t>{},
         py::arg("tile_tokens") = 128, py::arg("grid") = 0,
-        py::arg("status") = py::none(), py::arg("mode") = 0);
+        py::arg("status") = py::none(), py::arg("mode") = 0,
+        py::arg("counters") = py::none());
   m.def("fp8_staging_bytes", &fp8_staging_bytes);
   m.def("pd_push_multimem", &pd_push_multimem, py::arg("src"), py::arg("mc_rows"),
         py::arg("mc_flags"), py::arg("src_slots"), py::arg("layer_begin"),
@@ -179,6 +183,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("output_buffer"), py::arg("output_lengths"),
         py::arg("status") = py::none());
   m.def("decode_fast_prefsum", &decode_fast_prefsum);
+  m.def("cachegen_compact", &cachegen_compact);
   m.def("cachegen_quantize", &cachegen_quantize, py::arg("x"), py::arg("bins"), py::arg("sym"),
         py::arg("scale"), py::arg("row_dst") = py::none());
   m.def("cachegen_dequantize", &cachegen_dequantize, py::arg("sym"), py::arg("scale"),

@@ -43,6 +43,10 @@ from .. import ops
 from ..v1.kv_format import PagedKVLayout
 from .ipc import IpcDesc, PeerMappings, export_local
 
+# tokens per flag unit (one release per (layer, plane, tile)); sender and
+# receiver must use the same value for a push
+PUSH_TILE = 512
+
 
 @dataclass
 class ReceiverDesc:
@@ -130,9 +134,11 @@ class PushReceiver:
             self.desc.fp8_q_stride, self.desc.fp8_s_stride = qb, sb
             self.desc.fp8_release_index = self._release_index
 
-    def expect(self, num_tokens: int, layer_begin: int = 0,
-               num_layers: Optional[int] = None, tile_tokens: int = 128) -> torch.Tensor:
-        """Record one incoming push; returns the device targets for ``wait``."""
+    def expect_host(self, num_tokens: int, layer_begin: int = 0,
+                    num_layers: Optional[int] = None,
+                    tile_tokens: int = PUSH_TILE) -> List[int]:
+        """Record one incoming push; returns the per-layer flag targets (host
+        list; any thread may call this, nothing touches the device)."""
         nl = self.layout.num_layers - layer_begin if num_layers is None else num_layers
         units = ops.native().push_units_per_layer(num_tokens, self.layout.num_planes,
                                                   tile_tokens)
@@ -141,11 +147,21 @@ class PushReceiver:
             self.expected[l] = (self.expected[l] + units) & 0xFFFFFFFF
             tg.append(self.expected[l] - (1 << 32) if self.expected[l] >= (1 << 31)
                       else self.expected[l])
+        return tg
+
+    def expect(self, num_tokens: int, layer_begin: int = 0,
+               num_layers: Optional[int] = None, tile_tokens: int = PUSH_TILE) -> torch.Tensor:
+        """Record one incoming push; returns the device targets for ``wait``."""
+        tg = self.expect_host(num_tokens, layer_begin, num_layers, tile_tokens)
         return torch.tensor(tg, dtype=torch.int32).to(self.device, non_blocking=True)
 
-    def wait(self, targets: torch.Tensor, layer_begin: int = 0,
-             timeout_s: float = 10.0) -> None:
-        """Enqueue a bounded wait on the current stream (no host sync)."""
+    def wait(self, targets, layer_begin: int = 0, timeout_s: float = 10.0) -> None:
+        """Enqueue a bounded wait on the current stream (no host sync).
+        ``targets``: device tensor from ``expect``, or the host list of
+        ``expect_host`` (copied from pinned memory on the current stream)."""
+        if not isinstance(targets, torch.Tensor):
+            host = torch.tensor(targets, dtype=torch.int32).pin_memory()
+            targets = host.to(self.device, non_blocking=True)
         ops.native().pd_wait_flags(self._flags_buf.data_ptr(), targets, layer_begin,
                                    timeout_s, self.status.tensor)
 
@@ -208,6 +224,10 @@ class PushSender:
         self._flag_ptrs: List[int] = []
         self.replicas = 0
         self._last_push: Optional[torch.cuda.Event] = None  # unmap only after it
+        # per-unit completion counters of the bulk engine (zero between
+        # launches; launches of one sender run in stream order)
+        self._counters: Optional[torch.Tensor] = None
+        self._old_counters: List[torch.Tensor] = []
 
     def connect(self, receivers: Sequence[ReceiverDesc]) -> None:
         """Map one or more receivers (same layout, fan-out) for pushing."""
@@ -242,7 +262,7 @@ class PushSender:
                          r0.fp8_q_stride, r0.fp8_s_stride, rel)
 
     def push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, layer_begin: int = 0,
-             num_layers: Optional[int] = None, tile_tokens: int = 128, grid: int = 0,
+             num_layers: Optional[int] = None, tile_tokens: int = PUSH_TILE, grid: int = 0,
              quant: str = "none", staging_timeout_s: float = 10.0) -> None:
         """Enqueue the push of ``num_layers`` layers on the current stream.
         ``quant="fp8"`` sends block-scaled fp8 to the receiver's staging (the
@@ -274,9 +294,16 @@ class PushSender:
             return
         if quant != "none":
             raise ValueError("quant must be 'none' or 'fp8'")
+        units = ops.native().push_units_per_layer(src_slots.numel(), self.layout.num_planes,
+                                                  tile_tokens) * nl
+        if self._counters is None or self._counters.numel() < units:
+            if self._counters is not None:  # an earlier launch may still use it
+                self._old_counters.append(self._counters)
+            self._counters = torch.zeros(max(units, 1 << 16), dtype=torch.int32,
+                                         device=self.device)
         ops.native().pd_push(self.layout.native(), self._dst, src_slots, dst_slots,
                              layer_begin, nl, self.replicas, self._flag_ptrs, tile_tokens,
-                             grid, self.status.tensor, _ENGINES[self.engine])
+                             grid, self.status.tensor, _ENGINES[self.engine], self._counters)
         self._mark_pushed()
 
     def _mark_pushed(self) -> None:
@@ -285,7 +312,13 @@ class PushSender:
         self._last_push.record()
 
     def check(self) -> None:
-        self.status.check("pd push sender")
+        try:
+            self.status.check("pd push sender")
+        except RuntimeError:
+            # a push that stopped early leaves unit counters half counted
+            if self._counters is not None:
+                self._counters.zero_()
+            raise
 
     def close(self) -> None:
         """Unmap the receivers, after the pushes enqueued so far have run

@@ -380,7 +380,7 @@ class LMCacheEngine:
     def begin_direct_prefill(self, req_id: str, *, slot_mapping: torch.Tensor,
                              dst_slot_mapping: Optional[torch.Tensor] = None,
                              num_layers: Optional[int] = None, token_begin: int = 0,
-                             tile_tokens: int = 128) -> "DirectPrefillPush":
+                             tile_tokens: int = 512) -> "DirectPrefillPush":
         """Prefiller, layer-by-layer push during the prefill forward: get the
         decoder's grant for every layer of ``req_id`` now (raises, with
         nothing launched, on refusal), then call ``push_layer`` on the

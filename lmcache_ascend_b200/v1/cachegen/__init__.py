@@ -154,6 +154,14 @@ class CacheGenEncoded:
         return b"".join(parts)
 
     @staticmethod
+    def peek_shape(b: bytes) -> Tuple[int, int, int, torch.dtype]:
+        """(layers, tokens, channels, dtype) from a payload's header."""
+        magic, ver, L, T, C, dt, _ = struct.unpack("<4sHIIIBH", b[:struct.calcsize("<4sHIIIBH")])
+        if magic != MAGIC or ver != VERSION:
+            raise ValueError("not a CacheGen payload")
+        return L, T, C, _DT[dt]
+
+    @staticmethod
     def from_bytes(b: bytes) -> "CacheGenEncoded":
         fmt = "<4sHIIIBH"
         n = struct.calcsize(fmt)
@@ -186,10 +194,22 @@ class CacheGenEncoded:
         return CacheGenEncoded(L, T, C, _DT[dt], scales, kb, vb, groups)
 
 
+def _pack_nibbles_dev(x: torch.Tensor) -> torch.Tensor:
+    """Device version of the code-length packing: two 4-bit lengths per byte,
+    first in the high nibble (same bytes as ``_pack_nibbles``)."""
+    a = x.to(torch.uint8).flatten()
+    if a.numel() % 2:
+        a = torch.cat([a, torch.zeros(1, dtype=torch.uint8, device=a.device)])
+    return (a[0::2] << 4) | a[1::2]
+
+
 def encode_kv(kv: torch.Tensor, config: CacheGenConfig) -> CacheGenEncoded:
     """kv: KV_2LTD chunk [2, L, T, C] (device or host).  One quantise launch
     writes the symbols of rows sharing a bin count next to each other, so
-    every group's CDF and encode run on a contiguous slice."""
+    every group's CDF and encode run on a contiguous slice.  On the device
+    the streams are then packed back to back by one compaction kernel and
+    the whole payload (scales, lengths, code lengths, streams) leaves the GPU
+    in one copy, after one small read of the per-group stream totals."""
     _, L, T, C = kv.shape
     dev = kv.device
     kb, vb = config.bins("k"), config.bins("v")
@@ -198,8 +218,8 @@ def encode_kv(kv: torch.Tensor, config: CacheGenConfig) -> CacheGenEncoded:
     order, pos = _group_order(row_bins)
     sym, scale = api.cachegen_quantize(kv.reshape(2 * L, T, C), row_bins_t.to(dev),
                                        torch.tensor(pos, dtype=torch.int32, device=dev))
-    groups = []
     cap = ((T * 12 + 7) // 8 + 4) // 4 * 4
+    enc_out = []  # per group: (bins, rows, stream slots, lengths, code lengths)
     off = 0
     for bins, rows in order:
         sg = sym[off:off + len(rows)]
@@ -208,11 +228,116 @@ def encode_kv(kv: torch.Tensor, config: CacheGenConfig) -> CacheGenEncoded:
         out = torch.empty(len(rows), C, cap, dtype=torch.uint8, device=dev)
         lens = torch.empty(len(rows), C, dtype=torch.int32, device=dev)
         api.encode_fast_new(cdf, sg, out, lens)
-        mask = torch.arange(cap, device=dev).unsqueeze(0) < lens.view(-1, 1)
-        streams = out.view(-1, cap)[mask].cpu().numpy().tobytes()
         code_len = (cdf[..., :bins].to(torch.int32) & 0xF).to(torch.uint8)
-        groups.append(CacheGenGroup(rows, bins, code_len.cpu(), lens.cpu(), streams))
-    return CacheGenEncoded(L, T, C, kv.dtype, scale.float().cpu(), kb, vb, groups)
+        enc_out.append((bins, rows, out, lens, code_len))
+    if dev.type != "cuda":
+        groups = []
+        for bins, rows, out, lens, code_len in enc_out:
+            mask = torch.arange(cap).unsqueeze(0) < lens.view(-1, 1)
+            groups.append(CacheGenGroup(rows, bins, code_len, lens,
+                                        out.view(-1, cap)[mask].numpy().tobytes()))
+        return CacheGenEncoded(L, T, C, kv.dtype, scale.float(), kb, vb, groups)
+    from ...ops import native
+
+    all_lens = torch.cat([g[3].view(-1) for g in enc_out])
+    ends = torch.cumsum(all_lens.to(torch.int64), 0)
+    offsets = ends - all_lens
+    counts = [g[3].numel() for g in enc_out]
+    bounds = torch.tensor(counts, dtype=torch.int64).cumsum(0) - 1
+    totals = ends[bounds.to(dev)].cpu().tolist()  # the one device read before the copy
+    group_bytes = [t - (totals[i - 1] if i else 0) for i, t in enumerate(totals)]
+    streams = torch.empty(max(1, totals[-1]), dtype=torch.uint8, device=dev)
+    first = torch.tensor([0] + list(torch.tensor(counts).cumsum(0)[:-1].tolist()),
+                         dtype=torch.int64, device=dev)
+    native().cachegen_compact(
+        torch.tensor([g[2].data_ptr() for g in enc_out], dtype=torch.int64, device=dev),
+        torch.full((len(enc_out),), cap, dtype=torch.int64, device=dev), first, all_lens,
+        offsets, streams)
+    pieces = [scale.float().contiguous().view(torch.uint8).view(-1)]
+    for _, _, _, lens, code_len in enc_out:
+        pieces += [lens.contiguous().view(torch.uint8).view(-1), _pack_nibbles_dev(code_len)]
+    pieces.append(streams[:totals[-1]])
+    host = torch.empty(sum(p.numel() for p in pieces), dtype=torch.uint8, pin_memory=True)
+    host.copy_(torch.cat(pieces), non_blocking=True)
+    torch.cuda.current_stream(dev).synchronize()
+    o = 0
+
+    def take(n):
+        nonlocal o
+        t = host[o:o + n]
+        o += n
+        return t
+
+    scales_h = take(2 * L * T * 4).clone().view(torch.float32).view(2 * L, T)
+    groups = []
+    metas = []
+    for bins, rows, _, _, _ in enc_out:
+        lens_h = take(len(rows) * C * 4).clone().view(torch.int32).view(len(rows), C)
+        ncl = len(rows) * C * bins
+        cl_h = _unpack_nibbles(take((ncl + 1) // 2).numpy().tobytes(), ncl).view(
+            len(rows), C, bins)
+        metas.append((bins, rows, lens_h, cl_h))
+    sbytes = take(totals[-1]).numpy().tobytes()
+    so = 0
+    for (bins, rows, lens_h, cl_h), nb in zip(metas, group_bytes):
+        groups.append(CacheGenGroup(rows, bins, cl_h, lens_h, sbytes[so:so + nb]))
+        so += nb
+    return CacheGenEncoded(L, T, C, kv.dtype, scales_h, kb, vb, groups)
+
+
+def decode_kv_bytes(data: bytes, device="cpu", out: Optional[torch.Tensor] = None
+                    ) -> torch.Tensor:
+    """Decode a serialised payload (``CacheGenEncoded.to_bytes``) straight
+    from bytes: on the device the payload goes over in one copy and every
+    section is used in place (no per-group transfers)."""
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        return decode_kv(CacheGenEncoded.from_bytes(data), dev, out)
+    fmt = "<4sHIIIBH"
+    n = struct.calcsize(fmt)
+    magic, ver, L, T, C, dt, ng = struct.unpack(fmt, data[:n])
+    if magic != MAGIC or ver != VERSION:
+        raise ValueError("not a CacheGen payload")
+    dtype = _DT[dt]
+    kb = torch.frombuffer(bytearray(data[n:n + 4 * L]), dtype=torch.int32)
+    vb = torch.frombuffer(bytearray(data[n + 4 * L:n + 8 * L]), dtype=torch.int32)
+    payload = torch.frombuffer(bytearray(data), dtype=torch.uint8).to(dev)
+    off = n + 8 * L
+    scales = payload[off:off + 8 * L * T].clone().view(torch.float32).view(2 * L, T)
+    off += 8 * L * T
+    sym = torch.empty(2 * L, T, C, dtype=torch.uint8, device=dev)
+    pos = [0] * (2 * L)
+    row0 = 0
+    for _ in range(ng):
+        bins, nrows, slen = struct.unpack("<HII", data[off:off + 10])
+        off += 10
+        rows = np.frombuffer(data, dtype=np.int32, count=nrows, offset=off).tolist()
+        off += 4 * nrows
+        lens = payload[off:off + 4 * nrows * C].clone().view(torch.int32)
+        off += 4 * nrows * C
+        ncl = nrows * C * bins
+        packed = payload[off:off + (ncl + 1) // 2]
+        off += (ncl + 1) // 2
+        cl = torch.stack([packed >> 4, packed & 15], dim=1).flatten()[:ncl].view(nrows, C, bins)
+        stream = payload[off:off + slen] if slen else torch.zeros(1, dtype=torch.uint8,
+                                                                  device=dev)
+        off += slen
+        cum = torch.cumsum(lens, 0).to(torch.int32).view(nrows, C)
+        api.decode_fast_prefsum(cdf_from_lengths(cl), stream, cum, sym[row0:row0 + nrows])
+        for i, r in enumerate(rows):
+            pos[r] = row0 + i
+        row0 += nrows
+    row_bins = torch.cat([kb, vb]).to(torch.int32)
+    src = torch.tensor(pos, dtype=torch.int32, device=dev)
+    direct = out is not None and out.is_contiguous() and out.dtype == dtype and \
+        out.device == dev
+    y = api.cachegen_dequantize(sym, scales, row_bins, dtype, row_src=src,
+                                out=out.view(2 * L, T, C) if direct else None)
+    res = y.view(2, L, T, C)
+    if out is not None and not direct:
+        out.copy_(res)
+        return out
+    return out if direct else res
 
 
 def decode_kv(enc: CacheGenEncoded, device="cpu", out: Optional[torch.Tensor] = None

@@ -37,6 +37,7 @@ class ReceiverMixin:
         # destination slots the decoder reserved per request, and how many of
         # its tokens were granted so far
         self.reservations: Dict[str, dict] = {}
+        self._grant_cv = threading.Condition(self._lock)  # signalled on every grant
         self._done_socks: Dict[str, zmq.Socket] = {}
         self.init_url = self._rep_server(f"tcp://{bind_host}:{ip}", self._handle_init,
                                          "lmc-pd-init")
@@ -123,8 +124,9 @@ class ReceiverMixin:
                     self.stats.inc("pd_direct_refused_range")
                     return M.DirectPushGrant(False, epoch,
                                              "destination slot out of the paged cache")
-                tg = pr.expect(n, msg.layer_begin, msg.num_layers, msg.tile_tokens)
+                tg = pr.expect_host(n, msg.layer_begin, msg.num_layers, msg.tile_tokens)
                 self.direct[msg.req_id] = [tg, msg.layer_begin, msg.num_layers, msg.layer_begin]
+                self._grant_cv.notify_all()
                 self.stats.inc("pd_direct_granted")
                 return M.DirectPushGrant(True, epoch)
             arr = res["slots"]
@@ -150,13 +152,15 @@ class ReceiverMixin:
                                                            "the decoder's reservation")
             if int(part.max()) >= pr.layout.num_slots:
                 return M.DirectPushGrant(False, epoch, "reserved slot out of the paged cache")
-            res["targets"] = pr.expect(n, msg.layer_begin, msg.num_layers, msg.tile_tokens)
+            res["targets"] = pr.expect_host(n, msg.layer_begin, msg.num_layers,
+                                            msg.tile_tokens)
             res["granted"] = tb + n
             res["layers"] = (msg.layer_begin, msg.num_layers)
             if res["granted"] >= len(arr):  # every reserved token is on its way
                 self.reservations.pop(msg.req_id, None)
                 lb, nl = res["layers"]
                 self.direct[msg.req_id] = [res["targets"], lb, nl, lb]
+                self._grant_cv.notify_all()
         self.stats.inc("pd_direct_granted")
         return M.DirectPushGrant(True, epoch, slots=slots_out, first_token=res["first"])
 
@@ -294,13 +298,15 @@ class ReceiverMixin:
         return obj  # the caller owns the backend's reference
 
     def _granted(self, req_id: str, timeout_s: float):
+        """The granted entry of ``req_id``, waiting (bounded) for the grant."""
         deadline = time.monotonic() + timeout_s
-        while True:
-            with self._lock:
+        with self._grant_cv:
+            while True:
                 ent = self.direct.get(req_id)
-            if ent is not None or time.monotonic() > deadline:
-                return ent
-            time.sleep(0.0005)
+                left = deadline - time.monotonic()
+                if ent is not None or left <= 0:
+                    return ent
+                self._grant_cv.wait(left)
 
     def wait_direct(self, req_id: str, timeout_s: Optional[float] = None,
                     sync: bool = False) -> bool:
@@ -316,7 +322,7 @@ class ReceiverMixin:
         with self._lock:
             self.direct.pop(req_id, None)
         if nxt < lb + nl:
-            self.push_receiver.wait(tg[nxt - lb:], nxt, to)
+            self.push_receiver.wait(list(tg[nxt - lb:]), nxt, to)
         if sync:
             torch.cuda.current_stream().synchronize()
             self.push_receiver.check()
@@ -335,7 +341,7 @@ class ReceiverMixin:
         tg, lb, nl, nxt = ent
         last = min(layer, lb + nl - 1)
         if last >= nxt:
-            self.push_receiver.wait(tg[nxt - lb:last - lb + 1], nxt, to)
+            self.push_receiver.wait(list(tg[nxt - lb:last - lb + 1]), nxt, to)
             ent[3] = last + 1
         if ent[3] >= lb + nl:
             with self._lock:

@@ -189,7 +189,7 @@ class SenderMixin:
 
     def reserve_direct_push(self, req_id: str, num_tokens: int, dst_slots_host,
                             layer_begin: int = 0, num_layers: Optional[int] = None,
-                            tile_tokens: int = 128, token_begin: int = 0,
+                            tile_tokens: int = 512, token_begin: int = 0,
                             prompt_end: int = -1) -> Tuple[List[int], int]:
         """Ask the decoder to grant a direct push of ``req_id`` before anything
         is launched.  ``dst_slots_host`` (host tensor or sequence) are the
@@ -245,7 +245,7 @@ class SenderMixin:
 
     def direct_push(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, req_id: str,
                     layer_begin: int = 0, num_layers: Optional[int] = None,
-                    tile_tokens: int = 128, dst_slots_host=None) -> None:
+                    tile_tokens: int = 512, dst_slots_host=None) -> None:
         """Reserve (``reserve_direct_push``), then push the prefiller's paged
         KV rows ``src_slots`` straight into the decoder's paged blocks
         ``dst_slots`` with the fused kernel on the current stream.
@@ -264,7 +264,7 @@ class SenderMixin:
                        src_slots.numel() * nl * sum(self.push_sender.layout.row_bytes))
 
     def push_granted_layers(self, src_slots: torch.Tensor, dst_slots: torch.Tensor,
-                            layer_begin: int, num_layers: int, tile_tokens: int = 128) -> None:
+                            layer_begin: int, num_layers: int, tile_tokens: int = 512) -> None:
         """Launch layers of a push that ``reserve_direct_push`` granted (for
         the layer-by-layer push during prefill: one grant per request, then
         one launch per layer with no round trip)."""

@@ -15,7 +15,7 @@ from typing import Optional
 import torch
 
 from ...config import LMCacheEngineConfig
-from ..cachegen import CacheGenConfig, CacheGenEncoded, decode_kv, encode_kv
+from ..cachegen import CacheGenConfig, CacheGenEncoded, decode_kv, decode_kv_bytes, encode_kv
 from ..memory_management import MemoryFormat, MemoryObj
 
 _NAIVE = b"LMCN"
@@ -74,12 +74,14 @@ class CacheGenSerde:
         return encode_kv(kv, self._cfg(kv.shape[1])).to_bytes()
 
     def deserialize(self, data: bytes, allocator) -> Optional[MemoryObj]:
-        enc = CacheGenEncoded.from_bytes(data)
-        shape = torch.Size([2, enc.num_layers, enc.num_tokens, enc.channels])
-        obj = allocator.allocate(shape, enc.dtype, MemoryFormat.KV_2LTD)
+        L, T, C, dtype = CacheGenEncoded.peek_shape(data)
+        obj = allocator.allocate(torch.Size([2, L, T, C]), dtype, MemoryFormat.KV_2LTD)
         if obj is None:
             return None
-        kv = decode_kv(enc, self.device)
+        if self.device.startswith("cuda"):
+            kv = decode_kv_bytes(data, self.device)  # one H2D of the payload
+        else:
+            kv = decode_kv(CacheGenEncoded.from_bytes(data), self.device)
         obj.tensor.copy_(kv)
         return obj
 

@@ -43,7 +43,7 @@ class FakeReceiver:
                                  slot_stride=[0, 0], row_bytes=self.layout.row_bytes,
                                  planes=[], flags={}, device=0, epoch=uuid.uuid4().hex)
 
-    def expect(self, n, lb, nl, tile):
+    def expect_host(self, n, lb, nl, tile):
         self.expected.append((n, lb, nl, tile))
         return list(range(nl))
 
@@ -113,7 +113,7 @@ def test_granted_push_launches_once_after_the_grant():
         assert len(pd_s.push_sender.launches) == 1
         s, d, lb, nl = pd_s.push_sender.launches[0]
         assert torch.equal(d, dst) and torch.equal(s, src) and (lb, nl) == (0, L)
-        assert pd_r.push_receiver.expected == [(40, 0, L, 128)]
+        assert pd_r.push_receiver.expected == [(40, 0, L, 512)]
         assert recv.direct_prefill_granted("r1")
         assert recv.wait_direct_prefill("r1", timeout_s=1.0)
     finally:
