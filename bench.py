@@ -103,6 +103,9 @@ def parse():
     ap.add_argument("--overlap-iters", type=int, default=2)
     ap.add_argument("--no-config5", action="store_true",
                     help="skip the DeepSeek-V3.2 MLA latent + C8 indexer push (config 5)")
+    ap.add_argument("--no-config2", action="store_true",
+                    help="skip the Llama-3-8B local offload per DP replica (config 2)")
+    ap.add_argument("--config2-requests", type=int, default=64)
     ap.add_argument("--fp8-tile", type=int, default=512,
                     help="tokens per fp8 push unit (one flag release per unit)")
     return ap.parse_args()
@@ -577,6 +580,15 @@ def main():
             dist.all_reduce(p50, op=dist.ReduceOp.MAX)
         ttft["p50_ms_max_over_ranks"] = round(float(p50.item()), 3)
         barrier()
+        # the same hit served from the HBM tier (the prefix kept on the GPU)
+        ttft_hbm = run_ttft(dev, tokens=a.tokens, requests=a.ttft_requests, warmup=3,
+                            tier="hbm")
+        p50 = torch.tensor([ttft_hbm["p50_ms"]], device=dev)
+        if world > 1:
+            dist.all_reduce(p50, op=dist.ReduceOp.MAX)
+        ttft_hbm["p50_ms_max_over_ranks"] = round(float(p50.item()), 3)
+        ttft["hbm_tier"] = ttft_hbm
+        barrier()
 
     # ------------------------------------ push hidden under the prefill
     # The serving path: a Qwen3-32B TP4-shard prefill forward of the prompt,
@@ -604,6 +616,16 @@ def main():
 
         config5 = run_config5(dev, rank, world, gloo, warmup=max(3, a.warmup),
                               peer_copy_gbps=peer_copy["gbps_per_pair"] if peer_copy else None)
+        barrier()
+
+    # ------------------- config 2: local offload, one replica per GPU
+    config2 = None
+    if not a.no_config2:
+        torch.cuda.empty_cache()
+        barrier()
+        from lmcache_ascend_b200.bench_config2 import run_config2
+
+        config2 = run_config2(dev, rank, world, gloo, requests=a.config2_requests)
         barrier()
 
     if rank == 0:
@@ -635,6 +657,7 @@ def main():
              "per_pair_gbps": round(per_pair, 2), "roofline": roof, "baseline": baseline,
              "clocks": ck, "e2e": e2e, "gpu_launches": launches, "ttft": ttft,
              "push_fp8": fp8, "prefill_overlap": overlap, "config5_dsv32_mla_c8": config5,
+             "config2_llama3_8b_offload": config2,
              **({"multicast": mcast} if mcast is not None else {})})
     if sender is not None:
         sender.close()

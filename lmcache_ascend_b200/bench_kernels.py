@@ -234,6 +234,53 @@ def bench_cachegen(small: bool):
           rel_rms_err=round(float(err.pow(2).mean().sqrt() / x.float().pow(2).mean().sqrt()), 4))
 
 
+def bench_cachegen_serde(small: bool):
+    """BASELINE config 4 end to end through the serde API: KV_2LTD chunks of
+    256 tokens x 32 layers x 8 heads x 128 (bf16 N(0,1) x per-channel
+    U(0.5, 2); 8-bit for the first third of the layers, 4-bit after) encoded
+    by ``encode_kv(...).to_bytes()`` on the device (quantise, CDF, encode,
+    compaction, one D2H) and decoded by ``decode_kv_bytes`` (one H2D,
+    decode, dequantise) back into a device chunk.  Times include the
+    host <-> device copies of the payload; GB/s counts bf16 KV bytes."""
+    from .v1.cachegen import CacheGenConfig, decode_kv_bytes, encode_kv
+
+    chunks = 2 if small else 8
+    L, T, H, D = 32, 256, 8, 128
+    C = H * D
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ch_scale = torch.rand(1, 1, 1, C, device="cuda", generator=g) * 1.5 + 0.5
+    kvs = [(torch.randn(2, L, T, C, device="cuda", generator=g) * ch_scale).to(torch.bfloat16)
+           for _ in range(chunks)]
+    cfg = CacheGenConfig.from_ranges(L, [(0, L // 3, 256), (L // 3, L, 16)],
+                                     [(0, L // 3, 256), (L // 3, L, 16)])
+    kv_bytes = sum(k.numel() * 2 for k in kvs)
+    payloads = []
+
+    def enc():
+        payloads.clear()
+        for k in kvs:
+            payloads.append(encode_kv(k, cfg).to_bytes())
+
+    ms = _time(enc, iters=3, warmup=1)
+    wire = sum(len(b) for b in payloads)
+    _emit("cachegen_serde_encode", ms, kv_bytes, traffic_bytes=kv_bytes, chunks=chunks,
+          payload_bytes=wire, ratio_vs_bf16=round(kv_bytes / wire, 3),
+          note="to_bytes included (one D2H per chunk)")
+    outs = [torch.empty_like(k) for k in kvs]
+
+    def dec():
+        for b, o in zip(payloads, outs):
+            decode_kv_bytes(b, "cuda", out=o)
+
+    ms = _time(dec, iters=3, warmup=1)
+    err = torch.cat([(o.float() - k.float()).flatten() for o, k in zip(outs, kvs)])
+    ref = torch.cat([k.float().flatten() for k in kvs])
+    _emit("cachegen_serde_decode", ms, kv_bytes, traffic_bytes=kv_bytes, chunks=chunks,
+          payload_bytes=wire, max_abs_err=round(float(err.abs().max()), 4),
+          rel_rms_err=round(float(err.pow(2).mean().sqrt() / ref.pow(2).mean().sqrt()), 4),
+          note="from bytes: one H2D per chunk")
+
+
 def bench_rope(small: bool):
     """K re-rotation (BASELINE config 5 pass: theta 10000, deltas 0-8192) on a
     bf16 K of 65536 tokens x 8 heads x 128 (128 MiB, larger than L2)."""
@@ -314,6 +361,7 @@ def bench_push(small: bool):
 
 
 CASES = {"gather": bench_gather_scatter, "offload": bench_offload, "cachegen": bench_cachegen,
+         "cachegen_serde": bench_cachegen_serde,
          "rope": bench_rope, "c8": bench_c8, "push": bench_push}
 
 

@@ -40,7 +40,11 @@ def _block_slots(T: int, bs: int, blocks: torch.Tensor) -> torch.Tensor:
 def run_ttft(device, tokens: int = 16384, requests: int = 8, warmup: int = 2,
              model_config: Optional[LlamaConfig] = None, chunk_size: int = 256,
              block_size: int = 128, dtype=torch.bfloat16, seed: int = 0,
-             transfer_mode: str = "copy_engine", numa_node: int = -2) -> Dict:
+             transfer_mode: str = "copy_engine", numa_node: int = -2,
+             tier: str = "cpu") -> Dict:
+    """``tier``: "cpu" keeps the stored prefix in the pinned CPU tier (the
+    hit crosses the host link); "hbm" keeps it in the HBM tier (the hit is a
+    device-to-device scatter)."""
     from .v1.cache_engine import LMCacheEngine
     from .v1.gpu_connector import VLLMPagedMemLayerwiseGPUConnector
 
@@ -55,9 +59,12 @@ def run_ttft(device, tokens: int = 16384, requests: int = 8, warmup: int = 2,
     kv = [(torch.randn(nb, BS, KH, D, device=dev, dtype=dtype, generator=g),
            torch.randn(nb, BS, KH, D, device=dev, dtype=dtype, generator=g)) for _ in range(L)]
     kv_bytes = tokens * L * 2 * KH * D * torch.empty((), dtype=dtype).element_size()
+    hbm = tier == "hbm"
     cfg = LMCacheEngineConfig.from_defaults(
         chunk_size=chunk_size, use_layerwise=True, local_cpu=True,
-        max_local_cpu_size=kv_bytes * 1.05 / (1 << 30) + 0.05, save_unfull_chunk=True,
+        max_local_cpu_size=(0.05 if hbm else kv_bytes * 1.05 / (1 << 30) + 0.05),
+        save_unfull_chunk=True, local_gpu=hbm,
+        max_local_gpu_size=(kv_bytes * 1.05 / (1 << 30) + 0.05) if hbm else 0.0,
         cpu_transfer_mode=transfer_mode, numa_node=numa_node if dev.type == "cuda" else -1)
     md = LMCacheEngineMetadata("Qwen3-32B" if mc.num_layers == 64 else "model", 1, 0, "vllm",
                                dtype)
@@ -131,8 +138,10 @@ def run_ttft(device, tokens: int = 16384, requests: int = 8, warmup: int = 2,
            "phases_p50_ms": {k: round(sorted(v)[len(v) // 2], 3) for k, v in phases.items() if v},
            "model": f"{md.model_name} (random init, TP1: {L} layers, {mc.num_heads} heads, "
                     f"{KH} KV heads)",
-           "path": "lookup + layerwise CPU->GPU retrieve overlapped with the new token's "
-                   "forward + lm_head argmax + D2H"}
+           "tier": tier,
+           "path": ("lookup + layerwise " + ("HBM-tier device->paged" if hbm else "CPU->GPU")
+                    + " retrieve overlapped with the new token's forward + lm_head argmax "
+                      "+ D2H")}
     del model, kv, conn, eng
     if dev.type == "cuda":
         torch.cuda.empty_cache()
@@ -146,9 +155,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--mode", default="copy_engine", choices=["copy_engine", "zero_copy"])
     ap.add_argument("--numa", type=int, default=-2, help="-2 auto, -1 none, >= 0 node")
+    ap.add_argument("--tier", default="cpu", choices=["cpu", "hbm"])
     a = ap.parse_args()
     print(json.dumps(run_ttft("cuda", a.tokens, a.requests, a.warmup, transfer_mode=a.mode,
-                              numa_node=a.numa)), flush=True)
+                              numa_node=a.numa, tier=a.tier)), flush=True)
 
 
 if __name__ == "__main__":

@@ -48,6 +48,10 @@ class LMCacheEngineConfig:
     # --- local CPU ------------------------------------------------------------
     local_cpu: bool = True
     max_local_cpu_size: float = 5.0  # GB
+    # HBM tier above the CPU tier (device-resident chunks, LRU with write-back
+    # to the CPU tier on eviction)
+    local_gpu: bool = False
+    max_local_gpu_size: float = 0.0  # GB
     numa_node: int = -1  # >= 0: bind the CPU tier there, -1: no binding, -2: the GPU's node
     shared_cpu_cache: bool = False
     shared_cpu_cache_name: Optional[str] = None

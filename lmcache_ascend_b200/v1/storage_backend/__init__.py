@@ -1,8 +1,8 @@
 """Storage backends and the factory that assembles the hierarchy.
 
 Order (reference lmcache_ascend/v1/storage_backend/__init__.py:51-167):
-PD -> LocalCPU -> P2P -> LocalDisk -> Remote -> plugins, optionally wrapped
-by the audit backend.
+PD -> [LocalGPU, the HBM tier this repo adds] -> LocalCPU -> P2P -> LocalDisk
+-> Remote -> plugins, optionally wrapped by the audit backend.
 """
 
 from __future__ import annotations
@@ -38,11 +38,17 @@ def CreateStorageBackends(config: LMCacheEngineConfig,
     # The CPU tier always exists: it provides the allocator.  With
     # local_cpu=False it only allocates and does not keep objects.
     cpu = LocalCPUBackend(config, allocator=kw.get("cpu_allocator"))
+    gpu = None
+    if config.local_gpu and config.max_local_gpu_size > 0:
+        from .local_gpu_backend import LocalGPUBackend
+
+        gpu = LocalGPUBackend(config, lower=cpu)
+        backends[gpu.name] = gpu  # first: it allocates the chunks of every store
     backends[cpu.name] = cpu
     if config.enable_p2p:
         from .p2p_backend import P2PBackend
 
-        p2p = P2PBackend(config, metadata, cpu, **kw)
+        p2p = P2PBackend(config, metadata, cpu, hbm=gpu, **kw)
         backends[p2p.name] = p2p
     if config.local_disk:
         from .local_disk_backend import LocalDiskBackend

@@ -83,6 +83,12 @@ class LocalCPUBackend(StorageBackendInterface):
                                 transfer_spec: Any = None) -> Optional[List[Future]]:
         if not self.store_objects:
             return None
+        if type(self) is LocalCPUBackend:
+            # device chunks belong to the HBM tier; they reach this tier only
+            # through its eviction write-back
+            pairs = [(k, o) for k, o in zip(keys, objs)
+                     if o.raw_data is None or not o.raw_data.is_cuda]
+            keys, objs = [k for k, _ in pairs], [o for _, o in pairs]
         with self._lock:
             for k, o in zip(keys, objs):
                 old = self.hot_cache.pop(k, None)

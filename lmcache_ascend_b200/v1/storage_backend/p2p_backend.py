@@ -2,12 +2,20 @@
 
 Behaviour of the reference's ``P2PBackend`` (lmcache_ascend/v1/storage_backend/
 p2p_backend.py:106-985): chunks stored locally are announced to the
-controller (and withdrawn when the CPU tier evicts them); a lookup miss in
-the local tiers asks the controller which instance holds the key; a get pulls
-the chunk from that instance's peer server, retrying other holders (up to
-``p2p_max_retries``) when a peer fails or times out.  The peer server answers
-from its own CPU tier.  Chunk bytes travel as naive-serde messages over ZMQ
-(host-resident chunks; on one box the copy is PCIe/host-memory bound anyway).
+controller (and withdrawn when no local tier holds them any more); a lookup
+miss in the local tiers asks the controller which instance holds the key; a
+get pulls the chunk from that instance, retrying other holders (up to
+``p2p_max_retries``) when a peer fails or times out.
+
+Data plane:
+* chunk in the holder's HBM tier (one box): the holder pins the object under
+  a lease and answers with its offset in its HBM slab, which every instance
+  exported over CUDA IPC when it registered; the reader maps the slab once
+  and copies the chunk over NVLink into its own tier (one device-to-device
+  peer copy), then returns the lease.  Leases a reader never returns expire
+  after ``p2p_pull_pending_ttl`` seconds (reference delayed pull with proxy
+  objects, p2p_backend.py:838-960);
+* chunk in the holder's CPU tier: naive-serde bytes over ZMQ.
 """
 
 from __future__ import annotations
@@ -18,6 +26,7 @@ import uuid as _uuid
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import msgpack
+import torch
 import zmq
 
 from ...config import LMCacheEngineConfig
@@ -34,9 +43,20 @@ logger = init_logger(__name__)
 class P2PBackend(StorageBackendInterface):
     name = "P2PBackend"
 
-    def __init__(self, config: LMCacheEngineConfig, metadata, local_cpu, **kw):
+    def __init__(self, config: LMCacheEngineConfig, metadata, local_cpu, hbm=None, **kw):
         self.config = config
         self.local = local_cpu
+        self.hbm = hbm                      # LocalGPUBackend or None
+        self._leases: Dict[str, Tuple[MemoryObj, float]] = {}
+        self._lease_lock = threading.Lock()
+        self._peer_maps = None              # PeerMappings of the holders' HBM slabs
+        self._slab_desc = None
+        if hbm is not None:
+            from ...parallel.ipc import export_local
+
+            slab = hbm.allocator.dev.tensor
+            self._slab_base = slab.data_ptr()
+            self._slab_desc = export_local(self._slab_base, hbm.device.index or 0).to_dict()
         self.instance = f"{config.lmcache_instance_id}-{metadata.worker_id if metadata else 0}" \
                         f"-{_uuid.uuid4().hex[:6]}"
         self.timeout_ms = int(config.blocking_timeout_secs * 1000)
@@ -61,8 +81,10 @@ class P2PBackend(StorageBackendInterface):
         self._t.start()
         if not config.controller_url:
             raise ValueError("enable_p2p needs controller_url")
-        self._ctl_rpc("register", self.peer_url)
+        self._ctl_rpc("register", {"url": self.peer_url, "hbm": self._slab_desc})
         local_cpu.evict_listeners.append(self._on_evict)
+        if hbm is not None:
+            hbm.evict_listeners.append(self._on_evict)
 
     # ----------------------------------------------------------- controller
     def _ctl_rpc(self, op: str, payload):
@@ -86,6 +108,9 @@ class P2PBackend(StorageBackendInterface):
         return res
 
     def _on_evict(self, key: CacheEngineKey) -> None:
+        for tier in (self.hbm, self.local):
+            if tier is not None and tier.contains(key):
+                return  # still held here (an HBM eviction writes back to the CPU tier)
         try:
             self._ctl_rpc("evict", [key.to_string()])
         except (TimeoutError, RuntimeError):
@@ -100,18 +125,80 @@ class P2PBackend(StorageBackendInterface):
                 continue
             try:
                 op, key = msgpack.unpackb(self._srv.recv(), raw=False)
-                data = None
+                self._expire_leases()
+                if op == "release":
+                    self._release_lease(key)
+                    self._srv.send(msgpack.packb(["ok", None], use_bin_type=True))
+                    continue
+                reply = ["ok", None]
                 if op == "get":
-                    obj = self.local.get_blocking(CacheEngineKey.from_string(key))
-                    if obj is not None:
-                        try:
-                            data = self.serde.serialize(obj)
-                        finally:
-                            obj.ref_count_down()
-                self._srv.send(msgpack.packb(["ok", data], use_bin_type=True))
+                    ck = CacheEngineKey.from_string(key)
+                    obj = self.hbm.get_blocking(ck) if self.hbm is not None else None
+                    if obj is not None:  # stays pinned by the lease until released
+                        lease = _uuid.uuid4().hex
+                        with self._lease_lock:
+                            self._leases[lease] = (obj, time.monotonic() +
+                                                   self.config.p2p_pull_pending_ttl)
+                        reply = ["dev", {"off": obj.data_ptr() - self._slab_base,
+                                         "n": obj.get_size(), "shape": list(obj.get_shape()),
+                                         "dtype": str(obj.get_dtype()).removeprefix("torch."),
+                                         "fmt": obj.get_memory_format().name,
+                                         "lease": lease}]
+                    else:
+                        obj = self.local.get_blocking(ck)
+                        if obj is not None:
+                            try:
+                                reply = ["ok", self.serde.serialize(obj)]
+                            finally:
+                                obj.ref_count_down()
+                self._srv.send(msgpack.packb(reply, use_bin_type=True))
             except Exception as e:
                 self._srv.send(msgpack.packb(["err", str(e)], use_bin_type=True))
         self._srv.close()
+
+    def _release_lease(self, lease: str) -> None:
+        with self._lease_lock:
+            ent = self._leases.pop(lease, None)
+        if ent is not None:
+            ent[0].ref_count_down()
+
+    def _expire_leases(self) -> None:
+        now = time.monotonic()
+        with self._lease_lock:
+            dead = [k for k, (_, dl) in self._leases.items() if dl < now]
+        for k in dead:
+            logger.warning("P2P lease %s expired (reader never returned it)", k)
+            self.stats.inc("p2p_lease_expired")
+            self._release_lease(k)
+
+    # ------------------------------------------------- NVLink peer reads
+    def _read_peer_hbm(self, inst: str, desc: dict, meta: dict) -> Optional[MemoryObj]:
+        """Copy a chunk out of a holder's HBM slab (peer mapping, one
+        device-to-device copy over NVLink) into this instance's tier."""
+        from ... import ops
+        from ...parallel.ipc import IpcDesc, PeerMappings
+        from .pd.backend import dtype_from_str
+        from ..memory_management import MemoryFormat
+
+        dest_tier = self.hbm if self.hbm is not None else self.local
+        if self._peer_maps is None:
+            dev = torch.cuda.current_device()
+            self._peer_maps = (PeerMappings(dev), {})
+        maps, bases = self._peer_maps
+        base = bases.get(inst)
+        if base is None:
+            base = bases[inst] = maps.resolve(IpcDesc.from_dict(desc))
+        obj = dest_tier.allocate(torch.Size(meta["shape"]), dtype_from_str(meta["dtype"]),
+                                 MemoryFormat[meta["fmt"]])
+        if obj is None:
+            return None
+        n = int(meta["n"])
+        t = torch.tensor
+        ops.native().layerwise_prefill_dma_copy(t([obj.data_ptr()]), t([base + meta["off"]]),
+                                                t([n]))
+        torch.cuda.current_stream().synchronize()
+        self.stats.inc("p2p_nvlink_bytes", n)
+        return obj
 
     # ------------------------------------------------------- storage API
     def batched_submit_put_task(self, keys: Sequence[CacheEngineKey], objs: Sequence[MemoryObj],
@@ -142,7 +229,9 @@ class P2PBackend(StorageBackendInterface):
     def get_blocking(self, key: CacheEngineKey) -> Optional[MemoryObj]:
         k = key.to_string()
         holders = self._holders(k)[: max(1, self.config.p2p_max_retries)]
-        for inst, url in holders:
+        for inst, ent in holders:
+            url = ent["url"] if isinstance(ent, dict) else ent
+            desc = ent.get("hbm") if isinstance(ent, dict) else None
             s = self.ctx.socket(zmq.REQ)
             s.setsockopt(zmq.LINGER, 0)
             s.setsockopt(zmq.RCVTIMEO, self.timeout_ms)
@@ -151,6 +240,18 @@ class P2PBackend(StorageBackendInterface):
             try:
                 s.send(msgpack.packb(["get", k], use_bin_type=True))
                 st, data = msgpack.unpackb(s.recv(), raw=False)
+                if st == "dev":
+                    obj = None
+                    try:
+                        if desc is not None and torch.cuda.is_available():
+                            obj = self._read_peer_hbm(inst, desc, data)
+                    finally:  # return the lease whether or not the copy happened
+                        s.send(msgpack.packb(["release", data["lease"]], use_bin_type=True))
+                        s.recv()
+                    if obj is not None:
+                        return obj
+                    self.stats.inc("p2p_retries")
+                    continue
             except zmq.Again:
                 logger.warning("P2P peer %s timed out for %s; trying the next holder", inst, k)
                 self.stats.inc("p2p_retries")

@@ -98,3 +98,49 @@ def test_audit_backend_checks_and_keeps_data():
     assert rb.mismatches == 0
     assert eng.remove(tokens, locations=["RemoteBackend"]) == 0  # audit does not remove
     eng.close()
+
+
+import pytest
+
+
+@pytest.mark.gpu
+def test_p2p_reads_peer_hbm_tier():
+    """Both instances keep an HBM tier: B's miss is served by A leasing the
+    chunk in its HBM slab and B copying it over the peer mapping (same GPU
+    here: the same kernels and leases, local addresses); the lease is
+    returned and B then holds the chunk in its own HBM tier."""
+    ctl = P2PController().start()
+
+    def eng(seed, name):
+        kv = make_separate_kv(L, NB, BS, H, D, torch.bfloat16, "cuda", seed=seed)
+        cfg = LMCacheEngineConfig.from_defaults(
+            chunk_size=64, max_local_cpu_size=0.02, local_gpu=True, max_local_gpu_size=0.02,
+            enable_p2p=True, controller_url=ctl.url, p2p_init_ports=[0],
+            blocking_timeout_secs=2.0, lmcache_instance_id=name)
+        md = LMCacheEngineMetadata("m", 1, 0, "vllm", torch.bfloat16)
+        conn = VLLMPagedMemGPUConnector(cfg, kvcaches=kv)
+        return LMCacheEngine(cfg, md, conn), conn, kv
+
+    a, ca, kva = eng(1, "A")
+    b, cb, kvb = eng(2, "B")
+    try:
+        tokens = torch.arange(192)
+        s1 = random_slots(192, NB * BS, seed=3, device="cuda")
+        want = _rows(kva, s1)
+        a.store(tokens, slot_mapping=s1)
+        pa = a.storage_manager.backends["P2PBackend"]
+        assert b.lookup(tokens) == 192
+        s2 = random_slots(192, NB * BS, seed=4, device="cuda")
+        assert bool(b.retrieve(tokens, slot_mapping=s2).all())
+        torch.cuda.synchronize()
+        for x, y in zip(want, _rows(kvb, s2)):
+            assert torch.equal(x, y)
+        pb = b.storage_manager.backends["P2PBackend"]
+        assert pb.stats.counters.get("p2p_nvlink_bytes", 0) > 0
+        assert not pa._leases  # every lease came back
+        bh = b.storage_manager.backends["LocalGPUBackend"]
+        assert len(bh) == 3  # the three chunks now live in B's HBM tier
+    finally:
+        a.close()
+        b.close()
+        ctl.stop()
