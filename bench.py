@@ -517,24 +517,36 @@ def main():
         # to the device (and digests the destination slots for the grant)
         h_src = src_slots.cpu().pin_memory()
         h_dst = dst_slots.cpu().pin_memory()
-        h_status = torch.empty(4, dtype=torch.int64).pin_memory()
+        # each step reads its completion status back (D2H into pinned memory)
+        # and the host checks it one step later, so step i+1's grant overlaps
+        # step i's push on the device
+        h_status = [torch.empty(4, dtype=torch.int64).pin_memory() for _ in range(2)]
+        st_ev = [None, None]
+
+        def check_status(b):
+            if st_ev[b] is not None:
+                st_ev[b].synchronize()
+                if int(h_status[b][0]) != 0:
+                    raise RuntimeError(f"push reported status {h_status[b].tolist()}")
 
         def e2e_step(i):
+            b = hash(i) & 1
+            check_status(b)
             if eng_r is not None:  # the decoder's allocation for this request
                 eng_r.reserve_direct_prefill(f"bench-{i}", h_dst)
             if eng_s is not None:
                 eng_s.store_direct_prefill(slot_mapping=h_src, dst_slot_mapping=h_dst,
                                            req_id=f"bench-{i}")
                 pd = eng_s.storage_manager.backends["PDBackend"]
-                h_status.copy_(pd.push_sender.status.tensor, non_blocking=True)
+                h_status[b].copy_(pd.push_sender.status.tensor, non_blocking=True)
             if eng_r is not None:
                 if not eng_r.wait_direct_prefill(f"bench-{i}", timeout_s=10.0):
                     raise RuntimeError("decoder never granted the push")
                 pd = eng_r.storage_manager.backends["PDBackend"]
-                h_status.copy_(pd.push_receiver.status.tensor, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            if int(h_status[0]) != 0:
-                raise RuntimeError(f"push reported status {h_status.tolist()}")
+                h_status[b].copy_(pd.push_receiver.status.tensor, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            st_ev[b] = ev
 
         for i in range(a.warmup):
             e2e_step(f"w{i}")
@@ -546,6 +558,8 @@ def main():
             e2e_step(i)
         t1.record()
         torch.cuda.synchronize()
+        check_status(0)
+        check_status(1)
         ems = torch.tensor([t0.elapsed_time(t1) / a.steps], device=dev)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)

@@ -271,7 +271,7 @@ struct PieceAt {
   Unit u;      // tokens of the piece (u.n <= 0: an empty trailing piece)
 };
 
-__global__ void __launch_bounds__(kBulkWarps * 32)
+__global__ void __launch_bounds__(kBulkWarps * 32, 6)
     pd_push_bulk_kernel(BulkPushJob j) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int S = kBulkStages;
@@ -301,35 +301,52 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
   const long long first = gw * base + min(static_cast<long long>(gw), extra);
   const long long count = base + (gw < extra ? 1 : 0);
 
-  auto piece_at = [&](long long q) {
-    PieceAt r;
-    const int li = static_cast<int>(q / per_layer);
-    long long rem = q - li * per_layer;
-    int p = 0, ppu = ppu0;
-    if (rem >= static_cast<long long>(tiles) * ppu0) {
-      rem -= static_cast<long long>(tiles) * ppu0;
-      p = 1;
-      ppu = ppu1;
-      if (rem >= static_cast<long long>(tiles) * ppu1) {
-        rem -= static_cast<long long>(tiles) * ppu1;
-        p = 2;
-        ppu = ppu2;
-      }
+  // Position of a piece, advanced one piece at a time (a warp's pieces are
+  // consecutive): layer in launch, plane, tile, piece in the unit.
+  struct Cur {
+    int li, p, tile, pc;
+  };
+  auto ppu_p = [&](int p) { return p == 0 ? ppu0 : (p == 1 ? ppu1 : ppu2); };
+  auto seek = [&](long long q) {  // one division-based decode per warp
+    Cur r;
+    r.li = static_cast<int>(q / per_layer);
+    long long rem = q - r.li * per_layer;
+    r.p = 0;
+    while (r.p < 2 && rem >= static_cast<long long>(tiles) * ppu_p(r.p)) {
+      rem -= static_cast<long long>(tiles) * ppu_p(r.p);
+      ++r.p;
     }
-    const int tile = static_cast<int>(rem / ppu);
-    const int pc = static_cast<int>(rem - static_cast<long long>(tile) * ppu);
-    const int per = piece_tokens(p);
-    const int tend = min(c.num_tokens, (tile + 1) * j.tile_tokens);
-    r.unit = (li * np + p) * tiles + tile;
-    r.layer = li;
-    r.plane = p;
-    r.ppu = ppu;
-    r.last = pc == ppu - 1;
-    r.u.layer = li;
-    r.u.plane = p;
-    r.u.t0 = tile * j.tile_tokens + pc * per;
-    r.u.n = min(per, tend - r.u.t0);
+    const int ppu = ppu_p(r.p);
+    r.tile = static_cast<int>(rem / ppu);
+    r.pc = static_cast<int>(rem - static_cast<long long>(r.tile) * ppu);
     return r;
+  };
+  auto step_cur = [&](Cur &r) {
+    if (++r.pc < ppu_p(r.p)) return;
+    r.pc = 0;
+    if (++r.tile < tiles) return;
+    r.tile = 0;
+    do {  // next plane with pieces, else the next layer's first one
+      if (++r.p >= np) {
+        r.p = 0;
+        ++r.li;
+      }
+    } while (ppu_p(r.p) == 0);
+  };
+  auto piece_of = [&](const Cur &r) {
+    PieceAt a;
+    const int per = piece_tokens(r.p);
+    const int tend = min(c.num_tokens, (r.tile + 1) * j.tile_tokens);
+    a.unit = (r.li * np + r.p) * tiles + r.tile;
+    a.layer = r.li;
+    a.plane = r.p;
+    a.ppu = ppu_p(r.p);
+    a.last = r.pc == a.ppu - 1;
+    a.u.layer = r.li;
+    a.u.plane = r.p;
+    a.u.t0 = r.tile * j.tile_tokens + r.pc * per;
+    a.u.n = min(per, tend - a.u.t0);
+    return a;
   };
 
   if (lane == 0) {
@@ -338,8 +355,10 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
   }
   __syncwarp();
 
+  Cur lcur = seek(first), scur = lcur;  // load and store cursors
   auto issue_loads = [&](long long k) {
-    const PieceAt pa = piece_at(first + k);
+    const PieceAt pa = piece_of(lcur);
+    step_cur(lcur);
     const int s = static_cast<int>(k % S);
     unsigned bytes = 0;
     LaneRuns r;
@@ -417,7 +436,8 @@ __global__ void __launch_bounds__(kBulkWarps * 32)
                                    0);
       break;
     }
-    const PieceAt pa = piece_at(first + k);
+    const PieceAt pa = piece_of(scur);
+    step_cur(scur);
     if (pa.u.n > 0) {
       const LaneRuns r = plan_runs(c, pa.u, lane, c.num_tokens);
       const unsigned rb = plane_of(c.paged, pa.plane).row_bytes;

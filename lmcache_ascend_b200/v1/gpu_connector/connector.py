@@ -492,6 +492,29 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
                 self.load_stream.synchronize()
             yield
             return
+        row0 = objs_per_layer[0] if len(objs_per_layer) else []
+        if self.device.type == "cuda" and row0 and row0[0].raw_data.is_cuda and \
+                self._contiguous_batch(row0, starts, ends):
+            # device-resident chunks (HBM tier): layer l's pointer table is built
+            # when layer l moves, so the tiers are asked for layer l's chunks
+            # only then (the fetches of later layers overlap earlier copies)
+            for layer in range(self.layout.num_layers):
+                row = objs_per_layer[layer]
+                tbl = torch.tensor([o.tensor.data_ptr() for o in row],
+                                   dtype=torch.int64).pin_memory()
+                with torch.cuda.stream(self.load_stream):
+                    self._native_xfer(None, slots[starts[0]:ends[-1]], False,
+                                      chunk_ptrs=tbl.to(self.device, non_blocking=True),
+                                      chunk_tokens=self.config.chunk_size,
+                                      chunk_on_device=True, layer_begin=layer, num_layers=1,
+                                      chunk_layer_begin=0,
+                                      chunk_layout=self._layer_layout_native())
+                torch.cuda.current_stream(self.device).wait_stream(self.load_stream)
+                yield
+            if sync:
+                self.load_stream.synchronize()
+            yield
+            return
         table = self._layer_tables(objs_per_layer, starts, ends, self.load_stream)
         for layer in range(self.layout.num_layers):
             if self.device.type == "cuda":

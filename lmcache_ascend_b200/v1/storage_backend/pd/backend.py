@@ -77,6 +77,7 @@ class PDBackend(SenderMixin, ReceiverMixin, StorageBackendInterface):
         self.ctx = zmq.Context.instance()
         self.timeout_ms = int(config.blocking_timeout_secs * 1000)
         self._lock = threading.RLock()
+        self._req_lock = threading.Lock()
         self._closed = threading.Event()
         self._threads: List[threading.Thread] = []
         self.device = torch.device(config.pd_buffer_device if config.pd_buffer_device != "cuda"
@@ -195,24 +196,36 @@ class PDBackend(SenderMixin, ReceiverMixin, StorageBackendInterface):
         return url
 
     def _req(self, url: str, msg, timeout_ms: Optional[int] = None):
-        s = self.ctx.socket(zmq.REQ)
-        s.setsockopt(zmq.LINGER, 0)
+        """One request/reply with the peer at ``url`` over a REQ socket kept
+        per URL (a new TCP connection per request costs more than the round
+        trip); a timeout discards the socket so the next request starts clean."""
         to = timeout_ms or self.timeout_ms
-        s.setsockopt(zmq.RCVTIMEO, to)
-        s.setsockopt(zmq.SNDTIMEO, to)
-        s.connect(url)
-        try:
-            s.send(M.encode(msg))
-            return M.decode(s.recv())
-        except zmq.Again:
-            raise TimeoutError(f"PD peer at {url} did not answer within {to} ms")
-        finally:
-            s.close()
+        with self._req_lock:
+            socks = self.__dict__.setdefault("_req_socks", {})
+            s = socks.get((url, to))
+            if s is None:
+                s = self.ctx.socket(zmq.REQ)
+                s.setsockopt(zmq.LINGER, 0)
+                s.setsockopt(zmq.RCVTIMEO, to)
+                s.setsockopt(zmq.SNDTIMEO, to)
+                s.connect(url)
+                socks[(url, to)] = s
+            try:
+                s.send(M.encode(msg))
+                return M.decode(s.recv())
+            except zmq.Again:
+                socks.pop((url, to), None)
+                s.close()
+                raise TimeoutError(f"PD peer at {url} did not answer within {to} ms")
 
     def close(self) -> None:
         self._closed.set()
         for t in self._threads:
             t.join(timeout=2)
+        with self._req_lock:
+            for sock in self.__dict__.get("_req_socks", {}).values():
+                sock.close()
+            self.__dict__.get("_req_socks", {}).clear()
         self._close_role()
         if self.push_sender is not None:
             self.push_sender.close()

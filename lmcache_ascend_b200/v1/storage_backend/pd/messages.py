@@ -149,8 +149,8 @@ def slot_digest(slots) -> "tuple[str, int]":
         arr = slots.detach().to("cpu", torch.int64).numpy()
     else:
         arr = np.asarray(list(slots), dtype=np.int64)
-    raw = np.ascontiguousarray(arr.astype("<i8", copy=False)).tobytes()
-    # a consistency check (both ends are trusted), so two fast checksums of
-    # the bytes plus the length suffice: CRC-32 and Adler-32
-    h = f"{zlib.crc32(raw):08x}{zlib.adler32(raw):08x}{arr.size:x}"
-    return h, int(arr.max()) if arr.size else -1
+    a64 = np.ascontiguousarray(arr.astype("<i8", copy=False))
+    # a consistency check (both ends are trusted): CRC-32 of the bytes, the
+    # element sum and the length
+    h = f"{zlib.crc32(memoryview(a64)):08x}{int(a64.sum()) & 0xFFFFFFFFFFFF:012x}{a64.size:x}"
+    return h, int(a64.max()) if a64.size else -1
