@@ -16,20 +16,34 @@ class Admission:
         self.max_sessions, self.max_bytes = max_sessions, max_bytes
         self.sessions = 0
         self.bytes = 0
+        self.admitted = self.waited = self.rejected = 0
         self._cv = threading.Condition()
 
     def acquire(self, nbytes: int, timeout_s: float) -> bool:
         deadline = time.monotonic() + timeout_s
         with self._cv:
+            waited = False
             while self.sessions >= self.max_sessions or (
                     self.sessions > 0 and self.bytes + nbytes > self.max_bytes):
                 left = deadline - time.monotonic()
                 if left <= 0:
+                    self.rejected += 1
                     return False
+                waited = True
                 self._cv.wait(left)
             self.sessions += 1
             self.bytes += nbytes
+            self.admitted += 1
+            self.waited += int(waited)
             return True
+
+    def report(self) -> dict:
+        """Admission state for operators (bounded fields only)."""
+        with self._cv:
+            return {"sessions": self.sessions, "bytes": self.bytes,
+                    "max_sessions": self.max_sessions, "max_bytes": self.max_bytes,
+                    "admitted_total": self.admitted, "waited_total": self.waited,
+                    "rejected_total": self.rejected}
 
     def release(self, nbytes: int) -> None:
         with self._cv:
@@ -60,6 +74,11 @@ class CircuitBreaker:
         with self._lock:
             self._fails.pop(peer, None)
             self._open_until.pop(peer, None)
+
+    def open_peers(self) -> int:
+        with self._lock:
+            now = self.clock()
+            return sum(1 for t in self._open_until.values() if t > now)
 
     def failure(self, peer: str) -> None:
         with self._lock:

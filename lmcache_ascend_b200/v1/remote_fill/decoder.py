@@ -33,6 +33,7 @@ import torch
 import zmq
 
 from ...utils.logging import init_logger
+from .metrics import DecoderMetrics
 
 logger = init_logger(__name__)
 
@@ -90,7 +91,7 @@ class RemoteFillService:
                  deadline_s: float = 10.0, max_window_tokens: int = 4096,
                  on_ready: Optional[Callable[[str, int], None]] = None,
                  on_abort: Optional[Callable[[str, str], None]] = None,
-                 data_plane_desc: Optional[dict] = None):
+                 data_plane_desc: Optional[dict] = None, max_sessions: int = 64):
         self.slot_provider = slot_provider
         self.verifier = verifier or CopyVerifier()
         self.deadline_s = deadline_s
@@ -111,17 +112,42 @@ class RemoteFillService:
         self._stop = threading.Event()
         self._threads = []
         self._open_replies: "OrderedDict[str, list]" = OrderedDict()  # session-less verbs
+        self.metrics = DecoderMetrics()
+        self.max_sessions = max_sessions
 
     @property
     def url(self) -> str:
         return f"tcp://{self.host}:{self.port}"
 
+    token_bytes = 0  # bytes of one token's KV (set by the caller; 0 counts tokens only)
+
+    def metrics_snapshot(self, publish: bool = False) -> dict:
+        snap = self.metrics.snapshot()
+        if publish:
+            self.metrics.publish()
+        return snap
+
     # ------------------------------------------------------------ verbs
+    def _active(self, s: "_Session") -> int:
+        return sum(b - a for a, b in s.windows.values())
+
+    def _retire(self, s: "_Session", published: bool) -> None:
+        m = self.metrics
+        m.add("active_sessions", -1)
+        m.add("active_windows", -len(s.windows))
+        nbytes = self._active(s) * self.token_bytes
+        m.add("active_bytes", -nbytes)
+        m.add("published_bytes_total" if published else "discarded_bytes_total", nbytes)
+
     def _abort(self, sid: str, why: str) -> None:
         s = self.sessions.get(sid)
         if s is None or s.state in (FINISHED, ABORTED):
             return
         s.state = ABORTED
+        self._retire(s, published=False)
+        self.metrics.add("aborted_sessions_total")
+        if why == "deadline expired":
+            self.metrics.add("expired_sessions_total")
         s.armed.clear()
         self.aborted[s.req_id] = why
         logger.warning("remote fill session %s (%s) aborted: %s", sid, s.req_id, why)
@@ -133,11 +159,17 @@ class RemoteFillService:
             return {"version": PROTOCOL_VERSION, "max_window_tokens": self.max_window_tokens,
                     "data_plane": self.data_plane_desc}
         if op == "OPEN":
+            active = sum(1 for x in self.sessions.values() if x.state not in (FINISHED, ABORTED))
+            if active >= self.max_sessions:
+                self.metrics.add("capacity_rejections_total")
+                raise RuntimeError("decoder at its session capacity")
             slots = self.slot_provider(p["req_id"], int(p["num_tokens"]))
             if slots is None or slots.numel() < int(p["num_tokens"]):
+                self.metrics.add("capacity_rejections_total")
                 raise RuntimeError("no destination blocks for the request")
             sid = uuid.uuid4().hex
             self.sessions[sid] = _Session(p["req_id"], int(p["num_tokens"]), slots)
+            self.metrics.add("active_sessions")
             return {"session": sid}
         s = self.sessions.get(sid)
         if s is None:
@@ -155,6 +187,10 @@ class RemoteFillService:
             a, b = int(p["start"]), int(p["end"])
             if not (0 <= a < b <= s.num_tokens) or b - a > self.max_window_tokens:
                 raise ValueError("window outside the request or too large")
+            if w not in s.windows:
+                self.metrics.add("active_windows")
+                self.metrics.add("active_bytes", (b - a) * self.token_bytes)
+                self.metrics.add("reserved_bytes_total", (b - a) * self.token_bytes)
             s.windows[w] = (a, b)
             s.state = RESERVED
             return {"dst_slots": s.slots[a:b].cpu().numpy().astype(np.int64).tobytes()}
@@ -167,6 +203,7 @@ class RemoteFillService:
             if w not in s.armed:
                 raise RuntimeError("window was not armed")
             if not self.verifier.verify(s.armed.pop(w)):
+                self.metrics.add("verify_failures_total")
                 self._abort(sid, f"window {w} failed verification")
                 raise RuntimeError(f"window {w} failed verification")
             s.verified.add(w)
@@ -177,6 +214,8 @@ class RemoteFillService:
                 raise RuntimeError("FINISH before every window was verified")
             covered = sum(b - a for a, b in s.windows.values())
             s.state = FINISHED
+            self._retire(s, published=True)
+            self.metrics.add("finished_sessions_total")
             self.ready[s.req_id] = covered
             if self.on_ready:
                 self.on_ready(s.req_id, covered)

@@ -24,6 +24,7 @@ import zmq
 
 from ...utils.logging import init_logger
 from .coordinator import Admission, CircuitBreaker
+from .metrics import ProducerMetrics, classify
 from .planning import plan_windows
 
 logger = init_logger(__name__)
@@ -84,6 +85,7 @@ class RemoteFillProducer:
         self._sock = None
         self._negotiated: Optional[Dict] = None
         self.results: List[FillResult] = []
+        self.metrics = ProducerMetrics()
 
     # ------------------------------------------------------------- rpc
     def _socket(self):
@@ -122,6 +124,7 @@ class RemoteFillProducer:
     def fill(self, req_id: str, src_slots: torch.Tensor, num_tokens: Optional[int] = None,
              nbytes: int = 0, admit_timeout_s: float = 5.0) -> FillResult:
         n = int(src_slots.numel() if num_tokens is None else num_tokens)
+        self.metrics.submitted(nbytes)
         if not self.breaker.allow(self.url):
             return self._fail(req_id, "circuit open for the decoder", sent_open=None)
         if not self.admission.acquire(nbytes, admit_timeout_s):
@@ -143,6 +146,7 @@ class RemoteFillProducer:
             self.breaker.success(self.url)
             res = FillResult(req_id, True, len(windows), int(done["ready_tokens"]))
             self.results.append(res)
+            self.metrics.outcome("LOCAL_FULL", "none", nbytes)
             return res
         except (RuntimeError, TimeoutError, KeyError, ValueError) as e:
             return self._fail(req_id, str(e), sent_open=session)
@@ -166,7 +170,18 @@ class RemoteFillProducer:
                        "; persistent fallback" if fell_back else "")
         res = FillResult(req_id, False, fell_back=fell_back, reason=reason)
         self.results.append(res)
+        self.metrics.outcome("PERSISTENT_ONLY" if fell_back else "ABORTED", classify(reason))
         return res
+
+    def admission_report(self, publish: bool = False) -> dict:
+        """Admission and breaker state plus the bounded outcome counters."""
+        self.metrics.set_gauge("active_sessions", self.admission.sessions)
+        self.metrics.set_gauge("inflight_bytes", self.admission.bytes)
+        self.metrics.set_gauge("circuit_open_peers", self.breaker.open_peers())
+        rep = {"admission": self.admission.report(), "metrics": self.metrics.snapshot()}
+        if publish:
+            self.metrics.publish()
+        return rep
 
     def status(self, session: str) -> dict:
         return self._rpc("STATUS", session)

@@ -139,3 +139,55 @@ def test_admission_bounds_sessions_and_bytes():
     threading.Timer(0.1, a.release, args=(500,)).start()
     assert a.acquire(60, 1.0)
     a.release(60)
+
+
+def test_metrics_are_bounded_and_track_sessions():
+    """Decoder gauges follow sessions and bytes; producer counters take only
+    fixed outcome/reason labels (an unknown reason counts as "other"); the
+    admission report and the Prometheus export carry the same numbers."""
+    src, dst, table, svc, plane = _pair()
+    svc.token_bytes = 2 * L * H * D * 4
+    try:
+        prod = RemoteFillProducer(svc.url, plane, window_tokens=128, block_size=BS)
+        ss = random_slots(300, NB * BS, seed=9)
+        assert prod.fill("req-m", ss, nbytes=300 * svc.token_bytes).ok
+        snap = svc.metrics_snapshot(publish=True)
+        assert snap["active_sessions"] == 0 and snap["active_bytes"] == 0
+        assert snap["finished_sessions_total"] == 1
+        assert snap["published_bytes_total"] == 300 * svc.token_bytes
+        assert snap["reserved_bytes_total"] == 300 * svc.token_bytes
+        prod.metrics.outcome("ABORTED", "a reason nobody listed")
+        rep = prod.admission_report(publish=True)
+        m = rep["metrics"]
+        assert m["outcome_LOCAL_FULL"] == 1 and m["reason_other"] == 1
+        assert set(k for k in m if k.startswith("reason_")) == \
+            {f"reason_{r}" for r in ("none", "circuit_open", "admission_timeout",
+                                     "open_rejected", "reservation_rejected", "arm_rejected",
+                                     "transfer_failed", "verify_failed", "control_timeout",
+                                     "finish_rejected", "other")}
+        assert rep["admission"]["admitted_total"] == 1 and rep["admission"]["sessions"] == 0
+        try:
+            from prometheus_client import REGISTRY
+
+            v = REGISTRY.get_sample_value(
+                "lmcache_b200_remote_fill_decoder_finished_sessions_total")
+            assert v == 1.0
+        except ImportError:
+            pass
+        prod.close()
+    finally:
+        svc.stop()
+
+
+def test_capacity_rejection_is_counted():
+    src, dst, table, svc, plane = _pair()
+    svc.max_sessions = 0
+    try:
+        prod = RemoteFillProducer(svc.url, plane, window_tokens=128, block_size=BS)
+        res = prod.fill("req-c", random_slots(100, NB * BS, seed=2))
+        assert not res.ok
+        assert svc.metrics_snapshot()["capacity_rejections_total"] == 1
+        assert prod.metrics.snapshot()["reason_open_rejected"] == 1
+        prod.close()
+    finally:
+        svc.stop()
