@@ -146,6 +146,20 @@ class CacheEngineKey:
         return CacheEngineKey(parts[0], parts[1], int(parts[2]), int(parts[3]),
                               int(parts[4], 16), parts[5], group, tuple(tags))
 
+    @classmethod
+    def create(cls, model_name: str, world_size: int, worker_id: int, chunk_hash: int,
+               dtype: Any, tags: Optional[Dict[str, Any]] = None, kv_group: int = 0,
+               fmt: str = "vllm") -> "CacheEngineKey":
+        """Build a key from the argument order of upstream LMCache's
+        ``CacheEngineKey(model_name, world_size, worker_id, chunk_hash, dtype,
+        tags, kv_group=...)`` as the reference calls it (e.g. lmcache_ascend/
+        v1/cache_engine.py:9854, tests/v1/test_shared_cpu_sparse_collective.py
+        :178); ``dtype`` may be a torch dtype or its name."""
+        name = str(dtype).removeprefix("torch.")
+        tag_t = tuple(sorted((str(k), str(v)) for k, v in (tags or {}).items()))
+        return cls(fmt, model_name, int(world_size), int(worker_id),
+                   int(chunk_hash) & 0xFFFFFFFFFFFFFFFF, name, int(kv_group), tag_t)
+
     def with_worker(self, worker_id: int) -> "CacheEngineKey":
         return CacheEngineKey(self.fmt, self.model_name, self.world_size, worker_id,
                               self.chunk_hash, self.dtype, self.group, self.tags)

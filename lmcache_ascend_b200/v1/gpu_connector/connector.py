@@ -178,7 +178,7 @@ class VLLMPagedMemGPUConnector(GPUConnectorInterface):
         self.store_stream.wait_stream(cur)
         with torch.cuda.stream(self.store_stream):
             if (on_device or zero_copy) and self._contiguous_batch(memory_objs, starts, ends):
-                ptrs = torch.tensor([o.tensor.data_ptr() for o in memory_objs],
+                ptrs = torch.tensor([o.data_ptr() for o in memory_objs],
                                     dtype=torch.int64, device=self.device)
                 self._native_xfer(None, slots[starts[0]:ends[-1]], True, chunk_ptrs=ptrs,
                                   chunk_tokens=self.config.chunk_size,
@@ -239,7 +239,7 @@ class VLLMPagedMemGPUConnector(GPUConnectorInterface):
         self.load_stream.wait_stream(cur)
         with torch.cuda.stream(self.load_stream):
             if (on_device or zero_copy) and self._contiguous_batch(memory_objs, starts, ends):
-                ptrs = torch.tensor([o.tensor.data_ptr() for o in memory_objs],
+                ptrs = torch.tensor([o.data_ptr() for o in memory_objs],
                                     dtype=torch.int64, device=self.device)
                 self._native_xfer(None, slots[starts[0]:ends[-1]], False, chunk_ptrs=ptrs,
                                   chunk_tokens=self.config.chunk_size,
@@ -338,7 +338,7 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
             return None
         if not self._contiguous_batch(objs_per_layer[0], starts, ends):
             return None
-        ptrs = torch.tensor([[o.tensor.data_ptr() for o in row] for row in objs_per_layer],
+        ptrs = torch.tensor([[o.data_ptr() for o in row] for row in objs_per_layer],
                             dtype=torch.int64).pin_memory()
         with torch.cuda.stream(stream):
             return ptrs.to(self.device, non_blocking=True)
@@ -500,7 +500,7 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
             # only then (the fetches of later layers overlap earlier copies)
             for layer in range(self.layout.num_layers):
                 row = objs_per_layer[layer]
-                tbl = torch.tensor([o.tensor.data_ptr() for o in row],
+                tbl = torch.tensor([o.data_ptr() for o in row],
                                    dtype=torch.int64).pin_memory()
                 with torch.cuda.stream(self.load_stream):
                     self._native_xfer(None, slots[starts[0]:ends[-1]], False,

@@ -146,12 +146,16 @@ class StorageManager:
         return out
 
     def _promote(self, name: str, key: CacheEngineKey, obj: MemoryObj) -> None:
-        cpu = self.backends.get("LocalCPUBackend")
-        if cpu is None or name == "LocalCPUBackend" or not cpu.store_objects:
+        """A hit in a lower tier is kept in the tier its memory belongs to:
+        host chunks in the CPU tier, device chunks (a peer's HBM chunk copied
+        over NVLink) in the HBM tier."""
+        if obj.raw_data is None or obj.meta.dtype is None:
             return
-        if obj.tensor is None or obj.raw_data is None or obj.raw_data.is_cuda:
+        tier = "LocalGPUBackend" if obj.raw_data.is_cuda else "LocalCPUBackend"
+        dst = self.backends.get(tier)
+        if dst is None or name == tier or not dst.store_objects:
             return
-        cpu.batched_submit_put_task([key], [obj])
+        dst.batched_submit_put_task([key], [obj])
 
     def close(self) -> None:
         for b in reversed(list(self.backends.values())):
