@@ -216,8 +216,7 @@ __global__ void __launch_bounds__(256) cg_cdf_kernel(const uint8_t *__restrict__
           return kWide ? hist[s * kCgChan + col]
                        : (hist[(s >> 1) * kCgChan + col] >> ((s & 1) * 16)) & 0xFFFFu;
         },
-        bins,
-               [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
+        bins, [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
   }
 }
 
@@ -454,10 +453,24 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
     w = (p & 1) ? ((w & 0xFFFFu) | (v << 16)) : ((w & 0xFFFF0000u) | v);
   };
   const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
+  // The table is built from the channel's CDF entries, read kBatch at a time
+  // so that many loads are in flight (the build of a 256-bin table would
+  // otherwise wait on one load per symbol, as long as decoding a stream).
+  constexpr int kBatch = 16;
+  auto for_each_entry = [&](auto &&f) {
+    for (int s0 = 0; s0 < bins; s0 += kBatch) {
+      unsigned ev[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k)
+        ev[k] = s0 + k < bins ? static_cast<unsigned short>(__ldg(cd + s0 + k)) : 0u;
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k)
+        if (s0 + k < bins) f(s0 + k, ev[k]);
+    }
+  };
   if constexpr (kWide) {
     for (int p = 0; p < kCgLut; ++p) lut[p * kDecCh + tid] = 8u << 8;  // symbol 0, 8 bits
-    for (int s = 0; s < bins; ++s) {
-      const unsigned e = static_cast<unsigned short>(__ldg(cd + s));
+    for_each_entry([&](int s, unsigned e) {
       const unsigned ln = e & 0xFu;
       const unsigned st = e & 0xFFF0u;
       if (ln <= 8) {
@@ -469,14 +482,13 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
         const uint32_t bit = 1u << (8 + ((st >> 4) & 0xFu));
         w = (w & 0x80000000u) ? (w | bit) : (0x80000000u | bit | static_cast<unsigned>(s));
       }
-    }
+    });
   }
   const uint32_t dflt = (8u << 8) | ((8u << 8) << 16);  // safe default: symbol 0, 8 bits
   if constexpr (!kWide)
     for (int p = 0; p < kCgLut / 2; ++p) lut[p * kDecCh + tid] = dflt;
   int used = 0;
-  for (int s = 0; s < (kWide ? 0 : bins); ++s) {
-    const unsigned e = static_cast<unsigned short>(__ldg(cd + s));
+  if constexpr (!kWide) for_each_entry([&](int s, unsigned e) {
     const unsigned ln = e & 0xFu;
     const unsigned st = e & 0xFFF0u;
     if (ln <= 8) {
@@ -495,7 +507,7 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
         ++used;
       }
     }
-  }
+  });
   const int c = c0 + tid;
   const size_t idx = static_cast<size_t>(l) * C + c;
   const long long b0 = idx == 0 ? 0 : cum_len[idx - 1];

@@ -98,24 +98,41 @@ class CacheEngineKey:
     group: int = 0  # KV layer group (0 regular/latent, 1 DSA indexer)
     tags: Tuple[Tuple[str, str], ...] = field(default=(), compare=True)
 
-    # Keys are hashed on every dict access of every tier; the hash of the
-    # immutable fields is computed once (a 16k-token layerwise request touches
-    # thousands of keys).
+    # Keys are hashed and compared on every dict access of every tier (a
+    # 16k-token layerwise request touches thousands of keys): the field tuple
+    # and its hash are computed once per key, and equality compares the
+    # cached tuples (the per-layer keys of one chunk share the same tuple).
     def __hash__(self) -> int:
         h = self.__dict__.get("_h")
         if h is None:
-            h = hash(self._fields())
+            h = hash(self._ft())
             object.__setattr__(self, "_h", h)
         return h
+
+    def __eq__(self, other) -> bool:
+        if self is other:
+            return True
+        if other.__class__ is not self.__class__:
+            return NotImplemented
+        a, b = self._ft(), other._ft()
+        return a is b or a == b
 
     def _fields(self) -> tuple:
         return (self.fmt, self.model_name, self.world_size, self.worker_id, self.chunk_hash,
                 self.dtype, self.group, self.tags)
 
-    # str hashes differ between processes: never ship the cached value
+    def _ft(self) -> tuple:
+        t = self.__dict__.get("_t")
+        if t is None:
+            t = self._fields()
+            object.__setattr__(self, "_t", t)
+        return t
+
+    # str hashes differ between processes: never ship the cached values
     def __getstate__(self) -> dict:
         d = dict(self.__dict__)
         d.pop("_h", None)
+        d.pop("_t", None)
         return d
 
     def __setstate__(self, d: dict) -> None:
@@ -166,21 +183,28 @@ class CacheEngineKey:
 
     def split_layers(self, num_layers: int) -> List["LayerCacheEngineKey"]:
         # bypasses the frozen-dataclass __init__ (one object.__setattr__ per
-        # field): a layerwise request builds thousands of these
+        # field): a layerwise request builds thousands of these.  Each layer
+        # key shares this key's field tuple and gets its hash up front.
         base = {f: self.__dict__[f] for f in _KEY_FIELDS}
+        base["_t"] = ft = self._ft()
+        ph = hash(ft)
         out = []
         for i in range(num_layers):
             k = object.__new__(LayerCacheEngineKey)
             d = k.__dict__
             d.update(base)
             d["layer_id"] = i
+            d["_h"] = hash((ph, i))
             out.append(k)
         return out
 
     def layer_key(self, layer_id: int) -> "LayerCacheEngineKey":
         k = object.__new__(LayerCacheEngineKey)
-        k.__dict__.update({f: self.__dict__[f] for f in _KEY_FIELDS})
-        k.__dict__["layer_id"] = layer_id
+        d = k.__dict__
+        d.update({f: self.__dict__[f] for f in _KEY_FIELDS})
+        d["_t"] = ft = self._ft()
+        d["layer_id"] = layer_id
+        d["_h"] = hash((hash(ft), layer_id))
         return k
 
     def __str__(self) -> str:  # pragma: no cover - debugging aid
@@ -193,10 +217,20 @@ class LayerCacheEngineKey(CacheEngineKey):
 
     def __hash__(self) -> int:
         h = self.__dict__.get("_h")
-        if h is None:
-            h = hash(self._fields() + (self.layer_id,))
+        if h is None:  # the value ``split_layers`` assigns
+            h = hash((hash(self._ft()), self.layer_id))
             object.__setattr__(self, "_h", h)
         return h
+
+    def __eq__(self, other) -> bool:
+        if self is other:
+            return True
+        if other.__class__ is not self.__class__:
+            return NotImplemented
+        if self.layer_id != other.layer_id:
+            return False
+        a, b = self._ft(), other._ft()
+        return a is b or a == b
 
     def to_string(self) -> str:
         return super().to_string() + f"@L{self.layer_id}"

@@ -14,6 +14,7 @@ from __future__ import annotations
 import queue
 import threading
 import time
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, Generator, List, Optional, Sequence, Tuple
 
@@ -111,6 +112,10 @@ class _LazyLayers:
         row = self.rows.get(layer)
         if row is None:
             got = self.sm.batched_get([ks[layer] for ks in self.keys])
+            if None not in got:
+                self.owned.extend(got)
+                self.rows[layer] = got
+                return got
             prev = self[layer - 1]
             row = []
             for c, o in enumerate(got):
@@ -228,6 +233,10 @@ class LMCacheEngine:
         self.kv_events = ThreadSafeEventList()
         self._engine_state_lock = threading.RLock()
         self._lookup_pins: Dict[Any, List[CacheEngineKey]] = {}
+        # chunk key -> its per-layer keys, shared by the stores and retrieves
+        # of the same prefix so the tiers' dict lookups hit on identity
+        self._layer_keys: "OrderedDict[CacheEngineKey, list]" = OrderedDict()
+        self._layer_keys_lock = threading.Lock()
         self._healthy = True
         self._closed = False
         # async store worker (reference cache_engine.py:412-421, 3451)
@@ -540,12 +549,29 @@ class LMCacheEngine:
             self.stats.inc("lookup_hit_tokens", end)
             return end
 
+    _LAYER_KEY_MEMO = 2048  # chunks (a 512k-token working set at 256 tokens a chunk)
+
+    def _split(self, key: CacheEngineKey, num_layers: int) -> list:
+        """The per-layer keys of ``key``, memoised (LRU over chunk keys)."""
+        memo = self._layer_keys
+        with self._layer_keys_lock:
+            got = memo.get(key)
+            if got is not None and len(got) == num_layers:
+                memo.move_to_end(key)
+                return got
+        got = key.split_layers(num_layers)
+        with self._layer_keys_lock:
+            memo[key] = got
+            while len(memo) > self._LAYER_KEY_MEMO:
+                memo.popitem(last=False)
+        return got
+
     def _lookup_key(self, key: CacheEngineKey) -> CacheEngineKey:
         """Layerwise stores keep one object per layer: probe the last layer,
         which is written together with the others once the store finished."""
         if self.config.use_layerwise and getattr(self.gpu_connector, "layout", None) is not None:
             L = self.gpu_connector.layout.num_layers
-            return key.layer_key(L - 1)
+            return self._split(key, L)[L - 1]
         return key
 
     def agree_restorable(self, tokens: torch.Tensor) -> bool:
@@ -599,8 +625,9 @@ class LMCacheEngine:
         next(gen, None)  # finish the generator: every layer's bytes are in the objects
         q = self.layerwise_put_queue
         req_id = kwargs.get("req_id", "")
+        split = [self._split(k, L) for _, _, k in chunks]
         for layer in range(L):
-            lkeys = [k.split_layers(L)[layer] for _, _, k in chunks]
+            lkeys = [ks[layer] for ks in split]
             size = sum(o.get_size() for o in per_layer[layer])
             q.admit(size)
             try:
@@ -763,12 +790,15 @@ class LMCacheEngine:
         # the hit: chunks whose last layer is stored (store_layer puts layers
         # in order, so the last layer present means every layer is)
         hit = 0
+        split = []
         for _, _, k in chunks:
-            if sm.contains(k.layer_key(L - 1)) is None:
+            ks = self._split(k, L)
+            if sm.contains(ks[L - 1]) is None:
                 break
+            split.append(ks)
             hit += 1
         chunks = chunks[:hit]
-        layers = _LazyLayers(sm, [k.split_layers(L) for _, _, k in chunks], L)
+        layers = _LazyLayers(sm, split, L)
         if hit:
             hit = layers.prefix_of_layer0()  # layer 0 now; later layers on demand
             chunks = chunks[:hit]

@@ -498,13 +498,15 @@ class VLLMPagedMemLayerwiseGPUConnector(VLLMPagedMemGPUConnector):
             # device-resident chunks (HBM tier): layer l's pointer table is built
             # when layer l moves, so the tiers are asked for layer l's chunks
             # only then (the fetches of later layers overlap earlier copies)
-            for layer in range(self.layout.num_layers):
-                row = objs_per_layer[layer]
-                tbl = torch.tensor([o.data_ptr() for o in row],
-                                   dtype=torch.int64).pin_memory()
+            L = self.layout.num_layers
+            host_tbl = torch.empty(L, len(row0), dtype=torch.int64, pin_memory=True)
+            rows_np = host_tbl.numpy()
+            for layer in range(L):
+                rows_np[layer] = [o.data_ptr() for o in objs_per_layer[layer]]
                 with torch.cuda.stream(self.load_stream):
                     self._native_xfer(None, slots[starts[0]:ends[-1]], False,
-                                      chunk_ptrs=tbl.to(self.device, non_blocking=True),
+                                      chunk_ptrs=host_tbl[layer].to(self.device,
+                                                                    non_blocking=True),
                                       chunk_tokens=self.config.chunk_size,
                                       chunk_on_device=True, layer_begin=layer, num_layers=1,
                                       chunk_layer_begin=0,

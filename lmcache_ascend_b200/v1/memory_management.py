@@ -44,7 +44,7 @@ class MemoryFormat(Enum):
 
 
 def _dtype_size(dtype: torch.dtype) -> int:
-    return torch.empty((), dtype=dtype).element_size()
+    return dtype.itemsize
 
 
 def _numel(shape) -> int:

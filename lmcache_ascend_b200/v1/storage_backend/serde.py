@@ -79,10 +79,11 @@ class CacheGenSerde:
         if obj is None:
             return None
         if self.device.startswith("cuda"):
-            kv = decode_kv_bytes(data, self.device)  # one H2D of the payload
+            # one H2D of the payload; the dequantise writes straight into a
+            # device-resident object (else one copy into the host object)
+            decode_kv_bytes(data, self.device, out=obj.tensor)
         else:
-            kv = decode_kv(CacheGenEncoded.from_bytes(data), self.device)
-        obj.tensor.copy_(kv)
+            obj.tensor.copy_(decode_kv(CacheGenEncoded.from_bytes(data), self.device))
         return obj
 
 
