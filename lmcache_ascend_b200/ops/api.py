@@ -357,6 +357,8 @@ class IndexerC8GroupState:
                 if self.quantized:
                     ptrs.append(s.scales.data_ptr())
             table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+            self._planes = table
+            self._aligned = all(p % 16 == 0 for p in ptrs)
             blk = [C8_BLOCK * self.key_bytes] + ([C8_BLOCK * C8_SCALE_BYTES] if self.quantized
                                                  else [])
             slot = self.row_bytes
@@ -384,6 +386,13 @@ def indexer_c8_transfer_prepared(group: IndexerC8GroupState, packets: Sequence[t
     first (reference csrc/indexer_c8.cpp:126-185, kernel :28-150)."""
     phys = group.states[0].physical_slots(slot_mapping.to(group.device))
     ptrs = torch.tensor([p.data_ptr() for p in packets], dtype=torch.int64, device=group.device)
+    group.native()
+    if packets[0].is_cuda and group._aligned and all(p.data_ptr() % 16 == 0 for p in packets):
+        # device packets: the C8 kernel (slots staged once per chunk, 16-byte
+        # vectors over the key plane, a 2-byte copy per scale)
+        native().c8_copy(group._planes, phys, ptrs, chunk_capacity, group.num_layers,
+                         group.key_bytes, group.states[0].keys.shape[0] * C8_BLOCK, from_gpu)
+        return
     native().kv_transfer(group.native(), None, ptrs, group.chunk_layout(), 0, 0, chunk_capacity,
                          packets[0].is_cuda, phys, 0, 0, group.num_layers, from_gpu,
                          MODE_AUTO if packets[0].is_cuda else MODE_SIMT, None, None, 0, None)

@@ -44,6 +44,21 @@ __device__ __forceinline__ int64_t key_row(const PT *rows, int t) {
   return rows == nullptr ? static_cast<int64_t>(t) : static_cast<int64_t>(rows[t]);
 }
 
+// Rotation by the angle difference, with the contractions fixed so every
+// path (scalar, vector, head-grouped) rounds identically:
+//   cos(n - o) = cn co + sn so,  sin(n - o) = sn co - cn so,
+//   y1 = x1 cd - x2 sd,          y2 = x2 cd + x1 sd.
+__device__ __forceinline__ void rot_delta(float ca, float sa, float cb, float sb, float &cd,
+                                          float &sd) {
+  cd = __fmaf_rn(ca, cb, __fmul_rn(sa, sb));
+  sd = __fmaf_rn(sa, cb, -__fmul_rn(ca, sb));
+}
+__device__ __forceinline__ void rot_apply(float x1, float x2, float cd, float sd, float &y1,
+                                          float &y2) {
+  y1 = __fmaf_rn(x1, cd, -__fmul_rn(x2, sd));
+  y2 = __fmaf_rn(x2, cd, __fmul_rn(x1, sd));
+}
+
 template <typename KT, typename CT, typename PT>
 __global__ void rope_delta_kernel(const PT *__restrict__ old_pos,
                                   const PT *__restrict__ new_pos, KT *key,
@@ -65,15 +80,17 @@ __global__ void rope_delta_kernel(const PT *__restrict__ old_pos,
       const int i = q - h * half;
       const float ca = to_f(cn[i]), sa = to_f(cn[half + i]);
       const float cb = to_f(co[i]), sb = to_f(co[half + i]);
-      const float cd = ca * cb + sa * sb;   // cos(new - old)
-      const float sd = sa * cb - ca * sb;   // sin(new - old)
+      float cd, sd;  // cos / sin (new - old)
+      rot_delta(ca, sa, cb, sb, cd, sd);
       KT *kh = kt + static_cast<int64_t>(h) * head_size;
       const int i1 = neox ? i : 2 * i;
       const int i2 = neox ? i + half : 2 * i + 1;
       const float x1 = to_f(kh[i1]);
       const float x2 = to_f(kh[i2]);
-      kh[i1] = from_f<KT>(x1 * cd - x2 * sd);
-      kh[i2] = from_f<KT>(x2 * cd + x1 * sd);
+      float y1, y2;
+      rot_apply(x1, x2, cd, sd, y1, y2);
+      kh[i1] = from_f<KT>(y1);
+      kh[i2] = from_f<KT>(y2);
     }
   }
 }
@@ -123,6 +140,65 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
     const CT *co = cache + po * rot_dim;
     const CT *cn = cache + pn * rot_dim;
     KT *kt = key + row * key_stride;
+    if (per_head <= 32 && (32 % per_head) == 0 && num_heads <= 4 * (32 / per_head)) {
+      // Lane = (unit g of a head, head group): the rotation by the angle
+      // difference of unit g is formed once and applied to every head of the
+      // lane's group, whose key loads are all issued before the first use.
+      const int g = lane % per_head;
+      const int hg = 32 / per_head;
+      const int i0 = kNeox ? g * VE : g * VE / 2;
+      float ca[NP], sa[NP], cb[NP], sb[NP], cd[NP], sd[NP];
+      load_cs<CT, NP>(cn + i0, ca);
+      load_cs<CT, NP>(cn + half + i0, sa);
+      load_cs<CT, NP>(co + i0, cb);
+      load_cs<CT, NP>(co + half + i0, sb);
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        rot_delta(ca[j], sa[j], cb[j], sb[j], cd[j], sd[j]);
+      }
+      uint4 a[4], b[4];
+      KT *kh[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int h = lane / per_head + k * hg;
+        kh[k] = h < num_heads ? kt + static_cast<int64_t>(h) * head_size : nullptr;
+        if (kh[k] == nullptr) continue;
+        if (kNeox) {
+          a[k] = *reinterpret_cast<const uint4 *>(kh[k] + i0);
+          b[k] = *reinterpret_cast<const uint4 *>(kh[k] + half + i0);
+        } else {
+          a[k] = *reinterpret_cast<const uint4 *>(kh[k] + g * VE);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (kh[k] == nullptr) continue;
+        if (kNeox) {
+          KT *x1 = reinterpret_cast<KT *>(&a[k]);
+          KT *x2 = reinterpret_cast<KT *>(&b[k]);
+#pragma unroll
+          for (int j = 0; j < VE; ++j) {
+            float y1, y2;
+            rot_apply(to_f(x1[j]), to_f(x2[j]), cd[j], sd[j], y1, y2);
+            x1[j] = from_f<KT>(y1);
+            x2[j] = from_f<KT>(y2);
+          }
+          *reinterpret_cast<uint4 *>(kh[k] + i0) = a[k];
+          *reinterpret_cast<uint4 *>(kh[k] + half + i0) = b[k];
+        } else {
+          KT *x = reinterpret_cast<KT *>(&a[k]);
+#pragma unroll
+          for (int j = 0; j < VE / 2; ++j) {
+            float y1, y2;
+            rot_apply(to_f(x[2 * j]), to_f(x[2 * j + 1]), cd[j], sd[j], y1, y2);
+            x[2 * j] = from_f<KT>(y1);
+            x[2 * j + 1] = from_f<KT>(y2);
+          }
+          *reinterpret_cast<uint4 *>(kh[k] + g * VE) = a[k];
+        }
+      }
+      continue;
+    }
     for (int u = lane; u < units; u += 32) {
       const int h = u / per_head;
       const int g = u - h * per_head;
@@ -140,11 +216,11 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
         KT *x2 = reinterpret_cast<KT *>(&b);
 #pragma unroll
         for (int j = 0; j < VE; ++j) {
-          const float cd = ca[j] * cb[j] + sa[j] * sb[j];
-          const float sd = sa[j] * cb[j] - ca[j] * sb[j];
-          const float v1 = to_f(x1[j]), v2 = to_f(x2[j]);
-          x1[j] = from_f<KT>(v1 * cd - v2 * sd);
-          x2[j] = from_f<KT>(v2 * cd + v1 * sd);
+          float cd, sd, y1, y2;
+          rot_delta(ca[j], sa[j], cb[j], sb[j], cd, sd);
+          rot_apply(to_f(x1[j]), to_f(x2[j]), cd, sd, y1, y2);
+          x1[j] = from_f<KT>(y1);
+          x2[j] = from_f<KT>(y2);
         }
         *reinterpret_cast<uint4 *>(kh + i0) = a;
         *reinterpret_cast<uint4 *>(kh + half + i0) = b;
@@ -154,11 +230,11 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
         KT *x = reinterpret_cast<KT *>(&a);
 #pragma unroll
         for (int j = 0; j < VE / 2; ++j) {
-          const float cd = ca[j] * cb[j] + sa[j] * sb[j];
-          const float sd = sa[j] * cb[j] - ca[j] * sb[j];
-          const float v1 = to_f(x[2 * j]), v2 = to_f(x[2 * j + 1]);
-          x[2 * j] = from_f<KT>(v1 * cd - v2 * sd);
-          x[2 * j + 1] = from_f<KT>(v2 * cd + v1 * sd);
+          float cd, sd, y1, y2;
+          rot_delta(ca[j], sa[j], cb[j], sb[j], cd, sd);
+          rot_apply(to_f(x[2 * j]), to_f(x[2 * j + 1]), cd, sd, y1, y2);
+          x[2 * j] = from_f<KT>(y1);
+          x[2 * j + 1] = from_f<KT>(y2);
         }
         *reinterpret_cast<uint4 *>(kh + e0) = a;
       }

@@ -57,6 +57,9 @@ void pd_flag_add(int64_t flag_ptr, int64_t inc);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
+void c8_copy(const at::Tensor &planes, const at::Tensor &phys, const at::Tensor &packets,
+             int64_t cap, int64_t num_layers, int64_t key_bytes, int64_t phys_limit,
+             bool to_packet);
 void cachegen_compact(const at::Tensor &src, const at::Tensor &cap, const at::Tensor &first,
                       const at::Tensor &lengths, const at::Tensor &offsets, at::Tensor &dst);
 at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins);
@@ -183,6 +186,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("output_buffer"), py::arg("output_lengths"),
         py::arg("status") = py::none());
   m.def("decode_fast_prefsum", &decode_fast_prefsum);
+  m.def("c8_copy", &c8_copy);
   m.def("cachegen_compact", &cachegen_compact);
   m.def("cachegen_quantize", &cachegen_quantize, py::arg("x"), py::arg("bins"), py::arg("sym"),
         py::arg("scale"), py::arg("row_dst") = py::none());
