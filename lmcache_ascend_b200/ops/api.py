@@ -375,6 +375,21 @@ class IndexerC8GroupState:
         self.native()
         return self._chunk
 
+    def packet_table(self, addrs: List[int]) -> torch.Tensor:
+        """Device int64 table of packet addresses, uploaded without a host
+        synchronisation (pinned source) and kept for repeated packet sets."""
+        key = tuple(addrs)
+        cache = self.__dict__.setdefault("_packet_tables", {})
+        t = cache.get(key)
+        if t is None:
+            if len(cache) >= 64:
+                cache.clear()
+            host = torch.tensor(addrs, dtype=torch.int64)
+            if self.device.type == "cuda":
+                host = host.pin_memory()
+            t = cache[key] = host.to(self.device, non_blocking=True)
+        return t
+
 
 def indexer_c8_transfer_prepared(group: IndexerC8GroupState, packets: Sequence[torch.Tensor],
                                  slot_mapping: torch.Tensor, chunk_capacity: int,
@@ -384,15 +399,22 @@ def indexer_c8_transfer_prepared(group: IndexerC8GroupState, packets: Sequence[t
     packet t // capacity).  Runs of contiguous slots move as single copies;
     the logical -> physical slot map (factor / block permutation) is applied
     first (reference csrc/indexer_c8.cpp:126-185, kernel :28-150)."""
-    phys = group.states[0].physical_slots(slot_mapping.to(group.device))
-    ptrs = torch.tensor([p.data_ptr() for p in packets], dtype=torch.int64, device=group.device)
     group.native()
-    if packets[0].is_cuda and group._aligned and all(p.data_ptr() % 16 == 0 for p in packets):
-        # device packets: the C8 kernel (slots staged once per chunk, 16-byte
-        # vectors over the key plane, a 2-byte copy per scale)
-        native().c8_copy(group._planes, phys, ptrs, chunk_capacity, group.num_layers,
-                         group.key_bytes, group.states[0].keys.shape[0] * C8_BLOCK, from_gpu)
+    addrs = [p.data_ptr() for p in packets]
+    if packets[0].is_cuda and group._aligned and all(a % 16 == 0 for a in addrs):
+        # device packets: the C8 kernel maps the logical slots itself, stages
+        # them once per chunk, and moves 16-byte vectors over the key plane
+        # and a 2-byte copy per scale; one launch, no host synchronisation
+        s0 = group.states[0]
+        slots = slot_mapping.to(group.device, non_blocking=True)
+        if slots.dtype not in (torch.int32, torch.int64):
+            slots = slots.long()
+        native().c8_copy(group._planes, slots, group.packet_table(addrs), chunk_capacity,
+                         group.num_layers, group.key_bytes, s0.slot_factor, s0.block_map,
+                         s0.cache_slots, s0.keys.shape[0] * C8_BLOCK, from_gpu)
         return
+    phys = group.states[0].physical_slots(slot_mapping.to(group.device))
+    ptrs = torch.tensor(addrs, dtype=torch.int64, device=group.device)
     native().kv_transfer(group.native(), None, ptrs, group.chunk_layout(), 0, 0, chunk_capacity,
                          packets[0].is_cuda, phys, 0, 0, group.num_layers, from_gpu,
                          MODE_AUTO if packets[0].is_cuda else MODE_SIMT, None, None, 0, None)

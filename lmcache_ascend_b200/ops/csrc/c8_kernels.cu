@@ -26,6 +26,7 @@ namespace lmc {
 namespace {
 
 constexpr int kC8Threads = 256;
+constexpr int64_t kC8Block = 128;  // tokens per C8 cache block
 constexpr int kC8Unroll = 8;
 
 // One layer's key plane of one chunk in units of V (uint4, or 2 bytes for a
@@ -62,21 +63,38 @@ __device__ __forceinline__ void c8_keys(uint8_t *kc, uint8_t *kp, const int64_t 
   }
 }
 
+// Logical slot -> physical slot of the C8 cache (reference
+// csrc/indexer_c8.cpp:12-45): with a block map, block b lives at physical
+// block map[b]; otherwise at b * factor.  Slots outside the logical capacity,
+// or mapped outside the physical cache, give -1 (skipped).
+struct C8SlotMap {
+  const int32_t *block_map;  // [logical blocks] or null
+  int64_t cache_slots;       // logical capacity
+  int64_t phys_limit;        // physical slots
+  int factor;                // 1 or 2
+  __device__ __forceinline__ int64_t operator()(int64_t s) const {
+    if (s < 0 || s >= cache_slots) return -1;
+    const int64_t b = s / kC8Block, r = s - b * kC8Block;
+    const int64_t p = block_map != nullptr ? static_cast<int64_t>(block_map[b]) * kC8Block + r
+                                           : b * factor * kC8Block + r;
+    return (p >= 0 && p < phys_limit) ? p : -1;
+  }
+};
+
+template <typename ST>
 __global__ void __launch_bounds__(kC8Threads) c8_copy_kernel(
     const int64_t *__restrict__ planes,   // [L][P] cache base pointers (keys, scales)
-    const int64_t *__restrict__ phys,     // [n] physical slot per token, -1 = skip
+    const ST *__restrict__ slots,         // [n] logical slot per token
     const int64_t *__restrict__ packets,  // [chunks] packet base pointers
-    int n, int cap, int L, int layers_per_cta, int key_bytes, int P, int64_t phys_limit,
+    C8SlotMap map, int n, int cap, int L, int layers_per_cta, int key_bytes, int P,
     bool to_packet) {
   extern __shared__ int64_t c8_slots[];
   const int chunk = blockIdx.x;
   const int t0 = chunk * cap;
   const int cnt = min(cap, n - t0);  // a packet holds its own token count
   if (cnt <= 0) return;
-  for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
-    const int64_t p = phys[t0 + t];
-    c8_slots[t] = (p >= 0 && p < phys_limit) ? p : -1;  // bad slots are skipped
-  }
+  for (int t = threadIdx.x; t < cnt; t += blockDim.x)
+    c8_slots[t] = map(static_cast<int64_t>(slots[t0 + t]));
   __syncthreads();
   const int l0 = blockIdx.y * layers_per_cta;
   const int l1 = min(L, l0 + layers_per_cta);
@@ -107,29 +125,42 @@ __global__ void __launch_bounds__(kC8Threads) c8_copy_kernel(
 }  // namespace
 
 // planes: device int64 [L * P] (P = 2: keys and scales of each layer, P = 1:
-// keys only); phys: device int64 [n]; packets: device int64 [ceil(n / cap)];
-// phys_limit: physical slots of the cache (larger slots are skipped).  Every
-// base pointer must be 16-byte aligned (the caller checks and otherwise takes
-// the general copy engine); packet p holds min(cap, n - p cap) tokens.
-void c8_copy(const at::Tensor &planes, const at::Tensor &phys, const at::Tensor &packets,
-             int64_t cap, int64_t num_layers, int64_t key_bytes, int64_t phys_limit,
-             bool to_packet) {
-  TORCH_CHECK(planes.is_cuda() && phys.is_cuda() && packets.is_cuda(),
+// keys only); slots: device int32/int64 [n] logical slots; packets: device
+// int64 [ceil(n / cap)]; block_map: optional device int32 [logical blocks];
+// cache_slots: logical capacity; phys_limit: physical slots.  Every base
+// pointer must be 16-byte aligned (the caller checks and otherwise takes the
+// general copy engine); packet p holds min(cap, n - p cap) tokens.
+void c8_copy(const at::Tensor &planes, const at::Tensor &slots, const at::Tensor &packets,
+             int64_t cap, int64_t num_layers, int64_t key_bytes, int64_t factor,
+             const c10::optional<at::Tensor> &block_map, int64_t cache_slots,
+             int64_t phys_limit, bool to_packet) {
+  TORCH_CHECK(planes.is_cuda() && slots.is_cuda() && packets.is_cuda(),
               "c8_copy: pointer tables and slots must be device tensors");
-  TORCH_CHECK(planes.scalar_type() == at::kLong && phys.scalar_type() == at::kLong &&
-                  packets.scalar_type() == at::kLong,
-              "c8_copy: int64 tables");
+  TORCH_CHECK(planes.scalar_type() == at::kLong && packets.scalar_type() == at::kLong,
+              "c8_copy: int64 pointer tables");
+  TORCH_CHECK(slots.scalar_type() == at::kLong || slots.scalar_type() == at::kInt,
+              "c8_copy: int32 or int64 slots");
   TORCH_CHECK(key_bytes > 0 && key_bytes % 16 == 0, "c8_copy: key rows of 16-byte multiples");
   TORCH_CHECK(cap > 0 && cap <= 8192, "c8_copy: 1 <= capacity <= 8192 tokens");
+  TORCH_CHECK(factor == 1 || factor == 2, "c8_copy: block factor 1 or 2");
   TORCH_CHECK(num_layers > 0 && planes.numel() % num_layers == 0, "c8_copy: plane table");
   const int P = static_cast<int>(planes.numel() / num_layers);
   TORCH_CHECK(P == 1 || P == 2, "c8_copy: one or two planes per layer");
-  const int64_t n = phys.numel();
+  const int64_t n = slots.numel();
   const int64_t chunks = (n + cap - 1) / cap;
   TORCH_CHECK(packets.numel() >= chunks, "c8_copy: fewer packets than chunks");
+  C8SlotMap map{nullptr, cache_slots, phys_limit, static_cast<int>(factor)};
+  at::Tensor bm;
+  if (block_map.has_value()) {
+    bm = block_map->contiguous();
+    TORCH_CHECK(bm.is_cuda() && bm.scalar_type() == at::kInt &&
+                    bm.numel() * kC8Block >= cache_slots,
+                "c8_copy: block map must be device int32 covering the logical blocks");
+    map.block_map = bm.data_ptr<int32_t>();
+  }
   if (n == 0) return;
-  const c10::cuda::CUDAGuard guard(phys.device());
-  auto pl = planes.contiguous(), ph = phys.contiguous(), pk = packets.contiguous();
+  const c10::cuda::CUDAGuard guard(slots.device());
+  auto pl = planes.contiguous(), sl = slots.contiguous(), pk = packets.contiguous();
   int dev = 0, sms = 148;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -141,15 +172,19 @@ void c8_copy(const at::Tensor &planes, const at::Tensor &phys, const at::Tensor 
   const int lpc = static_cast<int>((num_layers + groups - 1) / groups);
   const int gy = static_cast<int>((num_layers + lpc - 1) / lpc);
   const size_t smem = static_cast<size_t>(cap) * sizeof(int64_t);
-  if (smem > 48 * 1024)
-    C10_CUDA_CHECK(cudaFuncSetAttribute(c8_copy_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)));
   dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(gy));
-  c8_copy_kernel<<<grid, kC8Threads, smem, at::cuda::getCurrentCUDAStream().stream()>>>(
-      pl.data_ptr<int64_t>(), ph.data_ptr<int64_t>(), pk.data_ptr<int64_t>(),
-      static_cast<int>(n), static_cast<int>(cap), static_cast<int>(num_layers), lpc,
-      static_cast<int>(key_bytes), P, phys_limit, to_packet);
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  auto launch = [&](auto *kernel, const auto *sp) {
+    if (smem > 48 * 1024)
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem)));
+    kernel<<<grid, kC8Threads, smem, stream>>>(
+        pl.data_ptr<int64_t>(), sp, pk.data_ptr<int64_t>(), map, static_cast<int>(n),
+        static_cast<int>(cap), static_cast<int>(num_layers), lpc, static_cast<int>(key_bytes),
+        P, to_packet);
+  };
+  if (sl.scalar_type() == at::kLong) launch(c8_copy_kernel<int64_t>, sl.data_ptr<int64_t>());
+  else launch(c8_copy_kernel<int32_t>, sl.data_ptr<int32_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -121,7 +121,7 @@ __device__ __forceinline__ void load_cs(const CT *p, float (&o)[N]) {
 // adjacent (2p, 2p + 1) pairs.  Same arithmetic as rope_delta_kernel, so both
 // paths give identical results.
 template <typename KT, typename CT, typename PT, bool kNeox>
-__global__ void __launch_bounds__(256) rope_delta_vec_kernel(
+__global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
     const PT *__restrict__ old_pos, const PT *__restrict__ new_pos, KT *key,
     const CT *__restrict__ cache, int num_tokens, int num_heads, int head_size, int rot_dim,
     int64_t key_stride, const PT *rows) {
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
     const CT *co = cache + po * rot_dim;
     const CT *cn = cache + pn * rot_dim;
     KT *kt = key + row * key_stride;
-    if (per_head <= 32 && (32 % per_head) == 0 && num_heads <= 4 * (32 / per_head)) {
+    if (per_head <= 32 && (32 % per_head) == 0) {
       // Lane = (unit g of a head, head group): the rotation by the angle
       // difference of unit g is formed once and applied to every head of the
       // lane's group, whose key loads are all issued before the first use.
@@ -156,45 +156,49 @@ __global__ void __launch_bounds__(256) rope_delta_vec_kernel(
       for (int j = 0; j < NP; ++j) {
         rot_delta(ca[j], sa[j], cb[j], sb[j], cd[j], sd[j]);
       }
-      uint4 a[4], b[4];
-      KT *kh[4];
+      // two heads of the lane's group at a time: their four key loads are in
+      // flight together, and the register count leaves room for 3 CTAs/SM
+      for (int hb = lane / per_head; hb < num_heads; hb += 2 * hg) {
+        uint4 a[2], b[2];
+        KT *kh[2];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int h = lane / per_head + k * hg;
-        kh[k] = h < num_heads ? kt + static_cast<int64_t>(h) * head_size : nullptr;
-        if (kh[k] == nullptr) continue;
-        if (kNeox) {
-          a[k] = *reinterpret_cast<const uint4 *>(kh[k] + i0);
-          b[k] = *reinterpret_cast<const uint4 *>(kh[k] + half + i0);
-        } else {
-          a[k] = *reinterpret_cast<const uint4 *>(kh[k] + g * VE);
+        for (int k = 0; k < 2; ++k) {
+          const int h = hb + k * hg;
+          kh[k] = h < num_heads ? kt + static_cast<int64_t>(h) * head_size : nullptr;
+          if (kh[k] == nullptr) continue;
+          if (kNeox) {
+            a[k] = *reinterpret_cast<const uint4 *>(kh[k] + i0);
+            b[k] = *reinterpret_cast<const uint4 *>(kh[k] + half + i0);
+          } else {
+            a[k] = *reinterpret_cast<const uint4 *>(kh[k] + g * VE);
+          }
         }
-      }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (kh[k] == nullptr) continue;
-        if (kNeox) {
-          KT *x1 = reinterpret_cast<KT *>(&a[k]);
-          KT *x2 = reinterpret_cast<KT *>(&b[k]);
+        for (int k = 0; k < 2; ++k) {
+          if (kh[k] == nullptr) continue;
+          if (kNeox) {
+            KT *x1 = reinterpret_cast<KT *>(&a[k]);
+            KT *x2 = reinterpret_cast<KT *>(&b[k]);
 #pragma unroll
-          for (int j = 0; j < VE; ++j) {
-            float y1, y2;
-            rot_apply(to_f(x1[j]), to_f(x2[j]), cd[j], sd[j], y1, y2);
-            x1[j] = from_f<KT>(y1);
-            x2[j] = from_f<KT>(y2);
+            for (int j = 0; j < VE; ++j) {
+              float y1, y2;
+              rot_apply(to_f(x1[j]), to_f(x2[j]), cd[j], sd[j], y1, y2);
+              x1[j] = from_f<KT>(y1);
+              x2[j] = from_f<KT>(y2);
+            }
+            *reinterpret_cast<uint4 *>(kh[k] + i0) = a[k];
+            *reinterpret_cast<uint4 *>(kh[k] + half + i0) = b[k];
+          } else {
+            KT *x = reinterpret_cast<KT *>(&a[k]);
+#pragma unroll
+            for (int j = 0; j < VE / 2; ++j) {
+              float y1, y2;
+              rot_apply(to_f(x[2 * j]), to_f(x[2 * j + 1]), cd[j], sd[j], y1, y2);
+              x[2 * j] = from_f<KT>(y1);
+              x[2 * j + 1] = from_f<KT>(y2);
+            }
+            *reinterpret_cast<uint4 *>(kh[k] + g * VE) = a[k];
           }
-          *reinterpret_cast<uint4 *>(kh[k] + i0) = a[k];
-          *reinterpret_cast<uint4 *>(kh[k] + half + i0) = b[k];
-        } else {
-          KT *x = reinterpret_cast<KT *>(&a[k]);
-#pragma unroll
-          for (int j = 0; j < VE / 2; ++j) {
-            float y1, y2;
-            rot_apply(to_f(x[2 * j]), to_f(x[2 * j + 1]), cd[j], sd[j], y1, y2);
-            x[2 * j] = from_f<KT>(y1);
-            x[2 * j + 1] = from_f<KT>(y2);
-          }
-          *reinterpret_cast<uint4 *>(kh[k] + g * VE) = a[k];
         }
       }
       continue;

@@ -57,9 +57,10 @@ void pd_flag_add(int64_t flag_ptr, int64_t inc);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
-void c8_copy(const at::Tensor &planes, const at::Tensor &phys, const at::Tensor &packets,
-             int64_t cap, int64_t num_layers, int64_t key_bytes, int64_t phys_limit,
-             bool to_packet);
+void c8_copy(const at::Tensor &planes, const at::Tensor &slots, const at::Tensor &packets,
+             int64_t cap, int64_t num_layers, int64_t key_bytes, int64_t factor,
+             const c10::optional<at::Tensor> &block_map, int64_t cache_slots,
+             int64_t phys_limit, bool to_packet);
 void cachegen_compact(const at::Tensor &src, const at::Tensor &cap, const at::Tensor &first,
                       const at::Tensor &lengths, const at::Tensor &offsets, at::Tensor &dst);
 at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins);
