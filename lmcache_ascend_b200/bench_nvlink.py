@@ -10,7 +10,10 @@ into GPU j's HBM:
   8 MiB (what a peer copy of the same bytes costs without any SM);
 * ``push_bulk`` / ``push_simt``: this repo's push kernel (TMA bulk stores or
   16-byte SIMT stores through the peer address), block-table gather on the
-  source side included.
+  source side included;
+* ``pull_bulk`` / ``pull_simt``: the same kernel launched on the receiving
+  GPU, loading the sender's rows through the peer address (TMA bulk loads
+  without multicast, or 16-byte loads) and storing them locally.
 
 Pairs are timed alone (0 -> 1) and all at once (i -> i + N/2 for every i,
 the pairing of ``bench.py``), each with CUDA events on the source GPU's
@@ -66,11 +69,12 @@ def main() -> None:
         t = torch.arange(T)
         slots[d] = (blocks[t // BS] * BS + t % BS).to(torch.int32).to(dev)
 
-    def dst_layout_on(src_dev: int, dst_dev: int):
-        lay = layouts[dst_dev]
+    def layout_seen_from(run_dev: int, owner: int):
+        """``owner``'s paged cache described on ``run_dev`` (peer addresses)."""
+        lay = layouts[owner]
         es = lay.elem_size
-        ptrs = torch.tensor([t.data_ptr() for layer in caches[dst_dev] for t in layer],
-                            dtype=torch.int64, device=torch.device("cuda", src_dev))
+        ptrs = torch.tensor([t.data_ptr() for layer in caches[owner] for t in layer],
+                            dtype=torch.int64, device=torch.device("cuda", run_dev))
         nat = mod.PagedLayout(ptrs, [p.views[0].stride(0) * es for p in lay.planes],
                               [p.views[0].stride(1) * es for p in lay.planes], lay.row_bytes,
                               lay.block_size, lay.num_slots, [], [])
@@ -78,6 +82,7 @@ def main() -> None:
         return nat
 
     def make_op(kind, i, k):
+        """(device that launches, op) moving GPU i's planes into GPU k's."""
         if kind == "ce":
             plane = T * H * D * 2
             dsts = torch.tensor([t.data_ptr() for layer in caches[k] for t in layer],
@@ -85,16 +90,23 @@ def main() -> None:
             srcs = torch.tensor([t.data_ptr() for layer in caches[i] for t in layer],
                                 dtype=torch.int64)
             sizes = torch.full((dsts.numel(),), plane, dtype=torch.int64)
-            return lambda: mod.layerwise_prefill_dma_copy(dsts, srcs, sizes)
-        dst = dst_layout_on(i, k)
-        mode = 1 if kind == "push_bulk" else 2
-        src = layouts[i].native()
-        cnt = torch.zeros(1 << 16, dtype=torch.int32, device=torch.device("cuda", i))
-        return lambda: mod.pd_push(src, dst, slots[i], slots[k], 0, L, 1, [], 512, 0, None,
-                                   mode, cnt)
+            return i, lambda: mod.layerwise_prefill_dma_copy(dsts, srcs, sizes)
+        mode = 1 if kind.endswith("bulk") else 2
+        if kind.startswith("pull"):
+            # the receiver's SMs load the sender's rows through the peer
+            # mapping and store them locally
+            src, dst, run_dev = layout_seen_from(k, i), layouts[k].native(), k
+            ss = slots[i].to(torch.device("cuda", k))
+            ds = slots[k]
+        else:
+            src, dst, run_dev = layouts[i].native(), layout_seen_from(i, k), i
+            ss, ds = slots[i], slots[k].to(torch.device("cuda", i))
+        cnt = torch.zeros(1 << 16, dtype=torch.int32, device=torch.device("cuda", run_dev))
+        return run_dev, lambda: mod.pd_push(src, dst, ss, ds, 0, L, 1, [], 512, 0, None,
+                                            mode, cnt)
 
     def run(kind, pairs):
-        ops_ = [(i, make_op(kind, i, k)) for i, k in pairs]
+        ops_ = [make_op(kind, i, k) for i, k in pairs]
         for _ in range(a.warmup):
             for i, f in ops_:
                 with torch.cuda.device(i):
@@ -126,7 +138,7 @@ def main() -> None:
     if n >= 4:
         cases.append((f"all_{half}_pairs", [(i, i + half) for i in range(half)]))
     for name, pairs in cases:
-        for kind in ("ce", "push_bulk", "push_simt"):
+        for kind in ("ce", "push_bulk", "push_simt", "pull_bulk", "pull_simt"):
             ms = run(kind, pairs)
             print(json.dumps({"probe": "nvlink", "case": name, "kind": kind, "gpus": n,
                               "pairs": len(pairs), "ms": round(ms, 4),

@@ -209,7 +209,10 @@ class PushSender:
       needs 16-byte aligned, contiguous (token-major) rows on both sides;
     * "simt": 16-byte vector loads and stores per lane; any row layout,
       including head-major segmented rows;
-    * "auto" (default): "bulk" when both layouts allow it, else "simt".
+    * "auto" (default): through a peer mapping (the decoder on another GPU)
+      "simt", which moved 703.8 GB/s per pair against 688.8 for "bulk" on
+      the same B200 pair; on this GPU "bulk" when both layouts allow it
+      (0.79 against 0.64 of HBM for "simt"), else "simt".
     """
 
     def __init__(self, layout: PagedKVLayout, engine: str = "auto"):
@@ -251,6 +254,12 @@ class PushSender:
         self._dst.set_bases_aligned(all(p % 16 == 0 for p in ptrs))
         self._flag_ptrs = [self.peers.resolve(IpcDesc.from_dict(r.flags)) for r in receivers]
         self.replicas = len(receivers)
+        try:
+            here = mod.get_gpu_pci_bus_id(self.device.index or 0)
+        except Exception:  # pragma: no cover - no bus id: treat as local
+            here = ""
+        self._remote = bool(here) and any(
+            IpcDesc.from_dict(r.flags).pci_bus_id not in ("", here) for r in receivers)
         self._fp8 = None
         self._fp8_seq, self._fp8_buf = 0, 0
         if r0.fp8_q is not None and len(receivers) == 1:
@@ -303,8 +312,13 @@ class PushSender:
                                          device=self.device)
         ops.native().pd_push(self.layout.native(), self._dst, src_slots, dst_slots,
                              layer_begin, nl, self.replicas, self._flag_ptrs, tile_tokens,
-                             grid, self.status.tensor, _ENGINES[self.engine], self._counters)
+                             grid, self.status.tensor, self._mode(), self._counters)
         self._mark_pushed()
+
+    def _mode(self) -> int:
+        if self.engine == "auto" and getattr(self, "_remote", False):
+            return _ENGINES["simt"]
+        return _ENGINES[self.engine]
 
     def _mark_pushed(self) -> None:
         if self._last_push is None:
