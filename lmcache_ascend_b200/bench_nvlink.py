@@ -46,6 +46,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--grid", type=int, default=0, help="push CTAs (0: the kernel's default)")
+    ap.add_argument("--kinds", default="ce,push_bulk,push_simt,pull_bulk,pull_simt")
     a = ap.parse_args()
     n = torch.cuda.device_count()
     if n < 2:
@@ -102,7 +104,7 @@ def main() -> None:
             src, dst, run_dev = layouts[i].native(), layout_seen_from(i, k), i
             ss, ds = slots[i], slots[k].to(torch.device("cuda", i))
         cnt = torch.zeros(1 << 16, dtype=torch.int32, device=torch.device("cuda", run_dev))
-        return run_dev, lambda: mod.pd_push(src, dst, ss, ds, 0, L, 1, [], 512, 0, None,
+        return run_dev, lambda: mod.pd_push(src, dst, ss, ds, 0, L, 1, [], 512, a.grid, None,
                                             mode, cnt)
 
     def run(kind, pairs):
@@ -138,9 +140,10 @@ def main() -> None:
     if n >= 4:
         cases.append((f"all_{half}_pairs", [(i, i + half) for i in range(half)]))
     for name, pairs in cases:
-        for kind in ("ce", "push_bulk", "push_simt", "pull_bulk", "pull_simt"):
+        for kind in a.kinds.split(","):
             ms = run(kind, pairs)
             print(json.dumps({"probe": "nvlink", "case": name, "kind": kind, "gpus": n,
+                              "grid": a.grid,
                               "pairs": len(pairs), "ms": round(ms, 4),
                               "gbps_per_pair": round(moved / ms / 1e6, 1),
                               "bytes_per_pair": moved}), flush=True)

@@ -168,14 +168,11 @@ __device__ __forceinline__ int cg_hcol(int c) { return (c >> 2) | ((c & 3) << 5)
 // Counters: 16-bit halves of 32-bit words, [bins / 2][kCgChan] words, when
 // T < 65536 (half the shared memory: 256 bins fit 3 blocks per SM); 32-bit
 // counters [bins][kCgChan] otherwise (kWide).
+// Histogram of one (layer, 128-channel tile) into shared memory.
 template <bool kWide>
-__global__ void __launch_bounds__(256) cg_cdf_kernel(const uint8_t *__restrict__ in,
-                                                     int16_t *out, int L, int T, int C,
-                                                     int bins, bool vec4) {
-  extern __shared__ unsigned hist[];
-  const int l = blockIdx.y;
-  const int c0 = blockIdx.x * kCgChan;
-  const int nc = min(kCgChan, C - c0);
+__device__ __forceinline__ void cg_histogram(const uint8_t *__restrict__ in, unsigned *hist,
+                                             int l, int T, int C, int c0, int nc, int bins,
+                                             bool vec4) {
   const int words = (kWide ? bins : (bins + 1) >> 1) * kCgChan;
   for (int i = threadIdx.x; i < words; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -208,16 +205,63 @@ __global__ void __launch_bounds__(256) cg_cdf_kernel(const uint8_t *__restrict__
     }
   }
   __syncthreads();
+}
+
+template <bool kWide>
+__device__ __forceinline__ unsigned cg_hist_count(const unsigned *hist, int s, int col) {
+  return kWide ? hist[s * kCgChan + col]
+               : (hist[(s >> 1) * kCgChan + col] >> ((s & 1) * 16)) & 0xFFFFu;
+}
+
+// Fused form (few bins): histogram, then the assignment by one thread per
+// channel from shared memory.
+template <bool kWide>
+__global__ void __launch_bounds__(256) cg_cdf_kernel(const uint8_t *__restrict__ in,
+                                                     int16_t *out, int L, int T, int C,
+                                                     int bins, bool vec4) {
+  extern __shared__ unsigned hist[];
+  const int l = blockIdx.y;
+  const int c0 = blockIdx.x * kCgChan;
+  const int nc = min(kCgChan, C - c0);
+  cg_histogram<kWide>(in, hist, l, T, C, c0, nc, bins, vec4);
   if (threadIdx.x < nc) {
     const int col = cg_hcol(threadIdx.x);
     int16_t *o = out + (static_cast<size_t>(l) * C + c0 + threadIdx.x) * (bins + 1);
-    cdf_assign(
-        [&](int s) {
-          return kWide ? hist[s * kCgChan + col]
-                       : (hist[(s >> 1) * kCgChan + col] >> ((s & 1) * 16)) & 0xFFFFu;
-        },
-        bins, [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
+    cdf_assign([&](int s) { return cg_hist_count<kWide>(hist, s, col); }, bins,
+               [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
   }
+}
+
+// Split form (many bins): the histogram tables of 256 bins leave room for
+// only 3 blocks per SM, and the serial assignment then runs on 12 warps per
+// SM.  Here the histogram goes to global memory as counts[L][bins][C]
+// (coalesced over channels), and the assignment runs as its own kernel with
+// one thread per (layer, channel), no shared memory and full occupancy.
+template <bool kWide>
+__global__ void __launch_bounds__(256) cg_hist_kernel(const uint8_t *__restrict__ in,
+                                                      uint32_t *counts, int L, int T, int C,
+                                                      int bins, bool vec4) {
+  extern __shared__ unsigned hist[];
+  const int l = blockIdx.y;
+  const int c0 = blockIdx.x * kCgChan;
+  const int nc = min(kCgChan, C - c0);
+  cg_histogram<kWide>(in, hist, l, T, C, c0, nc, bins, vec4);
+  uint32_t *cl = counts + static_cast<size_t>(l) * bins * C + c0;
+  for (int i = threadIdx.x; i < bins * kCgChan; i += blockDim.x) {
+    const int s = i / kCgChan, c = i - s * kCgChan;
+    if (c < nc) cl[static_cast<size_t>(s) * C + c] = cg_hist_count<kWide>(hist, s, cg_hcol(c));
+  }
+}
+
+__global__ void __launch_bounds__(256) cg_assign_kernel(const uint32_t *__restrict__ counts,
+                                                        int16_t *out, int L, int C, int bins) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(L) * C) return;
+  const int l = static_cast<int>(i / C), c = static_cast<int>(i - static_cast<long long>(l) * C);
+  const uint32_t *cn = counts + static_cast<size_t>(l) * bins * C + c;
+  int16_t *o = out + static_cast<size_t>(i) * (bins + 1);
+  cdf_assign([&](int s) { return __ldg(cn + static_cast<size_t>(s) * C); }, bins,
+             [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
 }
 
 // ---------------------------------------------------------------------------
@@ -768,7 +812,23 @@ at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
   const bool vec4 = C % 4 == 0 && cg_aligned(in.data_ptr(), 4);
   auto stream = at::cuda::getCurrentCUDAStream().stream();
   const auto *ip = reinterpret_cast<const uint8_t *>(in.data_ptr());
-  if (wide) {
+  if (n_bins > 64) {
+    auto counts = at::empty({L, n_bins, C}, in.options().dtype(at::kInt));
+    auto *cp = reinterpret_cast<uint32_t *>(counts.data_ptr<int32_t>());
+    if (wide) {
+      cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<true>), smem);
+      cg_hist_kernel<true><<<grid, 256, smem, stream>>>(ip, cp, L, T, C,
+                                                       static_cast<int>(n_bins), vec4);
+    } else {
+      cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<false>), smem);
+      cg_hist_kernel<false><<<grid, 256, smem, stream>>>(ip, cp, L, T, C,
+                                                        static_cast<int>(n_bins), vec4);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    const long long n = static_cast<long long>(L) * C;
+    cg_assign_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+        cp, out.data_ptr<int16_t>(), L, C, static_cast<int>(n_bins));
+  } else if (wide) {
     cg_smem_attr(reinterpret_cast<const void *>(cg_cdf_kernel<true>), smem);
     cg_cdf_kernel<true><<<grid, 256, smem, stream>>>(ip, out.data_ptr<int16_t>(), L, T, C,
                                                     static_cast<int>(n_bins), vec4);
