@@ -513,6 +513,7 @@ class LMCacheConnectorV1Impl:
         if self.metadata.kv_dtype is None:
             self.metadata.kv_dtype = first.dtype
         eng.post_init(kvcaches=caches0)
+        self._caches0 = caches0
         self._engines = [eng]
         for g in range(1, ng):
             self._engines.append(self._group_engine(g, [kv_caches[n]
@@ -623,6 +624,21 @@ class LMCacheConnectorV1Impl:
                                r.req_id, n)
                 self.load_error_block_ids.update(
                     (r.slot_mapping[skip:n] // self.block_size).unique().tolist())
+                continue
+            if self.config.enable_blending:
+                # CacheBlend: retrieve the cached segments and recompute the
+                # deviating tokens with the served model's weights, writing
+                # the blended KV into this request's blocks (the serving
+                # process registers its model under the instance id)
+                from ...v1.blend.vllm_model import get_or_create_blender
+
+                b = get_or_create_blender(self.config.lmcache_instance_id, eng,
+                                          eng.gpu_connector, self.config, self._caches0)
+                ret = b.blend(toks, mask, slot_mapping=r.slots_of_group(0)[:n])
+                got = int(ret.sum())
+                if got < n - skip:
+                    logger.warning("req %s: blended %d of %d expected tokens", r.req_id,
+                                   got, n - skip)
                 continue
             for gi, geng in enumerate(self._engines):
                 slots = r.slots_of_group(gi)[:n]
