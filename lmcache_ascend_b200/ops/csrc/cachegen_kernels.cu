@@ -60,18 +60,20 @@ __host__ __device__ inline int cg_popcount(unsigned x) {
 #endif
 }
 
-__host__ __device__ inline int cg_log2(unsigned w) {  // w is a power of two
-  int e = 0;
-  while ((1u << e) < w) ++e;
-  return e;
-}
-
 __host__ __device__ inline int cg_log2_floor(unsigned v) {  // v >= 1
 #ifdef __CUDA_ARCH__
   return 31 - __clz(v);
 #else
   return 31 - __builtin_clz(v);
 #endif
+}
+
+// Smallest e with 2^e >= w (the exponent of a power-of-two width; a last
+// symbol's remainder width rounds up).
+__host__ __device__ inline int cg_log2(unsigned w) {
+  if (w <= 1) return 0;
+  const int e = cg_log2_floor(w);
+  return (1u << e) < w ? e + 1 : e;
 }
 
 __host__ __device__ inline int cg_msb64(unsigned long long v) {  // v >= 1
@@ -89,17 +91,25 @@ __host__ __device__ inline int cg_msb64(unsigned long long v) {  // v >= 1
 // to the smoothed probability as the alignment of the running start allows,
 // with enough room left for the remaining symbols.
 // ---------------------------------------------------------------------------
-template <class Counts, class Put>
-__host__ __device__ inline void cdf_assign(Counts counts, int bins, Put put) {
-  if (bins == 1) {
-    put(0, 0);  // start 0, len 0: the only symbol costs no bits
-    put(1, 0);
-    return;
-  }
-  unsigned long long total = 0;
-  for (int s = 0; s < bins; ++s) total += counts(s);
-  // smoothed probability p_s = (2 c_s + 1) / (2 N + bins)
-  const unsigned long long den = 2ull * total + static_cast<unsigned>(bins);
+// Desired width exponent of a symbol with `count` occurrences: the largest
+// power of two wd in [16, 32768] with den * 2 wd <= x, x = (2 count + 1) 65536
+// (a monotone condition: start from an msb estimate and step to it), doubled
+// when p * 65536 is nearer the next power.  It depends on the symbol alone,
+// so it can be computed for every symbol at once.
+__host__ __device__ inline int cg_desired_exp(unsigned count, unsigned long long den) {
+  const unsigned long long x = (2ull * count + 1ull) * 65536ull;
+  int g = cg_msb64(x) - cg_msb64(den) - 1;
+  g = g < 4 ? 4 : (g > 15 ? 15 : g);
+  unsigned wd = 1u << g;
+  while (wd > 16u && den * (2ull * wd) > x) wd >>= 1;
+  while (wd < 32768u && den * (2ull * wd) <= x) wd <<= 1;
+  if (wd < 32768u && 2ull * x >= 3ull * den * wd) wd <<= 1;
+  return cg_log2(wd);
+}
+
+// The serial placement: ed_of(s) -> desired exponent of symbol s.
+template <class Ed, class Put>
+__host__ __device__ inline void cdf_place(Ed ed_of, int bins, Put put) {
   unsigned pos = 0;
   for (int s = 0; s < bins; ++s) {
     const int k = bins - s;  // symbols left, including s
@@ -108,17 +118,7 @@ __host__ __device__ inline void cdf_assign(Counts counts, int bins, Put put) {
     if (k == 1) {
       w = R;
     } else {
-      // desired width: the largest power of two wd in [16, 32768] with
-      // den * 2 wd <= x (a monotone condition: start from an msb estimate and
-      // step to it), then doubled when p * 65536 is nearer the next power
-      const unsigned long long x = (2ull * counts(s) + 1ull) * 65536ull;
-      int g = cg_msb64(x) - cg_msb64(den) - 1;
-      g = g < 4 ? 4 : (g > 15 ? 15 : g);
-      unsigned wd = 1u << g;
-      while (wd > 16u && den * (2ull * wd) > x) wd >>= 1;
-      while (wd < 32768u && den * (2ull * wd) <= x) wd <<= 1;
-      if (wd < 32768u && 2ull * x >= 3ull * den * wd) wd <<= 1;
-      const int ed = cg_log2(wd);
+      const int ed = ed_of(s);
       const unsigned maxw = pos == 0 ? 32768u : (pos & (~pos + 1u));
       // feasible widths 2^e: aligned at pos, leave room (a sum of at most k-1
       // powers of two >= 16) for the remaining symbols.  Take the feasible e
@@ -155,6 +155,20 @@ __host__ __device__ inline void cdf_assign(Counts counts, int bins, Put put) {
     pos += w;
   }
   put(bins, 0);  // stands for 0x10000
+}
+
+// smoothed probability p_s = (2 c_s + 1) / (2 N + bins), N = total count
+template <class Counts, class Put>
+__host__ __device__ inline void cdf_assign(Counts counts, int bins, Put put) {
+  if (bins == 1) {
+    put(0, 0);  // start 0, len 0: the only symbol costs no bits
+    put(1, 0);
+    return;
+  }
+  unsigned long long total = 0;
+  for (int s = 0; s < bins; ++s) total += counts(s);
+  const unsigned long long den = 2ull * total + static_cast<unsigned>(bins);
+  cdf_place([&](int s) { return cg_desired_exp(counts(s), den); }, bins, put);
 }
 
 // ---------------------------------------------------------------------------
@@ -234,34 +248,58 @@ __global__ void __launch_bounds__(256) cg_cdf_kernel(const uint8_t *__restrict__
 
 // Split form (many bins): the histogram tables of 256 bins leave room for
 // only 3 blocks per SM, and the serial assignment then runs on 12 warps per
-// SM.  Here the histogram goes to global memory as counts[L][bins][C]
-// (coalesced over channels), and the assignment runs as its own kernel with
-// one thread per (layer, channel), no shared memory and full occupancy.
+// SM.  Here the histogram kernel turns each (symbol, channel) count into its
+// desired width exponent at once (it depends on that count and on
+// den = 2 T + bins only: every token adds one symbol to every channel) and
+// writes them as exps[L][bins][C] bytes; the serial placement then runs as
+// its own kernel, one thread per (layer, channel), with no shared memory.
 template <bool kWide>
 __global__ void __launch_bounds__(256) cg_hist_kernel(const uint8_t *__restrict__ in,
-                                                      uint32_t *counts, int L, int T, int C,
+                                                      uint8_t *exps, int L, int T, int C,
                                                       int bins, bool vec4) {
   extern __shared__ unsigned hist[];
   const int l = blockIdx.y;
   const int c0 = blockIdx.x * kCgChan;
   const int nc = min(kCgChan, C - c0);
   cg_histogram<kWide>(in, hist, l, T, C, c0, nc, bins, vec4);
-  uint32_t *cl = counts + static_cast<size_t>(l) * bins * C + c0;
+  const unsigned long long den = 2ull * static_cast<unsigned>(T) + static_cast<unsigned>(bins);
+  uint8_t *el = exps + static_cast<size_t>(l) * bins * C + c0;
   for (int i = threadIdx.x; i < bins * kCgChan; i += blockDim.x) {
     const int s = i / kCgChan, c = i - s * kCgChan;
-    if (c < nc) cl[static_cast<size_t>(s) * C + c] = cg_hist_count<kWide>(hist, s, cg_hcol(c));
+    if (c < nc)
+      el[static_cast<size_t>(s) * C + c] = static_cast<uint8_t>(
+          cg_desired_exp(cg_hist_count<kWide>(hist, s, cg_hcol(c)), den));
   }
 }
 
-__global__ void __launch_bounds__(256) cg_assign_kernel(const uint32_t *__restrict__ counts,
-                                                        int16_t *out, int L, int C, int bins) {
+// Exponents read kBatch at a time (the placement asks for them in order).
+struct CgExpBatch {
+  static constexpr int kBatch = 16;
+  const uint8_t *p;
+  size_t stride;
+  int bins;
+  int base;
+  uint8_t buf[kBatch];
+  __device__ int operator()(int s) {
+    if (s < base || s >= base + kBatch) {
+      base = s;
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k)
+        buf[k] = s + k < bins ? __ldg(p + static_cast<size_t>(s + k) * stride) : 0;
+    }
+    return buf[s - base];
+  }
+};
+
+__global__ void __launch_bounds__(128) cg_place_kernel(const uint8_t *__restrict__ exps,
+                                                       int16_t *out, int L, int C, int bins) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<long long>(L) * C) return;
   const int l = static_cast<int>(i / C), c = static_cast<int>(i - static_cast<long long>(l) * C);
-  const uint32_t *cn = counts + static_cast<size_t>(l) * bins * C + c;
+  CgExpBatch eb{exps + static_cast<size_t>(l) * bins * C + c, static_cast<size_t>(C), bins,
+                -CgExpBatch::kBatch, {}};
   int16_t *o = out + static_cast<size_t>(i) * (bins + 1);
-  cdf_assign([&](int s) { return __ldg(cn + static_cast<size_t>(s) * C); }, bins,
-             [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
+  cdf_place(eb, bins, [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
 }
 
 // ---------------------------------------------------------------------------
@@ -813,8 +851,8 @@ at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
   auto stream = at::cuda::getCurrentCUDAStream().stream();
   const auto *ip = reinterpret_cast<const uint8_t *>(in.data_ptr());
   if (n_bins > 64) {
-    auto counts = at::empty({L, n_bins, C}, in.options().dtype(at::kInt));
-    auto *cp = reinterpret_cast<uint32_t *>(counts.data_ptr<int32_t>());
+    auto exps = at::empty({L, n_bins, C}, in.options().dtype(at::kByte));
+    auto *cp = exps.data_ptr<uint8_t>();
     if (wide) {
       cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<true>), smem);
       cg_hist_kernel<true><<<grid, 256, smem, stream>>>(ip, cp, L, T, C,
@@ -826,7 +864,7 @@ at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     const long long n = static_cast<long long>(L) * C;
-    cg_assign_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+    cg_place_kernel<<<static_cast<unsigned>((n + 127) / 128), 128, 0, stream>>>(
         cp, out.data_ptr<int16_t>(), L, C, static_cast<int>(n_bins));
   } else if (wide) {
     cg_smem_attr(reinterpret_cast<const void *>(cg_cdf_kernel<true>), smem);
