@@ -291,15 +291,44 @@ struct CgExpBatch {
   }
 };
 
-__global__ void __launch_bounds__(128) cg_place_kernel(const uint8_t *__restrict__ exps,
-                                                       int16_t *out, int L, int C, int bins) {
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<long long>(L) * C) return;
-  const int l = static_cast<int>(i / C), c = static_cast<int>(i - static_cast<long long>(l) * C);
+// Placement, one thread per (layer, channel), kPlaceCh channels per block.
+// Entries are collected kPlaceRun symbols at a time in shared memory and
+// then written as one contiguous 2 kPlaceRun-byte piece per channel: written
+// one by one, each 2-byte entry would be its own sector write (the lanes'
+// rows are 2 (bins + 1) bytes apart).  Every thread runs the same number of
+// steps (threads past the last channel repeat it and store nothing), so the
+// block can synchronise at every flush.
+constexpr int kPlaceCh = 128;
+constexpr int kPlaceRun = 16;
+
+__global__ void __launch_bounds__(kPlaceCh) cg_place_kernel(const uint8_t *__restrict__ exps,
+                                                            int16_t *out, int L, int C,
+                                                            int bins) {
+  __shared__ int16_t run[kPlaceCh][kPlaceRun + 1];
+  const int row = bins + 1;
+  const long long n = static_cast<long long>(L) * C;
+  const long long i0 = static_cast<long long>(blockIdx.x) * kPlaceCh;
+  const long long i = min(i0 + threadIdx.x, n - 1);
+  const int nrows = static_cast<int>(n - i0 < kPlaceCh ? n - i0 : kPlaceCh);
+  const int l = static_cast<int>(i / C);
+  const int c = static_cast<int>(i - static_cast<long long>(l) * C);
   CgExpBatch eb{exps + static_cast<size_t>(l) * bins * C + c, static_cast<size_t>(C), bins,
                 -CgExpBatch::kBatch, {}};
-  int16_t *o = out + static_cast<size_t>(i) * (bins + 1);
-  cdf_place(eb, bins, [&](int s, unsigned short v) { o[s] = static_cast<int16_t>(v); });
+  int16_t *base = out + static_cast<size_t>(i0) * row;
+  cdf_place(eb, bins, [&](int s, unsigned short v) {
+    run[threadIdx.x][s % kPlaceRun] = static_cast<int16_t>(v);
+    if (s % kPlaceRun == kPlaceRun - 1 || s == bins) {
+      const int s0 = s - s % kPlaceRun;
+      const int cnt = s - s0 + 1;
+      __syncthreads();
+      // flush entries s0 .. s of every channel, lanes over (channel, entry)
+      for (int e = threadIdx.x; e < nrows * cnt; e += kPlaceCh) {
+        const int ch = e / cnt, k = e - ch * cnt;
+        base[static_cast<size_t>(ch) * row + s0 + k] = run[ch][k];
+      }
+      __syncthreads();
+    }
+  });
 }
 
 // ---------------------------------------------------------------------------
@@ -864,7 +893,8 @@ at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     const long long n = static_cast<long long>(L) * C;
-    cg_place_kernel<<<static_cast<unsigned>((n + 127) / 128), 128, 0, stream>>>(
+    cg_place_kernel<<<static_cast<unsigned>((n + kPlaceCh - 1) / kPlaceCh), kPlaceCh, 0,
+                      stream>>>(
         cp, out.data_ptr<int16_t>(), L, C, static_cast<int>(n_bins));
   } else if (wide) {
     cg_smem_attr(reinterpret_cast<const void *>(cg_cdf_kernel<true>), smem);
