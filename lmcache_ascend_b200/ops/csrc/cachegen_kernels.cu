@@ -49,6 +49,7 @@ namespace lmc {
 
 constexpr int kCgMaxBins = 256;
 constexpr int kCgChan = 128;     // channels per histogram block
+constexpr int kCgExpTab = 8192;  // counts with a precomputed width exponent (split CDF)
 constexpr int kCgTile = 64;      // tokens per encode shared-memory tile
 constexpr int kCgLut = 256;      // decode table entries (top 8 window bits): 32 KB per block
 
@@ -261,14 +262,23 @@ __global__ void __launch_bounds__(256) cg_hist_kernel(const uint8_t *__restrict_
   const int l = blockIdx.y;
   const int c0 = blockIdx.x * kCgChan;
   const int nc = min(kCgChan, C - c0);
-  cg_histogram<kWide>(in, hist, l, T, C, c0, nc, bins, vec4);
   const unsigned long long den = 2ull * static_cast<unsigned>(T) + static_cast<unsigned>(bins);
+  // the exponent depends on the count alone (den is fixed), so short chunks
+  // (T < kCgExpTab) look it up in a table of every count 0..T built once
+  uint8_t *tab = reinterpret_cast<uint8_t *>(hist + (kWide ? bins : (bins + 1) / 2) * kCgChan);
+  const bool use_tab = T < kCgExpTab;
+  if (use_tab)
+    for (int v = threadIdx.x; v <= T; v += blockDim.x)
+      tab[v] = static_cast<uint8_t>(cg_desired_exp(static_cast<unsigned>(v), den));
+  cg_histogram<kWide>(in, hist, l, T, C, c0, nc, bins, vec4);  // synchronises
   uint8_t *el = exps + static_cast<size_t>(l) * bins * C + c0;
   for (int i = threadIdx.x; i < bins * kCgChan; i += blockDim.x) {
     const int s = i / kCgChan, c = i - s * kCgChan;
-    if (c < nc)
-      el[static_cast<size_t>(s) * C + c] = static_cast<uint8_t>(
-          cg_desired_exp(cg_hist_count<kWide>(hist, s, cg_hcol(c)), den));
+    if (c < nc) {
+      const unsigned cnt = cg_hist_count<kWide>(hist, s, cg_hcol(c));
+      el[static_cast<size_t>(s) * C + c] =
+          use_tab ? tab[cnt] : static_cast<uint8_t>(cg_desired_exp(cnt, den));
+    }
   }
 }
 
@@ -882,14 +892,15 @@ at::Tensor calculate_cdf(const at::Tensor &input, int64_t n_bins) {
   if (n_bins > 64) {
     auto exps = at::empty({L, n_bins, C}, in.options().dtype(at::kByte));
     auto *cp = exps.data_ptr<uint8_t>();
+    const size_t hsmem = smem + (T < kCgExpTab ? static_cast<size_t>(T) + 1 : 0);
     if (wide) {
-      cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<true>), smem);
-      cg_hist_kernel<true><<<grid, 256, smem, stream>>>(ip, cp, L, T, C,
-                                                       static_cast<int>(n_bins), vec4);
-    } else {
-      cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<false>), smem);
-      cg_hist_kernel<false><<<grid, 256, smem, stream>>>(ip, cp, L, T, C,
+      cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<true>), hsmem);
+      cg_hist_kernel<true><<<grid, 256, hsmem, stream>>>(ip, cp, L, T, C,
                                                         static_cast<int>(n_bins), vec4);
+    } else {
+      cg_smem_attr(reinterpret_cast<const void *>(cg_hist_kernel<false>), hsmem);
+      cg_hist_kernel<false><<<grid, 256, hsmem, stream>>>(ip, cp, L, T, C,
+                                                         static_cast<int>(n_bins), vec4);
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     const long long n = static_cast<long long>(L) * C;
