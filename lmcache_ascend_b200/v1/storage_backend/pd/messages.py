@@ -147,6 +147,8 @@ def slot_digest(slots) -> "tuple[str, int]":
 
     if isinstance(slots, torch.Tensor):
         arr = slots.detach().to("cpu", torch.int64).numpy()
+    elif isinstance(slots, np.ndarray):
+        arr = slots
     else:
         arr = np.asarray(list(slots), dtype=np.int64)
     a64 = np.ascontiguousarray(arr.astype("<i8", copy=False))

@@ -196,7 +196,8 @@ class SenderMixin:
         destination slots the sender was given; ``None`` asks the decoder for
         the slots it reserved, from reserved token ``token_begin`` on, at most
         ``num_tokens`` (-1: all) and not past prompt position ``prompt_end``.
-        Returns (granted destination slots, prompt position of the
+        Returns (the destination slots: the decoder's list when it chose them,
+        else ``dst_slots_host`` as given; prompt position of the
         reservation's first token).
         Raises -- and trips the per-peer circuit breaker -- when the decoder
         does not answer, answers with a stale registration epoch twice, or
@@ -224,8 +225,7 @@ class SenderMixin:
                     self.stats.inc("pd_direct_grants")
                     if want:
                         return list(resp.slots), int(resp.first_token)
-                    return (dst_slots_host.tolist() if isinstance(dst_slots_host, torch.Tensor)
-                            else list(dst_slots_host)), int(resp.first_token)
+                    return dst_slots_host, int(resp.first_token)  # as given
                 if isinstance(resp, M.DirectPushGrant) and resp.epoch and \
                         resp.epoch != self._receiver_epoch and reconnects < 1:
                     reconnects += 1  # the decoder re-registered: map it again
