@@ -32,11 +32,13 @@
 // Encode stages [64 tokens x CH channels] symbol tiles in shared memory with
 // 16-byte loads (double buffered: the next tile's loads are in flight while
 // the current one is coded) and emits 32-bit big-endian words.  Decode
-// resolves every code with one lookup in a per-channel 256-entry table
-// indexed by the window's top byte plus bit arithmetic for codes longer than
-// 8 bits, refilling the window once per two symbols from 16-byte loads issued
-// well ahead.  Shared tables are laid out [entry][channel] so that a warp's
-// lanes hit 32 different banks.
+// keeps no tables in shared memory (they bounded the resident streams): up
+// to 16 symbols it compares the window against the whole CDF held in
+// registers; above that, against every 16th entry in registers and then a
+// 4-step binary search over the chosen group's entries in the stream's own
+// (L1-resident) CDF row.  The window is refilled once per two symbols from
+// 16-byte loads issued well ahead.  Shared tables elsewhere are laid out
+// [entry][channel] so that a warp's lanes hit 32 different banks.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -51,7 +53,6 @@ constexpr int kCgMaxBins = 256;
 constexpr int kCgChan = 128;     // channels per histogram block
 constexpr int kCgExpTab = 8192;  // counts with a precomputed width exponent (split CDF)
 constexpr int kCgTile = 64;      // tokens per encode shared-memory tile
-constexpr int kCgLut = 256;      // decode table entries (top 8 window bits): 32 KB per block
 
 __host__ __device__ inline int cg_popcount(unsigned x) {
 #ifdef __CUDA_ARCH__
@@ -508,28 +509,8 @@ __global__ void __launch_bounds__(CH) cg_encode_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// decode (prefix-summed lengths): block of 32 threads per (layer, 32-channel
-// tile), thread per stream.  Per-channel table lut[256] of 16-bit entries,
-// indexed by the window's top byte p and stored as [p / 2][32 channels]
-// words (one bank per lane):
-//   bit 15 clear: one symbol covers every value with top byte p:
-//                 bits 0-7 symbol, 8-11 code length (<= 8);
-//   bit 15 set:   several symbols start inside p's range (an interval narrower
-//                 than 256 is aligned to its width, so it starts and ends
-//                 inside one top-byte range and starts at a multiple of 16);
-//                 bits 0-7 index a per-channel pool record holding the first
-//                 of them (bits 0-7) and a mask of their start nibbles (bits
-//                 8-23, nibble = bits 4-7 of the start).  The symbol is the
-//                 first plus the number of starts at or below the window's
-//                 nibble, minus one; its width is the gap to the next start.
-// A multi-symbol range holds at least two symbols, so the pool needs at most
-// bins / 2 records: the table costs 512 + 2 * bins bytes per channel.
-// The window is refilled once per two symbols (codes are at most 12 bits)
-// from a ring of three 16-byte loads, so a load is issued about eight refills
-// before its bits are needed; the same straight-line code runs on every lane.
+// decode (prefix-summed stream lengths): bit reader shared by the decoders.
 // ---------------------------------------------------------------------------
-constexpr int kDecCh = 32;
-
 // 16 bytes at `pos` (a multiple of 16 counted from the 16-aligned `abase`);
 // the buffer is the byte range [lo, hi), bytes outside it read as 0.
 __device__ __forceinline__ uint4 cg_fetch16(const uint8_t *abase, long long pos, long long lo,
@@ -549,88 +530,34 @@ __device__ __forceinline__ uint32_t cg_word(const uint4 &v, int j) {
   return cg_bswap(w);
 }
 
-// kWide (bins > 64): the table holds 32-bit entries and keeps a multi-symbol
-// range's first symbol and nibble mask in the entry itself (no pool lookup):
-// 1 KB per channel, worth it when long codes are common.
-template <bool kWide>
-__global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
+// ---------------------------------------------------------------------------
+// decode, at most 16 symbols: the stream's CDF fits in registers (interval
+// starts and code lengths), so no table is built and no shared memory is
+// used; a thread per (layer, channel) stream at full occupancy.  A symbol is
+// the last interval whose start is <= the window's top 16 bits (the starts
+// increase; unused entries start at 0x10000, past every window value).
+// The bit reader: a ring of three 16-byte loads, refilled once per two
+// symbols (a code is at most 12 bits).
+// ---------------------------------------------------------------------------
+constexpr int kDecSmallBins = 16;
+constexpr int kDecSmallThreads = 128;
+
+__global__ void __launch_bounds__(kDecSmallThreads) cg_decode_small_kernel(
     const int16_t *__restrict__ cdf, const uint8_t *__restrict__ bytes,
     const int32_t *__restrict__ cum_len, long long total_bytes, uint8_t *out, int L, int T,
     int C, int bins) {
-  extern __shared__ uint32_t cg_dsmem[];
-  uint32_t *lut = cg_dsmem;                     // [kCgLut / 2][kDecCh]
-  uint32_t *pool = cg_dsmem + (kCgLut / 2) * kDecCh;  // [max(1, bins / 2)][kDecCh]
-  const int l = blockIdx.y;
-  const int c0 = blockIdx.x * kDecCh;
-  const int tid = threadIdx.x;
-  if (c0 + tid >= C) return;  // no block-wide barrier below: every thread owns its columns
-  const int pool_cap = max(1, bins / 2);
-  auto lget = [&](int p) {
-    const uint32_t w = lut[(p >> 1) * kDecCh + tid];
-    return (p & 1) ? (w >> 16) : (w & 0xFFFFu);
-  };
-  auto lset = [&](int p, unsigned v) {
-    uint32_t &w = lut[(p >> 1) * kDecCh + tid];
-    w = (p & 1) ? ((w & 0xFFFFu) | (v << 16)) : ((w & 0xFFFF0000u) | v);
-  };
-  const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
-  // The table is built from the channel's CDF entries, read kBatch at a time
-  // so that many loads are in flight (the build of a 256-bin table would
-  // otherwise wait on one load per symbol, as long as decoding a stream).
-  constexpr int kBatch = 16;
-  auto for_each_entry = [&](auto &&f) {
-    for (int s0 = 0; s0 < bins; s0 += kBatch) {
-      unsigned ev[kBatch];
+  const long long idx = static_cast<long long>(blockIdx.x) * kDecSmallThreads + threadIdx.x;
+  if (idx >= static_cast<long long>(L) * C) return;
+  const int l = static_cast<int>(idx / C);
+  const int c = static_cast<int>(idx - static_cast<long long>(l) * C);
+  const int16_t *cd = cdf + idx * (bins + 1);
+  unsigned st[kDecSmallBins], ln_of[kDecSmallBins];
 #pragma unroll
-      for (int k = 0; k < kBatch; ++k)
-        ev[k] = s0 + k < bins ? static_cast<unsigned short>(__ldg(cd + s0 + k)) : 0u;
-#pragma unroll
-      for (int k = 0; k < kBatch; ++k)
-        if (s0 + k < bins) f(s0 + k, ev[k]);
-    }
-  };
-  if constexpr (kWide) {
-    for (int p = 0; p < kCgLut; ++p) lut[p * kDecCh + tid] = 8u << 8;  // symbol 0, 8 bits
-    for_each_entry([&](int s, unsigned e) {
-      const unsigned ln = e & 0xFu;
-      const unsigned st = e & 0xFFF0u;
-      if (ln <= 8) {
-        const unsigned en = min(65536u, st + (1u << (16 - ln)));
-        for (unsigned p = st >> 8; p < (en >> 8); ++p)
-          lut[p * kDecCh + tid] = (ln << 8) | static_cast<unsigned>(s);
-      } else {
-        uint32_t &w = lut[(st >> 8) * kDecCh + tid];
-        const uint32_t bit = 1u << (8 + ((st >> 4) & 0xFu));
-        w = (w & 0x80000000u) ? (w | bit) : (0x80000000u | bit | static_cast<unsigned>(s));
-      }
-    });
+  for (int k = 0; k < kDecSmallBins; ++k) {
+    const unsigned e = k < bins ? static_cast<unsigned short>(__ldg(cd + k)) : 0u;
+    st[k] = k < bins ? (e & 0xFFF0u) : 0x10000u;
+    ln_of[k] = e & 0xFu;
   }
-  const uint32_t dflt = (8u << 8) | ((8u << 8) << 16);  // safe default: symbol 0, 8 bits
-  if constexpr (!kWide)
-    for (int p = 0; p < kCgLut / 2; ++p) lut[p * kDecCh + tid] = dflt;
-  int used = 0;
-  if constexpr (!kWide) for_each_entry([&](int s, unsigned e) {
-    const unsigned ln = e & 0xFu;
-    const unsigned st = e & 0xFFF0u;
-    if (ln <= 8) {
-      const unsigned en = min(65536u, st + (1u << (16 - ln)));
-      for (unsigned p = st >> 8; p < (en >> 8); ++p)
-        lset(static_cast<int>(p), (ln << 8) | static_cast<unsigned>(s));
-    } else {
-      const int p = static_cast<int>(st >> 8);
-      const uint32_t bit = 1u << (8 + ((st >> 4) & 0xFu));
-      const unsigned cur = lget(p);
-      if (cur & 0x8000u) {
-        pool[(cur & 0xFFu) * kDecCh + tid] |= bit;
-      } else if (used < pool_cap) {
-        pool[used * kDecCh + tid] = bit | static_cast<unsigned>(s);
-        lset(p, 0x8000u | static_cast<unsigned>(used));
-        ++used;
-      }
-    }
-  });
-  const int c = c0 + tid;
-  const size_t idx = static_cast<size_t>(l) * C + c;
   const long long b0 = idx == 0 ? 0 : cum_len[idx - 1];
   const uint8_t *abase =
       reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(bytes) & ~uintptr_t(15));
@@ -657,39 +584,116 @@ __global__ void __launch_bounds__(kDecCh) cg_decode_kernel(
     }
   };
   next_word();
-  const uint32_t *my = lut + tid;
   auto decode1 = [&]() -> unsigned {
     const unsigned v = static_cast<unsigned>(win >> 48);
-    const unsigned p = v >> 8;
-    unsigned sym, ln;
-    uint32_t e = 0;
-    bool single;
-    if constexpr (kWide) {
-      e = my[p * kDecCh];
-      single = !(e & 0x80000000u);
-      sym = e & 0xFFu;
-      ln = (e >> 8) & 0xFu;
-    } else {
-      const uint32_t w = my[(p >> 1) * kDecCh];
-      const unsigned h = (p & 1) ? (w >> 16) : (w & 0xFFFFu);
-      single = !(h & 0x8000u);
-      sym = h & 0xFFu;
-      ln = (h >> 8) & 0xFu;
-      if (!single) e = pool[(h & 0xFFu) * kDecCh + tid];
-    }
-    if (!single) {
-      const unsigned nib = (v >> 4) & 0xFu;
-      const unsigned m = (e >> 8) & 0xFFFFu;
-      const unsigned below = (m & ((2u << nib) - 1u)) | 1u;  // bit 0: the first symbol
-      const int cur = 31 - __clz(below);
-      const unsigned above = m & ~((2u << cur) - 1u);
-      const int nxt = above ? __ffs(above) - 1 : 16;
-      sym = (e & 0xFFu) + static_cast<unsigned>(__popc(below) - 1);
-      ln = 12u - static_cast<unsigned>(31 - __clz(static_cast<unsigned>(nxt - cur)));
+    unsigned sym = 0, ln = ln_of[0];
+#pragma unroll
+    for (int k = 1; k < kDecSmallBins; ++k) {
+      const bool ge = v >= st[k];
+      sym = ge ? static_cast<unsigned>(k) : sym;
+      ln = ge ? ln_of[k] : ln;
     }
     win <<= ln;
     nb -= static_cast<int>(ln);
     return sym;
+  };
+  uint8_t *op = out + static_cast<size_t>(l) * T * C + c;
+  const size_t step = static_cast<size_t>(C);
+  int t = 0;
+  for (; t + 2 <= T; t += 2) {
+    if (nb <= 32) {  // two codes need at most 24 bits
+      win |= static_cast<unsigned long long>(cg_word(A, j)) << (32 - nb);
+      nb += 32;
+      next_word();
+    }
+    const unsigned s0 = decode1();
+    const unsigned s1 = decode1();
+    op[0] = static_cast<uint8_t>(s0);
+    op[step] = static_cast<uint8_t>(s1);
+    op += 2 * step;
+  }
+  if (t < T) {
+    if (nb <= 32) win |= static_cast<unsigned long long>(cg_word(A, j)) << (32 - nb);
+    op[0] = static_cast<uint8_t>(decode1());
+  }
+}
+
+// ---------------------------------------------------------------------------
+// decode, 17..256 symbols: a two-level search of the stream's CDF instead of
+// a per-stream lookup table in shared memory (the 1 KB tables of 256-symbol
+// streams left room for 7 warps per SM).  Registers hold every 16th entry;
+// the last of those <= the window's top 16 bits picks a group of 16 symbols,
+// and a 4-step binary search over that group's entries (L1-resident global
+// loads of the stream's own 2 (bins + 1)-byte CDF row) picks the symbol.  An
+// entry is start | code length with start a multiple of 16, so
+// "start <= v" is "entry <= v | 15".
+// ---------------------------------------------------------------------------
+constexpr int kDecWideThreads = 128;
+
+__global__ void __launch_bounds__(kDecWideThreads) cg_decode_wide_kernel(
+    const int16_t *__restrict__ cdf, const uint8_t *__restrict__ bytes,
+    const int32_t *__restrict__ cum_len, long long total_bytes, uint8_t *out, int L, int T,
+    int C, int bins) {
+  const long long idx = static_cast<long long>(blockIdx.x) * kDecWideThreads + threadIdx.x;
+  if (idx >= static_cast<long long>(L) * C) return;
+  const int l = static_cast<int>(idx / C);
+  const int c = static_cast<int>(idx - static_cast<long long>(l) * C);
+  const unsigned short *cd = reinterpret_cast<const unsigned short *>(cdf) + idx * (bins + 1);
+  unsigned coarse[16];
+#pragma unroll
+  for (int g = 0; g < 16; ++g)
+    coarse[g] = 16 * g < bins ? static_cast<unsigned>(__ldg(cd + 16 * g)) : 0x10000u;
+  const long long b0 = idx == 0 ? 0 : cum_len[idx - 1];
+  const uint8_t *abase =
+      reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(bytes) & ~uintptr_t(15));
+  const long long lo = bytes - abase;  // 0..15
+  const long long hi = lo + total_bytes;
+  const long long start = lo + b0;
+  long long pos = start & ~15ll;
+  uint4 A = cg_fetch16(abase, pos, lo, hi);
+  uint4 B = cg_fetch16(abase, pos + 16, lo, hi);
+  uint4 D = cg_fetch16(abase, pos + 32, lo, hi);
+  pos += 48;
+  int j = static_cast<int>((start - (start & ~15ll)) >> 2);  // next word of A
+  const int skip = static_cast<int>(start & 3) * 8;
+  unsigned long long win = static_cast<unsigned long long>(cg_word(A, j)) << 32;
+  win <<= skip;
+  int nb = 32 - skip;  // valid bits at the top of win
+  auto next_word = [&]() {
+    if (++j == 4) {
+      A = B;
+      B = D;
+      D = cg_fetch16(abase, pos, lo, hi);
+      pos += 16;
+      j = 0;
+    }
+  };
+  next_word();
+  auto decode1 = [&]() -> unsigned {
+    const unsigned vv = static_cast<unsigned>(win >> 48) | 15u;
+    int k = 0;
+    unsigned e = coarse[0];
+#pragma unroll
+    for (int g = 1; g < 16; ++g) {
+      const bool ge = vv >= coarse[g];
+      k = ge ? 16 * g : k;
+      e = ge ? coarse[g] : e;
+    }
+#pragma unroll
+    for (int step = 8; step >= 1; step >>= 1) {
+      const int m = k + step;
+      if (m < bins) {
+        const unsigned em = __ldg(cd + m);
+        if (vv >= em) {
+          k = m;
+          e = em;
+        }
+      }
+    }
+    const unsigned ln = e & 0xFu;
+    win <<= ln;
+    nb -= static_cast<int>(ln);
+    return static_cast<unsigned>(k);
   };
   uint8_t *op = out + static_cast<size_t>(l) * T * C + c;
   const size_t step = static_cast<size_t>(C);
@@ -992,20 +996,20 @@ void decode_fast_prefsum(const at::Tensor &cdf, const at::Tensor &bytestreams,
   auto len = lengths.contiguous();
   const c10::cuda::CUDAGuard guard(c.device());
   if (L == 0 || C == 0 || T == 0) return;
-  dim3 grid((C + kDecCh - 1) / kDecCh, L);
   auto stream = at::cuda::getCurrentCUDAStream().stream();
   const auto *bp = reinterpret_cast<const uint8_t *>(b.data_ptr());
   auto *op8 = reinterpret_cast<uint8_t *>(output.data_ptr());
   const long long nbytes = static_cast<long long>(b.numel());
-  if (bins > 64) {
-    const size_t smem = static_cast<size_t>(kCgLut) * kDecCh * 4;
-    cg_smem_attr(reinterpret_cast<const void *>(cg_decode_kernel<true>), smem);
-    cg_decode_kernel<true><<<grid, kDecCh, smem, stream>>>(
+  const long long nstreams = static_cast<long long>(L) * C;
+  if (bins <= kDecSmallBins) {
+    cg_decode_small_kernel<<<static_cast<unsigned>((nstreams + kDecSmallThreads - 1) /
+                                                   kDecSmallThreads),
+                             kDecSmallThreads, 0, stream>>>(
         c.data_ptr<int16_t>(), bp, len.data_ptr<int32_t>(), nbytes, op8, L, T, C, bins);
   } else {
-    const size_t smem = (kCgLut / 2 + std::max(1, bins / 2)) * kDecCh * 4;
-    cg_smem_attr(reinterpret_cast<const void *>(cg_decode_kernel<false>), smem);
-    cg_decode_kernel<false><<<grid, kDecCh, smem, stream>>>(
+    cg_decode_wide_kernel<<<static_cast<unsigned>((nstreams + kDecWideThreads - 1) /
+                                                  kDecWideThreads),
+                            kDecWideThreads, 0, stream>>>(
         c.data_ptr<int16_t>(), bp, len.data_ptr<int32_t>(), nbytes, op8, L, T, C, bins);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
