@@ -374,21 +374,34 @@ __global__ void __launch_bounds__(CH) cg_encode_kernel(
   const int tid = threadIdx.x;
   const int nc = min(CH, C - c0);
   if (tid < nc) {
-    const int16_t *cd = cdf + (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
-    unsigned st = static_cast<unsigned short>(cd[0]) & 0xFFF0u;
-    for (int s = 0; s < bins; ++s) {
-      const unsigned en =
-          (s + 1 == bins) ? 65536u : (static_cast<unsigned short>(cd[s + 1]) & 0xFFF0u);
-      const unsigned w = en > st ? en - st : 0u;
-      unsigned e = 0xFu;  // not encodable
-      if (w != 0) {
-        const int ln = 16 - (31 - __clz(w));  // 16 - floor(log2 w)
-        e = (static_cast<unsigned>(ln == 0 ? 0 : (st >> (16 - ln))) << 4) |
-            static_cast<unsigned>(ln);
+    // the channel's CDF entries are read 16 at a time, so the loads of a
+    // 256-symbol table are in flight together instead of one per step
+    const unsigned short *cd = reinterpret_cast<const unsigned short *>(cdf) +
+                               (static_cast<size_t>(l) * C + c0 + tid) * (bins + 1);
+    unsigned st = __ldg(cd) & 0xFFF0u;
+    for (int s0 = 0; s0 < bins; s0 += 16) {
+      unsigned nxt[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int s = s0 + k;
+        nxt[k] = s + 1 < bins ? (__ldg(cd + s + 1) & 0xFFF0u) : 65536u;
       }
-      uint32_t &tw = tab[(s >> 1) * CH + tid];
-      tw = (s & 1) ? ((tw & 0xFFFFu) | (e << 16)) : ((tw & 0xFFFF0000u) | e);
-      st = en;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int s = s0 + k;
+        if (s >= bins) break;
+        const unsigned en = nxt[k];
+        const unsigned w = en > st ? en - st : 0u;
+        unsigned e = 0xFu;  // not encodable
+        if (w != 0) {
+          const int ln = 16 - (31 - __clz(w));  // 16 - floor(log2 w)
+          e = (static_cast<unsigned>(ln == 0 ? 0 : (st >> (16 - ln))) << 4) |
+              static_cast<unsigned>(ln);
+        }
+        uint32_t &tw = tab[(s >> 1) * CH + tid];
+        tw = (s & 1) ? ((tw & 0xFFFFu) | (e << 16)) : ((tw & 0xFFFF0000u) | e);
+        st = en;
+      }
     }
   }
   const uint8_t *base = sym + static_cast<size_t>(l) * T * C + c0;
