@@ -97,14 +97,16 @@ def run_config5(dev, rank: int, world: int, gloo=None, tokens: int = 32768,
         if dec:
             recv.wait(targets[i], timeout_s=10.0)
 
+    rope_keys = [layer[0].view(nb * BS, LATENT)[:, 512:] for layer in dst] if dec else []
+
     def rope_step(i):
         if not dec:
             return
         _, ds = tables[i % requests]
         new_pos = old_pos + deltas[i % requests]
-        for layer in dst:
-            key = layer[0].view(nb * BS, LATENT)[:, 512:]
-            native.rotary_embedding_k_fused(old_pos, new_pos, key, ROPE, rope_cache, True, ds)
+        # every layer's rope columns in one launch
+        native.rotary_embedding_k_fused_layers(old_pos, new_pos, rope_keys, ROPE, rope_cache,
+                                               True, ds)
 
     def timed(fn, base):
         barrier()
@@ -144,7 +146,7 @@ def run_config5(dev, rank: int, world: int, gloo=None, tokens: int = 32768,
            "rope_reposition": {"ms_per_request": round(rope_ms, 4),
                                "gbps": round(rope_bytes / (rope_ms / 1e3) / 1e9, 2),
                                "theta": 10000.0, "delta_range": [0, 8192],
-                               "launches_per_request": L}}
+                               "launches_per_request": 1}}
     if peer_copy_gbps:
         out["frac_of_measured_peer_copy"] = round(per_pair / peer_copy_gbps, 4)
     if send is not None:

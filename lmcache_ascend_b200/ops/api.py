@@ -537,6 +537,20 @@ def rotary_embedding_k_fused(old_positions, new_positions, key, head_size, cos_s
                                      cos_sin_cache, is_neox).to(key.dtype)
 
 
+def rotary_embedding_k_fused_layers(old_positions, new_positions, keys, head_size,
+                                    cos_sin_cache, is_neox, slot_mapping=None) -> None:
+    """The same re-rotation of the key views of several layers (same shape,
+    strides and dtype), one launch for all of them on CUDA."""
+    if keys and keys[0].is_cuda:
+        native().rotary_embedding_k_fused_layers(old_positions, new_positions, list(keys),
+                                                 head_size, cos_sin_cache, is_neox,
+                                                 slot_mapping)
+        return
+    for k in keys:
+        rotary_embedding_k_fused(old_positions, new_positions, k, head_size, cos_sin_cache,
+                                 is_neox, slot_mapping)
+
+
 # ----------------------------------------------------------------- misc
 def layerwise_prefill_dma_copy(dsts: torch.Tensor, srcs: torch.Tensor,
                                sizes: torch.Tensor) -> None:

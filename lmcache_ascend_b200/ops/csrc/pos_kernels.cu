@@ -124,14 +124,69 @@ template <typename KT, typename CT, typename PT, bool kNeox>
 __global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
     const PT *__restrict__ old_pos, const PT *__restrict__ new_pos, KT *key,
     const CT *__restrict__ cache, int num_tokens, int num_heads, int head_size, int rot_dim,
-    int64_t key_stride, const PT *rows) {
+    int64_t key_stride, const PT *rows, const int64_t *__restrict__ layer_keys) {
   constexpr int VE = 16 / sizeof(KT);
   constexpr int NP = kNeox ? VE : VE / 2;  // rotation pairs per unit
+  // several layers in one launch: blockIdx.y picks the layer's key view
+  if (layer_keys != nullptr) key = reinterpret_cast<KT *>(layer_keys[blockIdx.y]);
   const int half = rot_dim / 2;
   const int per_head = kNeox ? half / VE : rot_dim / VE;
   const int units = num_heads * per_head;
   const int lane = threadIdx.x & 31;
   const int nw = gridDim.x * (blockDim.x >> 5);
+  if (units <= 16 && (32 % units) == 0) {
+    // few units per token (e.g. MLA's single 64-dim rope head: 4 units):
+    // a warp takes 32 / units tokens at once, one unit per lane
+    const int tpw = 32 / units;
+    const int u = lane % units;
+    const int h = u / per_head;
+    const int g = u - h * per_head;
+    const int i0 = kNeox ? g * VE : g * VE / 2;
+    const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    for (int64_t tb = wid * tpw; tb < num_tokens; tb += static_cast<int64_t>(nw) * tpw) {
+      const int64_t t = tb + lane / units;
+      if (t >= num_tokens) continue;
+      const int64_t row = key_row(rows, t);
+      if (row < 0) continue;
+      const CT *co = cache + static_cast<int64_t>(old_pos[t]) * rot_dim;
+      const CT *cn = cache + static_cast<int64_t>(new_pos[t]) * rot_dim;
+      KT *kh = key + row * key_stride + static_cast<int64_t>(h) * head_size;
+      float ca[NP], sa[NP], cb[NP], sb[NP];
+      load_cs<CT, NP>(cn + i0, ca);
+      load_cs<CT, NP>(cn + half + i0, sa);
+      load_cs<CT, NP>(co + i0, cb);
+      load_cs<CT, NP>(co + half + i0, sb);
+      if (kNeox) {
+        uint4 a = *reinterpret_cast<const uint4 *>(kh + i0);
+        uint4 b = *reinterpret_cast<const uint4 *>(kh + half + i0);
+        KT *x1 = reinterpret_cast<KT *>(&a);
+        KT *x2 = reinterpret_cast<KT *>(&b);
+#pragma unroll
+        for (int j = 0; j < VE; ++j) {
+          float cd, sd, y1, y2;
+          rot_delta(ca[j], sa[j], cb[j], sb[j], cd, sd);
+          rot_apply(to_f(x1[j]), to_f(x2[j]), cd, sd, y1, y2);
+          x1[j] = from_f<KT>(y1);
+          x2[j] = from_f<KT>(y2);
+        }
+        *reinterpret_cast<uint4 *>(kh + i0) = a;
+        *reinterpret_cast<uint4 *>(kh + half + i0) = b;
+      } else {
+        uint4 a = *reinterpret_cast<const uint4 *>(kh + g * VE);
+        KT *x = reinterpret_cast<KT *>(&a);
+#pragma unroll
+        for (int j = 0; j < VE / 2; ++j) {
+          float cd, sd, y1, y2;
+          rot_delta(ca[j], sa[j], cb[j], sb[j], cd, sd);
+          rot_apply(to_f(x[2 * j]), to_f(x[2 * j + 1]), cd, sd, y1, y2);
+          x[2 * j] = from_f<KT>(y1);
+          x[2 * j + 1] = from_f<KT>(y2);
+        }
+        *reinterpret_cast<uint4 *>(kh + g * VE) = a;
+      }
+    }
+    return;
+  }
   for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tokens; t += nw) {
     const int64_t row = key_row(rows, t);
     if (row < 0) continue;
@@ -249,7 +304,8 @@ __global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
 template <typename KT, typename CT, typename PT>
 static void launch_rope_t(const PT *op, const PT *np, at::Tensor &key, const at::Tensor &cache,
                           int T, int H, int D, int rot, int64_t stride, bool neox,
-                          cudaStream_t s, const PT *rows) {
+                          cudaStream_t s, const PT *rows, const int64_t *layer_keys = nullptr,
+                          int num_layers = 1) {
   constexpr int VE = 16 / sizeof(KT);
   const int half = rot / 2;
   const bool vec = (reinterpret_cast<uintptr_t>(key.data_ptr()) % 16 == 0) &&
@@ -264,15 +320,19 @@ static void launch_rope_t(const PT *op, const PT *np, at::Tensor &key, const at:
     int dev = 0, sms = 148;
     C10_CUDA_CHECK(cudaGetDevice(&dev));
     C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int blocks = std::max(1, std::min((T + 7) / 8, sms * 8));
+    const int per_layer = std::max(1, std::min((T + 7) / 8, sms * 8 / std::max(1, num_layers)));
+    const dim3 grid(per_layer, num_layers);
     if (neox)
-      rope_delta_vec_kernel<KT, CT, PT, true><<<blocks, 256, 0, s>>>(op, np, kp, cp, T, H, D,
-                                                                     rot, stride, rows);
+      rope_delta_vec_kernel<KT, CT, PT, true><<<grid, 256, 0, s>>>(op, np, kp, cp, T, H, D,
+                                                                   rot, stride, rows,
+                                                                   layer_keys);
     else
-      rope_delta_vec_kernel<KT, CT, PT, false><<<blocks, 256, 0, s>>>(op, np, kp, cp, T, H, D,
-                                                                      rot, stride, rows);
+      rope_delta_vec_kernel<KT, CT, PT, false><<<grid, 256, 0, s>>>(op, np, kp, cp, T, H, D,
+                                                                    rot, stride, rows,
+                                                                    layer_keys);
     return;
   }
+  TORCH_CHECK(layer_keys == nullptr, "rope: several layers need 16-byte aligned key rows");
   const int threads = std::min(1024, std::max(32, ((H * rot / 2) + 31) / 32 * 32));
   const int blocks = std::min(T, 148 * 16);
   rope_delta_kernel<KT, CT, PT><<<blocks, threads, 0, s>>>(op, np, kp, cp, T, H, D, rot, stride,
@@ -283,24 +343,27 @@ template <typename KT, typename CT>
 static void launch_rope(const at::Tensor &op, const at::Tensor &np, at::Tensor &key,
                         const at::Tensor &cache, int T, int H, int D, int rot,
                         int64_t stride, bool neox, cudaStream_t s,
-                        const c10::optional<at::Tensor> &rows) {
+                        const c10::optional<at::Tensor> &rows,
+                        const int64_t *layer_keys = nullptr, int num_layers = 1) {
   if (op.scalar_type() == at::kLong)
     launch_rope_t<KT, CT, int64_t>(op.data_ptr<int64_t>(), np.data_ptr<int64_t>(), key, cache,
                                    T, H, D, rot, stride, neox, s,
-                                   rows.has_value() ? rows->data_ptr<int64_t>() : nullptr);
+                                   rows.has_value() ? rows->data_ptr<int64_t>() : nullptr,
+                                   layer_keys, num_layers);
   else
     launch_rope_t<KT, CT, int32_t>(op.data_ptr<int32_t>(), np.data_ptr<int32_t>(), key, cache,
                                    T, H, D, rot, stride, neox, s,
-                                   rows.has_value() ? rows->data_ptr<int32_t>() : nullptr);
+                                   rows.has_value() ? rows->data_ptr<int32_t>() : nullptr,
+                                   layer_keys, num_layers);
 }
 
 // `slot_mapping` (optional, the positions' dtype): token t's key row is
 // key[slot_mapping[t]] -- key is then a [cache rows, H*D] view of a paged
 // cache plane -- and tokens with a negative slot are skipped.
-void rotary_embedding_k_fused(const at::Tensor &old_positions,
-                              const at::Tensor &new_positions, at::Tensor &key,
-                              int64_t head_size, const at::Tensor &cos_sin_cache,
-                              bool is_neox, const c10::optional<at::Tensor> &slot_mapping) {
+static void rope_impl(const at::Tensor &old_positions, const at::Tensor &new_positions,
+                      at::Tensor &key, int64_t head_size, const at::Tensor &cos_sin_cache,
+                      bool is_neox, const c10::optional<at::Tensor> &slot_mapping,
+                      const int64_t *layer_keys, int num_layers) {
   TORCH_CHECK(key.is_cuda() && old_positions.is_cuda() && new_positions.is_cuda() &&
                   cos_sin_cache.is_cuda(),
               "rope: all tensors must be on the device");
@@ -342,13 +405,14 @@ void rotary_embedding_k_fused(const at::Tensor &old_positions,
 #define LMC_ROPE_CASE(KTYPE, KCT)                                                  \
   if (ct == at::kFloat)                                                            \
     launch_rope<KTYPE, float>(op, np, key, cos_sin_cache, T, H, D, rot, stride,    \
-                              is_neox, s, slot_mapping);                           \
+                              is_neox, s, slot_mapping, layer_keys, num_layers);   \
   else if (ct == at::kBFloat16)                                                    \
     launch_rope<KTYPE, __nv_bfloat16>(op, np, key, cos_sin_cache, T, H, D, rot,    \
-                                      stride, is_neox, s, slot_mapping);           \
+                                      stride, is_neox, s, slot_mapping,            \
+                                      layer_keys, num_layers);                     \
   else if (ct == at::kHalf)                                                        \
     launch_rope<KTYPE, __half>(op, np, key, cos_sin_cache, T, H, D, rot, stride,   \
-                               is_neox, s, slot_mapping);                          \
+                               is_neox, s, slot_mapping, layer_keys, num_layers);  \
   else                                                                             \
     TORCH_CHECK(false, "rope: unsupported cos_sin_cache dtype");
   if (kt == at::kBFloat16) {
@@ -362,6 +426,51 @@ void rotary_embedding_k_fused(const at::Tensor &old_positions,
   }
 #undef LMC_ROPE_CASE
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rotary_embedding_k_fused(const at::Tensor &old_positions,
+                              const at::Tensor &new_positions, at::Tensor &key,
+                              int64_t head_size, const at::Tensor &cos_sin_cache,
+                              bool is_neox, const c10::optional<at::Tensor> &slot_mapping) {
+  rope_impl(old_positions, new_positions, key, head_size, cos_sin_cache, is_neox, slot_mapping,
+            nullptr, 1);
+}
+
+// The same re-rotation applied to the key views of several layers (same
+// shape, strides and dtype: e.g. the rope columns of every layer of an MLA
+// cache) in one launch; blockIdx.y picks the layer.  Layers whose views are
+// not 16-byte aligned run one launch each.
+void rotary_embedding_k_fused_layers(const at::Tensor &old_positions,
+                                     const at::Tensor &new_positions,
+                                     const std::vector<at::Tensor> &keys, int64_t head_size,
+                                     const at::Tensor &cos_sin_cache, bool is_neox,
+                                     const c10::optional<at::Tensor> &slot_mapping) {
+  TORCH_CHECK(!keys.empty(), "rope: no layers");
+  const at::Tensor &k0 = keys[0];
+  bool aligned = true;
+  for (const auto &k : keys) {
+    TORCH_CHECK(k.device() == k0.device() && k.scalar_type() == k0.scalar_type() &&
+                    k.sizes() == k0.sizes() && k.strides() == k0.strides(),
+                "rope: every layer's key view needs the same shape, strides and dtype");
+    aligned = aligned && reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0;
+  }
+  if (!aligned || keys.size() == 1) {
+    for (const auto &k : keys) {
+      at::Tensor kk = k;
+      rope_impl(old_positions, new_positions, kk, head_size, cos_sin_cache, is_neox,
+                slot_mapping, nullptr, 1);
+    }
+    return;
+  }
+  const c10::cuda::CUDAGuard guard(k0.device());
+  auto host = at::empty({static_cast<int64_t>(keys.size())},
+                        at::TensorOptions().dtype(at::kLong).pinned_memory(true));
+  for (size_t i = 0; i < keys.size(); ++i)
+    host.data_ptr<int64_t>()[i] = reinterpret_cast<int64_t>(keys[i].data_ptr());
+  auto table = host.to(k0.device(), /*non_blocking=*/true);
+  at::Tensor kk = k0;
+  rope_impl(old_positions, new_positions, kk, head_size, cos_sin_cache, is_neox, slot_mapping,
+            table.data_ptr<int64_t>(), static_cast<int>(keys.size()));
 }
 
 }  // namespace lmc

@@ -78,6 +78,11 @@ void rotary_embedding_k_fused(const at::Tensor &old_positions, const at::Tensor 
                               at::Tensor &key, int64_t head_size,
                               const at::Tensor &cos_sin_cache, bool is_neox,
                               const c10::optional<at::Tensor> &slot_mapping);
+void rotary_embedding_k_fused_layers(const at::Tensor &old_positions,
+                                     const at::Tensor &new_positions,
+                                     const std::vector<at::Tensor> &keys, int64_t head_size,
+                                     const at::Tensor &cos_sin_cache, bool is_neox,
+                                     const c10::optional<at::Tensor> &slot_mapping);
 // dma.cu
 void dma_copy_batch(const at::Tensor &dsts, const at::Tensor &srcs, const at::Tensor &sizes);
 double dma_copy_batch_timed(const at::Tensor &dsts, const at::Tensor &srcs,
@@ -193,6 +198,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("row_dst") = py::none());
   m.def("cachegen_dequantize", &cachegen_dequantize, py::arg("sym"), py::arg("scale"),
         py::arg("bins"), py::arg("y"), py::arg("row_src") = py::none());
+  m.def("rotary_embedding_k_fused_layers", &rotary_embedding_k_fused_layers,
+        py::arg("old_positions"), py::arg("new_positions"), py::arg("keys"),
+        py::arg("head_size"), py::arg("cos_sin_cache"), py::arg("is_neox"),
+        py::arg("slot_mapping") = py::none());
   m.def("rotary_embedding_k_fused", &rotary_embedding_k_fused, py::arg("old_positions"),
         py::arg("new_positions"), py::arg("key"), py::arg("head_size"),
         py::arg("cos_sin_cache"), py::arg("is_neox"), py::arg("slot_mapping") = py::none());

@@ -103,3 +103,34 @@ def test_fused_rope_on_paged_mla_rope_part_by_slot(dtype):
     api.rotary_embedding_k_fused(old.cpu(), new.cpu(), cpu[:, 512:], 64, cache.cpu(), True,
                                  slots.cpu())
     assert torch.allclose(got.float().cpu(), cpu.float(), atol=tol * 4, rtol=tol)
+
+
+@pytest.mark.gpu
+def test_fused_rope_several_layers_in_one_launch_matches_per_layer():
+    """The multi-layer form (every layer's rope columns of a paged MLA cache
+    in one launch) leaves the same bits as one call per layer, and matches
+    the fp32 PyTorch oracle."""
+    L, NB, BS, T = 5, 32, 64, 900
+    g = torch.Generator(device="cpu").manual_seed(3)
+    lats = [torch.randn(NB, BS, 576, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
+    twins = [x.clone() for x in lats]
+    before = [x.clone() for x in lats]
+    slots = torch.randperm(NB * BS, generator=g)[:T].int().cuda()
+    slots[::7] = -1
+    cache = R.make_cos_sin_cache(16384, 64, base=10000.0).cuda()
+    old = torch.randint(0, 8192, (T,), generator=g).int().cuda()
+    new = old + torch.randint(0, 8192, (T,), generator=g).int().cuda()
+    keys = [x.view(NB * BS, 576)[:, 512:] for x in lats]
+    ops.native().rotary_embedding_k_fused_layers(old, new, keys, 64, cache, True, slots)
+    for x in twins:
+        ops.native().rotary_embedding_k_fused(old, new, x.view(NB * BS, 576)[:, 512:], 64,
+                                              cache, True, slots)
+    torch.cuda.synchronize()
+    keep = slots >= 0
+    s = slots[keep].long()
+    for x, y, b in zip(lats, twins, before):
+        assert torch.equal(x, y)
+        ref = R.rope_delta_ref(old[keep].long().cpu(), new[keep].long().cpu(),
+                               b.view(NB * BS, 576)[s, 512:].cpu(), 64, cache.cpu(), True)
+        got = x.view(NB * BS, 576)[s, 512:].float().cpu()
+        assert torch.allclose(got, ref, atol=4e-2, rtol=1e-2)
