@@ -121,7 +121,7 @@ __device__ __forceinline__ void load_cs(const CT *p, float (&o)[N]) {
 // adjacent (2p, 2p + 1) pairs.  Same arithmetic as rope_delta_kernel, so both
 // paths give identical results.
 template <typename KT, typename CT, typename PT, bool kNeox>
-__global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
+__global__ void __launch_bounds__(128) rope_delta_vec_kernel(
     const PT *__restrict__ old_pos, const PT *__restrict__ new_pos, KT *key,
     const CT *__restrict__ cache, int num_tokens, int num_heads, int head_size, int rot_dim,
     int64_t key_stride, const PT *rows, const int64_t *__restrict__ layer_keys) {
@@ -187,11 +187,27 @@ __global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
     }
     return;
   }
-  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tokens; t += nw) {
-    const int64_t row = key_row(rows, t);
+  // the warp's next 32 tokens' rows and positions are read one per lane and
+  // handed out by shuffles, so a token's cos/sin loads do not wait on its own
+  // position loads
+  int64_t pf_row = -1, pf_po = 0, pf_pn = 0;
+  int it = 0;
+  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tokens;
+       t += nw, ++it) {
+    if ((it & 31) == 0) {
+      const long long tl = static_cast<long long>(t) + static_cast<long long>(lane) * nw;
+      pf_row = -1;
+      if (tl < num_tokens) {
+        pf_row = key_row(rows, static_cast<int>(tl));
+        pf_po = static_cast<int64_t>(old_pos[tl]);
+        pf_pn = static_cast<int64_t>(new_pos[tl]);
+      }
+    }
+    const int src = it & 31;
+    const int64_t row = __shfl_sync(0xffffffffu, pf_row, src);
     if (row < 0) continue;
-    const int64_t po = static_cast<int64_t>(old_pos[t]);
-    const int64_t pn = static_cast<int64_t>(new_pos[t]);
+    const int64_t po = __shfl_sync(0xffffffffu, pf_po, src);
+    const int64_t pn = __shfl_sync(0xffffffffu, pf_pn, src);
     const CT *co = cache + po * rot_dim;
     const CT *cn = cache + pn * rot_dim;
     KT *kt = key + row * key_stride;
@@ -202,20 +218,12 @@ __global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
       const int g = lane % per_head;
       const int hg = 32 / per_head;
       const int i0 = kNeox ? g * VE : g * VE / 2;
-      float ca[NP], sa[NP], cb[NP], sb[NP], cd[NP], sd[NP];
-      load_cs<CT, NP>(cn + i0, ca);
-      load_cs<CT, NP>(cn + half + i0, sa);
-      load_cs<CT, NP>(co + i0, cb);
-      load_cs<CT, NP>(co + half + i0, sb);
-#pragma unroll
-      for (int j = 0; j < NP; ++j) {
-        rot_delta(ca[j], sa[j], cb[j], sb[j], cd[j], sd[j]);
-      }
       // two heads of the lane's group at a time: their four key loads are in
-      // flight together, and the register count leaves room for 3 CTAs/SM
-      for (int hb = lane / per_head; hb < num_heads; hb += 2 * hg) {
-        uint4 a[2], b[2];
-        KT *kh[2];
+      // flight together (the first pair's before the cos/sin loads), and the
+      // register count leaves room for 3 CTAs/SM
+      uint4 a[2], b[2];
+      KT *kh[2];
+      auto load_pair = [&](int hb) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int h = hb + k * hg;
@@ -228,6 +236,20 @@ __global__ void __launch_bounds__(256, 3) rope_delta_vec_kernel(
             a[k] = *reinterpret_cast<const uint4 *>(kh[k] + g * VE);
           }
         }
+      };
+      const int hb0 = lane / per_head;
+      if (hb0 < num_heads) load_pair(hb0);
+      float ca[NP], sa[NP], cb[NP], sb[NP], cd[NP], sd[NP];
+      load_cs<CT, NP>(cn + i0, ca);
+      load_cs<CT, NP>(cn + half + i0, sa);
+      load_cs<CT, NP>(co + i0, cb);
+      load_cs<CT, NP>(co + half + i0, sb);
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        rot_delta(ca[j], sa[j], cb[j], sb[j], cd[j], sd[j]);
+      }
+      for (int hb = hb0; hb < num_heads; hb += 2 * hg) {
+        if (hb != hb0) load_pair(hb);
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           if (kh[k] == nullptr) continue;
@@ -320,14 +342,16 @@ static void launch_rope_t(const PT *op, const PT *np, at::Tensor &key, const at:
     int dev = 0, sms = 148;
     C10_CUDA_CHECK(cudaGetDevice(&dev));
     C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int per_layer = std::max(1, std::min((T + 7) / 8, sms * 8 / std::max(1, num_layers)));
+    // 4 warps per block; about 16 blocks per SM in all, over the layers
+    const int per_layer =
+        std::max(1, std::min((T + 3) / 4, sms * 16 / std::max(1, num_layers)));
     const dim3 grid(per_layer, num_layers);
     if (neox)
-      rope_delta_vec_kernel<KT, CT, PT, true><<<grid, 256, 0, s>>>(op, np, kp, cp, T, H, D,
+      rope_delta_vec_kernel<KT, CT, PT, true><<<grid, 128, 0, s>>>(op, np, kp, cp, T, H, D,
                                                                    rot, stride, rows,
                                                                    layer_keys);
     else
-      rope_delta_vec_kernel<KT, CT, PT, false><<<grid, 256, 0, s>>>(op, np, kp, cp, T, H, D,
+      rope_delta_vec_kernel<KT, CT, PT, false><<<grid, 128, 0, s>>>(op, np, kp, cp, T, H, D,
                                                                     rot, stride, rows,
                                                                     layer_keys);
     return;
