@@ -221,3 +221,67 @@ def test_two_group_model_latent_and_indexer():
     assert sched.get_num_new_matched_tokens(req_c, 0) == (0, False)
     worker.shutdown()
     worker.engine.close()
+
+
+def test_blending_on_load_through_the_served_model():
+    """enable_blending: the worker's load of a hit runs CacheBlend on the
+    model the serving process registered (here a vLLM-shaped wrapper around
+    this repo's reference model); with every token recomputed the request's
+    blocks end up with exactly the KV a prefill of the prompt writes, although
+    the cached KV it started from was different."""
+    from lmcache_ascend_b200.models.llama import LlamaConfig, LlamaForBlend
+    from lmcache_ascend_b200.v1.blend.vllm_model import VLLMModelTracker, drop_blender
+
+    from .test_blend_vllm_model import _served
+
+    cfg = LMCacheEngineConfig.from_defaults(
+        chunk_size=256, max_local_cpu_size=0.05, enable_blending=True, use_layerwise=True,
+        blend_recompute_ratios=[1.0], blend_check_layers=[0],
+        lmcache_instance_id="adapter-blend-test")
+    mc = LlamaConfig.tiny(vocab_size=2000, hidden_size=128, num_layers=L, num_heads=4,
+                          num_kv_heads=H, head_dim=D, intermediate_size=256, max_position=4096)
+    ref = LlamaForBlend(mc, device="cpu")
+    VLLMModelTracker.unregister(cfg.lmcache_instance_id)
+    drop_blender(cfg.lmcache_instance_id)
+    VLLMModelTracker.register_model(cfg.lmcache_instance_id, _served(ref, mc, False))
+    sched, worker, kv = _pair(cfg)
+    try:
+        prompt = list(range(1000, 1300))  # 300 tokens
+        blocks_a = list(range(0, 19))
+        req_a = SimpleNamespace(request_id="A", prompt_token_ids=prompt)
+        sched.get_num_new_matched_tokens(req_a, 0)
+        sched.update_state_after_alloc(req_a, None, 0)
+        new_a = SimpleNamespace(req_id="A", prompt_token_ids=prompt, block_ids=(blocks_a,),
+                                num_computed_tokens=0)
+        meta = sched.build_connector_meta(_sched_out([new_a], scheduled={"A": 300}))
+        sa = _slots(blocks_a, 300)
+        # the cached KV of A is NOT what the model computes for this prompt, so
+        # only a recompute (the blend) can produce the model's KV for B
+        _fill(kv, sa, seed=1)
+        _step(worker, meta)
+
+        req_b = SimpleNamespace(request_id="B", prompt_token_ids=prompt)
+        need, _ = sched.get_num_new_matched_tokens(req_b, 0)
+        assert need > 0
+        sched.update_state_after_alloc(req_b, None, need)
+        blocks_b = list(range(40, 59))
+        new_b = SimpleNamespace(req_id="B", prompt_token_ids=prompt, block_ids=(blocks_b,),
+                                num_computed_tokens=0)
+        meta = sched.build_connector_meta(_sched_out([new_b], scheduled={"B": 1}))
+        _step(worker, meta)
+        n = meta.requests[0].load_spec.lmcache_cached_tokens
+        sb = _slots(blocks_b, 300)[:n]
+        got = _read(kv, sb)
+        fresh = {k: torch.zeros_like(t) for k, t in kv.items()}
+        ref.prefill(torch.tensor(prompt[:n]), [(t[0], t[1]) for t in fresh.values()], sb)
+        for a, b in zip(got, _read(fresh, sb)):
+            assert torch.allclose(a, b, atol=1e-4, rtol=1e-4)
+        from lmcache_ascend_b200.v1.blend.vllm_model import _blenders
+
+        assert cfg.lmcache_instance_id in _blenders
+        sched.request_finished(req_b, blocks_b)
+    finally:
+        worker.shutdown()
+        worker.engine.close()
+        drop_blender(cfg.lmcache_instance_id)
+        VLLMModelTracker.unregister(cfg.lmcache_instance_id)
