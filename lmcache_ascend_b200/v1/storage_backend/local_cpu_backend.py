@@ -111,15 +111,14 @@ class LocalCPUBackend(StorageBackendInterface):
     def batched_get_blocking(self, keys: Sequence[CacheEngineKey]) -> List[Optional[MemoryObj]]:
         """One lock acquisition for the whole batch (a layerwise 16k-token
         request asks for thousands of per-layer chunks)."""
-        out: List[Optional[MemoryObj]] = []
         with self._lock:
             hc = self.hot_cache
-            for key in keys:
-                obj = hc.get(key)
+            get, touch = hc.get, hc.move_to_end
+            out: List[Optional[MemoryObj]] = [get(k) for k in keys]
+            for key, obj in zip(keys, out):
                 if obj is not None:
-                    hc.move_to_end(key)
+                    touch(key)
                     obj.ref_count_up()
-                out.append(obj)
         return out
 
     def pin(self, key: CacheEngineKey) -> bool:

@@ -136,12 +136,15 @@ class StorageManager:
                 continue
             got = b.batched_get_blocking([keys[i] for i in todo])
             rest = []
+            # hits of the CPU and HBM tiers are already where they belong
+            promote = name not in ("LocalCPUBackend", "LocalGPUBackend")
             for i, obj in zip(todo, got):
                 if obj is None:
                     rest.append(i)
                 else:
                     out[i] = obj
-                    self._promote(name, keys[i], obj)
+                    if promote:
+                        self._promote(name, keys[i], obj)
             todo = rest
         return out
 
