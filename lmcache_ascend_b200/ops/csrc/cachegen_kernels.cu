@@ -730,6 +730,30 @@ __global__ void __launch_bounds__(kDecWideThreads) cg_decode_wide_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// CDF rows from the stored code lengths (the serialised form keeps 4-bit
+// lengths, two per byte, first in the high nibble): a thread per (row,
+// channel) walks its bins, start_s = sum over r < s of 2^(16 - len_r), entry
+// = (start & 0xFFF0) | len, and a closing 0 entry.  One launch in place of the
+// unpack / power / scan / pack sequence of tensor ops.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) cg_cdf_from_lengths_kernel(
+    const uint8_t *__restrict__ packed, int16_t *out, long long streams, int bins) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= streams) return;
+  unsigned short *o = reinterpret_cast<unsigned short *>(out) + i * (bins + 1);
+  unsigned pos = 0;
+  const long long e0 = i * bins;
+  for (int s = 0; s < bins; ++s) {
+    const long long e = e0 + s;
+    const unsigned b = __ldg(packed + (e >> 1));
+    const unsigned ln = (e & 1) ? (b & 0xFu) : (b >> 4);
+    o[s] = static_cast<unsigned short>((pos & 0xFFF0u) | ln);
+    pos += 1u << (16 - ln);
+  }
+  o[bins] = 0;
+}
+
+// ---------------------------------------------------------------------------
 // quantise: x [R, T, C] (rows = K layers then V layers of a KV_2LTD chunk) ->
 // symbols [R, T, C] uint8 and scale [R, T] fp32, warp per (row, token):
 //   half = bins / 2 - 1, scale = max(amax |x|, 1e-8) / half,
@@ -985,6 +1009,23 @@ void encode_fast_new(const at::Tensor &cdf, const at::Tensor &input_sym,
   else
     launch(std::integral_constant<int, 128>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+at::Tensor cachegen_cdf_from_lengths(const at::Tensor &packed, int64_t rows, int64_t channels,
+                                     int64_t bins) {
+  TORCH_CHECK(packed.is_cuda() && packed.scalar_type() == at::kByte && packed.is_contiguous(),
+              "cdf_from_lengths: packed lengths must be a contiguous device uint8 tensor");
+  TORCH_CHECK(bins >= 1 && bins <= kCgMaxBins, "cdf_from_lengths: 1 <= bins <= 256");
+  const long long streams = rows * channels;
+  TORCH_CHECK(packed.numel() * 2 >= streams * bins, "cdf_from_lengths: too few lengths");
+  const c10::cuda::CUDAGuard guard(packed.device());
+  auto out = at::empty({rows, channels, bins + 1}, packed.options().dtype(at::kShort));
+  if (streams == 0) return out;
+  cg_cdf_from_lengths_kernel<<<static_cast<unsigned>((streams + 127) / 128), 128, 0,
+                               at::cuda::getCurrentCUDAStream().stream()>>>(
+      packed.data_ptr<uint8_t>(), out.data_ptr<int16_t>(), streams, static_cast<int>(bins));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
 }
 
 void decode_fast_prefsum(const at::Tensor &cdf, const at::Tensor &bytestreams,

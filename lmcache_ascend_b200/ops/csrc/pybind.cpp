@@ -57,6 +57,8 @@ void pd_flag_add(int64_t flag_ptr, int64_t inc);
 void pd_wait_flags(int64_t flags_ptr, const at::Tensor &targets, int64_t layer_begin,
                    double timeout_s, const c10::optional<at::Tensor> &status);
 // cachegen_kernels.cu
+at::Tensor cachegen_cdf_from_lengths(const at::Tensor &packed, int64_t rows, int64_t channels,
+                                     int64_t bins);
 void c8_copy(const at::Tensor &planes, const at::Tensor &slots, const at::Tensor &packets,
              int64_t cap, int64_t num_layers, int64_t key_bytes, int64_t factor,
              const c10::optional<at::Tensor> &block_map, int64_t cache_slots,
@@ -192,6 +194,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("output_buffer"), py::arg("output_lengths"),
         py::arg("status") = py::none());
   m.def("decode_fast_prefsum", &decode_fast_prefsum);
+  m.def("cachegen_cdf_from_lengths", &cachegen_cdf_from_lengths);
   m.def("c8_copy", &c8_copy);
   m.def("cachegen_compact", &cachegen_compact);
   m.def("cachegen_quantize", &cachegen_quantize, py::arg("x"), py::arg("bins"), py::arg("sym"),

@@ -22,7 +22,7 @@ from typing import List, Optional, Tuple
 import numpy as np
 import torch
 
-from ...ops import api
+from ...ops import api, native
 
 MAGIC = b"LMCG"
 VERSION = 1
@@ -341,17 +341,18 @@ def decode_kv_bytes(data: bytes, device="cpu", out: Optional[torch.Tensor] = Non
         ncl = nrows * C * bins
         packed = payload[off:off + (ncl + 1) // 2]
         off += (ncl + 1) // 2
-        cl = torch.stack([packed >> 4, packed & 15], dim=1).flatten()[:ncl].view(nrows, C, bins)
+        cdf = native().cachegen_cdf_from_lengths(packed, nrows, C, bins)  # one launch
         stream = payload[off:off + slen] if slen else torch.zeros(1, dtype=torch.uint8,
                                                                   device=dev)
         off += slen
         cum = torch.cumsum(lens, 0).to(torch.int32).view(nrows, C)
-        api.decode_fast_prefsum(cdf_from_lengths(cl), stream, cum, sym[row0:row0 + nrows])
+        api.decode_fast_prefsum(cdf, stream, cum, sym[row0:row0 + nrows])
         for i, r in enumerate(rows):
             pos[r] = row0 + i
         row0 += nrows
-    row_bins = torch.cat([kb, vb]).to(torch.int32)
-    src = torch.tensor(pos, dtype=torch.int32, device=dev)
+    # small host tables go over from pinned memory without a synchronisation
+    row_bins = torch.cat([kb, vb]).to(torch.int32).pin_memory().to(dev, non_blocking=True)
+    src = torch.tensor(pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
     direct = out is not None and out.is_contiguous() and out.dtype == dtype and \
         out.device == dev
     y = api.cachegen_dequantize(sym, scales, row_bins, dtype, row_src=src,

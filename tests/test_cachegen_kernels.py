@@ -225,3 +225,19 @@ def test_gpu_cachegen_kv_round_trip_matches_cpu():
     y = decode_kv(e_gpu, device="cuda", out=out)
     assert y.data_ptr() == out.data_ptr()
     assert torch.equal(y.cpu(), decode_kv(e_cpu))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bins", [1, 16, 33, 256])
+def test_cdf_from_packed_lengths_kernel_matches_tensor_ops(bins):
+    """The fused rebuild of CDF rows from the serialised 4-bit code lengths
+    gives the same int16 rows as the tensor-op form (``cdf_from_lengths``)."""
+    from lmcache_ascend_b200.ops import native
+    from lmcache_ascend_b200.v1.cachegen import _pack_nibbles_dev, cdf_from_lengths
+
+    g = torch.Generator().manual_seed(bins)
+    rows, C = 3, 37
+    lengths = torch.randint(0, 13, (rows, C, bins), generator=g).to(torch.uint8).cuda()
+    packed = _pack_nibbles_dev(lengths)
+    got = native().cachegen_cdf_from_lengths(packed, rows, C, bins)
+    assert torch.equal(got.cpu(), cdf_from_lengths(lengths).cpu())
