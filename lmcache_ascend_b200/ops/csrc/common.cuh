@@ -92,6 +92,18 @@ __device__ __forceinline__ void red_release_sys_add(unsigned *p, unsigned v) {
                : "memory");
 }
 
+// GPU-scope forms, for a flag whose waiter runs on this same GPU (its
+// acquire, system-scoped, synchronises with a release of GPU scope: both
+// threads are inside that scope).
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v)
+               : "memory");
+}
+
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v)
                : "memory");

@@ -223,7 +223,23 @@ struct BulkPushJob {
   uint32_t bulk_planes;            // bit p: plane p moves by TMA bulk copies, else by
                                    // per-lane loads/stores (rows not 16-byte aligned)
   unsigned *counters;              // [units of this launch], zero between launches
+  bool gpu_scope;                  // every destination (and its waiter) on this GPU
 };
+
+// Publish a finished unit: order this thread's earlier writes (and, through
+// the counters' acq_rel, the other warps' writes of the unit) before the
+// flag increments.  System scope when a destination is a peer GPU.
+__device__ __forceinline__ void bulk_publish(const BulkPushJob &j, int layer) {
+  if (j.gpu_scope) {
+    fence_acq_rel_gpu();
+    for (int r = 0; r < j.replicas; ++r)
+      if (j.flags[r]) red_release_gpu_add(j.flags[r] + layer, 1u);
+  } else {
+    fence_acq_rel_sys();
+    for (int r = 0; r < j.replicas; ++r)
+      if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
+  }
+}
 
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -389,10 +405,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 6)
                                                    static_cast<unsigned>(qc[0]));
       if (before + static_cast<unsigned>(qc[0]) == static_cast<unsigned>(ppu_front)) {
         j.counters[qu[0]] = 0u;  // ready for the next launch
-        fence_acq_rel_sys();
-        const int layer = c.layer_begin + ql[0];
-        for (int r = 0; r < j.replicas; ++r)
-          if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
+        bulk_publish(j, c.layer_begin + ql[0]);
       }
     }
 #pragma unroll
@@ -514,11 +527,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 6)
       }
     }
     __syncwarp();
-    if (lane == 0) {
-      fence_acq_rel_sys();
-      for (int r = 0; r < j.replicas; ++r)
-        if (j.flags[r]) red_release_sys_add(j.flags[r] + layer, 1u);
-    }
+    if (lane == 0) bulk_publish(j, layer);
   }
 }
 
@@ -811,7 +820,7 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
              int64_t layer_begin, int64_t num_layers, int64_t replicas,
              const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
              int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode,
-             const c10::optional<at::Tensor> &counters) {
+             const c10::optional<at::Tensor> &counters, bool local_dst) {
   TORCH_CHECK(src_slots.is_cuda() && dst_slots.is_cuda(),
               "slot mappings must live on the device");
   TORCH_CHECK(src_slots.scalar_type() == dst_slots.scalar_type(),
@@ -924,6 +933,7 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst,
       cnt = at::zeros({std::max<long long>(1, units)}, src_slots.options().dtype(at::kInt));
     }
     b.counters = reinterpret_cast<unsigned *>(cnt.data_ptr());
+    b.gpu_scope = local_dst;
     const size_t smem = kTmaRingOffset +
                         static_cast<size_t>(kBulkWarps) * kBulkStages * kBulkStageBytes;
     static bool attr_set[64] = {false};

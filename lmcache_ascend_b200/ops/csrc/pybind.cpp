@@ -37,7 +37,7 @@ void pd_push(const PagedLayout &src, const PagedLayout &dst, const at::Tensor &s
              const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
              int64_t replicas, const std::vector<int64_t> &flag_ptrs, int64_t tile_tokens,
              int64_t grid, const c10::optional<at::Tensor> &status, int64_t mode,
-             const c10::optional<at::Tensor> &counters);
+             const c10::optional<at::Tensor> &counters, bool local_dst);
 int64_t fp8_staging_bytes(const PagedLayout &layout, int64_t num_tokens, int64_t num_layers,
                           int64_t group, bool scales);
 void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
@@ -170,7 +170,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("replicas") = 1, py::arg("flag_ptrs") = std::vector<int64_t>{},
         py::arg("tile_tokens") = 128, py::arg("grid") = 0,
         py::arg("status") = py::none(), py::arg("mode") = 0,
-        py::arg("counters") = py::none());
+        py::arg("counters") = py::none(), py::arg("local_dst") = false);
   m.def("fp8_staging_bytes", &fp8_staging_bytes);
   m.def("pd_push_multimem", &pd_push_multimem, py::arg("src"), py::arg("mc_rows"),
         py::arg("mc_flags"), py::arg("src_slots"), py::arg("layer_begin"),

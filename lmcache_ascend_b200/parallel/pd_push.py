@@ -258,8 +258,11 @@ class PushSender:
             here = mod.get_gpu_pci_bus_id(self.device.index or 0)
         except Exception:  # pragma: no cover - no bus id: treat as local
             here = ""
-        self._remote = bool(here) and any(
-            IpcDesc.from_dict(r.flags).pci_bus_id not in ("", here) for r in receivers)
+        buses = [IpcDesc.from_dict(r.flags).pci_bus_id for r in receivers]
+        self._remote = bool(here) and any(b not in ("", here) for b in buses)
+        # flags released at GPU scope only when every receiver is known to be
+        # on this GPU (an unknown bus id keeps system scope)
+        self._all_local = bool(here) and all(b == here for b in buses)
         self._fp8 = None
         self._fp8_seq, self._fp8_buf = 0, 0
         if r0.fp8_q is not None and len(receivers) == 1:
@@ -312,7 +315,8 @@ class PushSender:
                                          device=self.device)
         ops.native().pd_push(self.layout.native(), self._dst, src_slots, dst_slots,
                              layer_begin, nl, self.replicas, self._flag_ptrs, tile_tokens,
-                             grid, self.status.tensor, self._mode(), self._counters)
+                             grid, self.status.tensor, self._mode(), self._counters,
+                             getattr(self, "_all_local", False))
         self._mark_pushed()
 
     def _mode(self) -> int:
