@@ -15,7 +15,9 @@ Ops here:
   load_and_reshape_flash, reshape_and_cache_back_flash,
   IndexerC8State / IndexerC8GroupState / indexer_c8_transfer_prepared,
   calculate_cdf, encode_fast_new, decode_fast_prefsum,
-  rotary_embedding_k_fused, layerwise_prefill_dma_copy, get_gpu_pci_bus_id.
+  rotary_embedding_k_fused, rotary_embedding_k_fused_layers (every layer in one
+  launch), layerwise_prefill_dma_copy, get_gpu_pci_bus_id.
+The reference's raw-pointer call signatures are in ``lmcache_ascend_b200.c_ops``.
 """
 
 from __future__ import annotations
