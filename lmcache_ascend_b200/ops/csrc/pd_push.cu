@@ -555,6 +555,7 @@ struct PushQJob {
   float *scales;          // peer staging, fp32
   unsigned *flags;
   DeviceStatus *status;
+  int32_t gpu_scope;      // the staging (and its waiter) is on this GPU
 };
 
 __device__ __forceinline__ float bf16x2_lo(uint32_t w) {
@@ -680,8 +681,13 @@ __global__ void __launch_bounds__(kPushWarps * 32) pd_push_fp8_kernel(PushQJob j
     }
     __syncthreads();
     if (tid == 0 && j.flags) {
-      fence_acq_rel_sys();
-      red_release_sys_add(j.flags + layer, 1u);
+      if (j.gpu_scope) {
+        fence_acq_rel_gpu();
+        red_release_gpu_add(j.flags + layer, 1u);
+      } else {
+        fence_acq_rel_sys();
+        red_release_sys_add(j.flags + layer, 1u);
+      }
     }
   }
 }
@@ -995,7 +1001,7 @@ int64_t fp8_staging_bytes(const PagedLayout &layout, int64_t num_tokens, int64_t
 void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
                  const at::Tensor &src_slots, int64_t layer_begin, int64_t num_layers,
                  int64_t flag_ptr, int64_t tile_tokens, int64_t grid, int64_t group,
-                 const c10::optional<at::Tensor> &status) {
+                 const c10::optional<at::Tensor> &status, bool local_dst) {
   TORCH_CHECK(src_slots.is_cuda() && src_slots.is_contiguous() &&
                   (src_slots.scalar_type() == at::kInt || src_slots.scalar_type() == at::kLong),
               "src_slots: contiguous device int32/int64");
@@ -1034,6 +1040,7 @@ void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
   j.q = reinterpret_cast<uint8_t *>(q_ptr);
   j.scales = reinterpret_cast<float *>(scale_ptr);
   j.flags = reinterpret_cast<unsigned *>(flag_ptr);
+  j.gpu_scope = local_dst ? 1 : 0;
   if (status.has_value()) j.status = reinterpret_cast<DeviceStatus *>(status->data_ptr());
   const int dev = src_slots.device().index();
   const long long units =

@@ -43,7 +43,7 @@ int64_t fp8_staging_bytes(const PagedLayout &layout, int64_t num_tokens, int64_t
 void pd_push_fp8(const PagedLayout &src, int64_t q_ptr, int64_t scale_ptr,
                  const at::Tensor &src_slots, int64_t layer_begin, int64_t num_layers,
                  int64_t flag_ptr, int64_t tile_tokens, int64_t grid, int64_t group,
-                 const c10::optional<at::Tensor> &status);
+                 const c10::optional<at::Tensor> &status, bool local_dst);
 void pd_dequant_scatter(const PagedLayout &dst, int64_t q_ptr, int64_t scale_ptr,
                         const at::Tensor &dst_slots, int64_t layer_begin, int64_t num_layers,
                         int64_t group, const c10::optional<at::Tensor> &status);
@@ -179,7 +179,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pd_push_fp8", &pd_push_fp8, py::arg("src"), py::arg("q_ptr"), py::arg("scale_ptr"),
         py::arg("src_slots"), py::arg("layer_begin"), py::arg("num_layers"),
         py::arg("flag_ptr"), py::arg("tile_tokens") = 128, py::arg("grid") = 0,
-        py::arg("group") = 128, py::arg("status") = py::none());
+        py::arg("group") = 128, py::arg("status") = py::none(),
+        py::arg("local_dst") = false);
   m.def("pd_dequant_scatter", &pd_dequant_scatter, py::arg("dst"), py::arg("q_ptr"),
         py::arg("scale_ptr"), py::arg("dst_slots"), py::arg("layer_begin"),
         py::arg("num_layers"), py::arg("group") = 128, py::arg("status") = py::none());

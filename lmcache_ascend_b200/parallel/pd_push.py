@@ -301,7 +301,8 @@ class PushSender:
             b = self._fp8_buf
             ops.native().pd_push_fp8(self.layout.native(), q_ptr + b * qst, s_ptr + b * sst,
                                      src_slots, layer_begin, nl, self._flag_ptrs[0],
-                                     tile_tokens, grid, group, self.status.tensor)
+                                     tile_tokens, grid, group, self.status.tensor,
+                                     getattr(self, "_all_local", False))
             self._mark_pushed()
             return
         if quant != "none":
